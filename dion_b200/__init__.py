@@ -1,0 +1,8 @@
+"""dion_b200: Blackwell-native (sm_100a) distributed orthonormalizing optimizers.
+
+Muon, Dion, Dion2, AdaDion and AdaDionV2 (plus the research variants SDion,
+GSDion, AGDion and QCDion) with torch.optim-style constructors, backed by
+hand-written tcgen05/TMA kernels and NVLink collectives.
+"""
+
+__version__ = "0.1.0"

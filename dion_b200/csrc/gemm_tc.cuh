@@ -1,0 +1,359 @@
+// Persistent, warp-specialised bf16 GEMM on the sm_100a tensor cores.
+//
+//   D[b] = epilogue( alpha_b * A[b] @ B[b] , C[b] )
+//
+// A[b] is M x K and B[b] is K x N; each operand may be stored K-major or
+// MN-major (the layout is chosen through the TMA tensor map and the UMMA
+// shared-memory descriptor, never by a transpose copy).
+//
+// Roles (192 threads, one CTA per SM):
+//   warp 0      : TMA producer (one elected lane), STAGES-deep smem ring
+//   warp 1      : TMEM allocator + tcgen05.mma issuer (one elected lane)
+//   warps 2..5  : epilogue, one TMEM lane quarter each (tcgen05.ld -> regs ->
+//                 fused math -> st.global)
+// The accumulator is double buffered in TMEM (2 x BN fp32 columns) so the
+// epilogue of tile i overlaps the main loop of tile i+1.
+//
+// Epilogue modes:
+//   store   : D = alpha_b*acc + beta_b*C
+//   sym     : same, but only tiles touching the upper triangle are computed;
+//             each element (i,j), j>i, is also written to (j,i). Used for the
+//             symmetric products X X^T and A A of Newton-Schulz.
+//   PARAM   : D = gamma*D + delta*(alpha_b*acc + beta_b*C)  (in-place weight
+//             update fused into the last Newton-Schulz GEMM)
+//
+// alpha_b = alpha * scale[b]^alpha_pow, beta_b = beta * scale[b]^beta_pow when
+// a per-batch scale vector is given (used to fold the Frobenius
+// normalisation of Newton-Schulz into the first iteration).
+#pragma once
+#include "common.cuh"
+#include "ptx.cuh"
+
+namespace bdion {
+
+struct GemmArgs {
+  int M, N, K, batch;
+  void* D;
+  int64_t ldd, strideD;
+  const void* C;  // may be null
+  int64_t ldc, strideC;
+  float alpha, beta;
+  const float* scale;  // per-batch scale (may be null)
+  int alpha_pow, beta_pow;
+  float gamma, delta;  // PARAM mode
+  int sym;
+  int tiles_m, tiles_n;
+  int tiles_per_batch;
+  int total_tiles;
+  int* status;
+  uint64_t limit_ns;
+};
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;  // 64 bf16 = 128 bytes = one swizzle row
+constexpr int kGroupM = 8;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int kStages = BN >= 256 ? 4 : 6;
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTmemCols = 2 * BN;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+__device__ __forceinline__ int sym_row_start(int tm, int BN) { return (tm * kBM) / BN; }
+
+// Map a linear tile id inside one batch to (tm, tn).
+template <int BN>
+__device__ __forceinline__ void decode_tile(const GemmArgs& a, int local, int& tm, int& tn) {
+  if (a.sym) {
+    int r = 0;
+    while (true) {
+      int cnt = a.tiles_n - sym_row_start(r, BN);
+      if (local < cnt || r == a.tiles_m - 1) {
+        tm = r;
+        tn = sym_row_start(r, BN) + local;
+        return;
+      }
+      local -= cnt;
+      ++r;
+    }
+  }
+  const int per_group = kGroupM * a.tiles_n;
+  const int g = local / per_group;
+  const int first_m = g * kGroupM;
+  const int gsize = min(a.tiles_m - first_m, kGroupM);
+  const int in_g = local - g * per_group;
+  tm = first_m + in_g % gsize;
+  tn = in_g / gsize;
+}
+
+template <int BN, bool A_MN, bool B_MN, typename OutT, typename CT, bool PARAM>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const GemmArgs args) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + S * Cfg::kABytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint64_t* full_bar = bars;
+  uint64_t* empty_bar = bars + S;
+  uint64_t* tfull_bar = bars + 2 * S;
+  uint64_t* tempty_bar = bars + 2 * S + 2;
+  uint64_t* drain_bar = bars + 2 * S + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(bars + 2 * S + 6);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull_bar[i], 1);
+      mbar_init(&tempty_bar[i], 4);
+    }
+    mbar_init(drain_bar, 1);
+    *s_abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_kb = (args.K + kBK - 1) / kBK;
+  const uint64_t limit = args.limit_ns;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      long issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < args.total_tiles && ok; t += gridDim.x) {
+        const int b = t / args.tiles_per_batch;
+        int tm, tn;
+        decode_tile<BN>(args, t - b * args.tiles_per_batch, tm, tn);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1, s_abort, limit)) {
+            report_status(args.status, kStatusGemmProducerTimeout);
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full_bar[stage], Cfg::kStageBytes);
+          uint8_t* a_dst = sA + stage * Cfg::kABytes;
+          uint8_t* b_dst = sB + stage * Cfg::kBBytes;
+          if (!A_MN) {
+            tma_load_3d(&tmA, &full_bar[stage], a_dst, kb * kBK, tm * kBM, b);
+          } else {
+#pragma unroll
+            for (int h = 0; h < kBM / 64; ++h)
+              tma_load_3d(&tmA, &full_bar[stage], a_dst + h * 8192, tm * kBM + h * 64, kb * kBK, b);
+          }
+          if (!B_MN) {
+            tma_load_3d(&tmB, &full_bar[stage], b_dst, kb * kBK, tn * BN, b);
+          } else {
+#pragma unroll
+            for (int h = 0; h < BN / 64; ++h)
+              tma_load_3d(&tmB, &full_bar[stage], b_dst + h * 8192, tn * BN + h * 64, kb * kBK, b);
+          }
+          ++issued;
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // Drain: wait (bounded) for the loads of the last S issued stages.
+        int st = stage;
+        uint32_t ph = phase;
+        for (long i = 0; i < min(issued, (long)S); ++i) {
+          if (--st < 0) {
+            st = S - 1;
+            ph ^= 1;
+          }
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(&full_bar[st], ph) && globaltimer_ns() - t0 < 100000000ull) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc(kBM, BN, A_MN, B_MN, 1u);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local_tile = 0;
+      bool ok = true;
+      bool issued_any = false;
+      for (int t = blockIdx.x; t < args.total_tiles && ok; t += gridDim.x, ++local_tile) {
+        const int acc = local_tile & 1;
+        const uint32_t acc_phase = (local_tile >> 1) & 1;
+        if (!mbar_wait_bounded(&tempty_bar[acc], acc_phase ^ 1, s_abort, limit)) {
+          report_status(args.status, kStatusGemmMmaTimeout);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_bounded(&full_bar[stage], phase, s_abort, limit)) {
+            report_status(args.status, kStatusGemmMmaTimeout);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + stage * Cfg::kABytes);
+          const uint32_t b_base = smem_u32(sB + stage * Cfg::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t adesc = A_MN ? make_sdesc_sw128(a_base + k * 2048, 8192, 1024)
+                                        : make_sdesc_sw128(a_base + k * 32, 16, 1024);
+            const uint64_t bdesc = B_MN ? make_sdesc_sw128(b_base + k * 2048, 8192, 1024)
+                                        : make_sdesc_sw128(b_base + k * 32, 16, 1024);
+            umma_f16(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          issued_any = true;
+          umma_commit(&empty_bar[stage]);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull_bar[acc]);
+      }
+      if (!ok && issued_any) {
+        // Wait (bounded) for the MMAs already issued before TMEM is freed.
+        umma_commit(drain_bar);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(drain_bar, 0) && globaltimer_ns() - t0 < 100000000ull) {
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int local_tile = 0;
+    for (int t = blockIdx.x; t < args.total_tiles; t += gridDim.x, ++local_tile) {
+      const int b = t / args.tiles_per_batch;
+      int tm, tn;
+      decode_tile<BN>(args, t - b * args.tiles_per_batch, tm, tn);
+      const int acc = local_tile & 1;
+      const uint32_t acc_phase = (local_tile >> 1) & 1;
+      if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, s_abort, limit)) {
+        report_status(args.status, kStatusGemmEpilogueTimeout);
+        break;
+      }
+      tc_fence_after();
+
+      float alpha = args.alpha, beta = args.beta;
+      if (args.scale != nullptr) {
+        const float s = args.scale[b];
+        for (int i = 0; i < args.alpha_pow; ++i) alpha *= s;
+        for (int i = 0; i < args.beta_pow; ++i) beta *= s;
+      }
+      const int row = tm * kBM + q * 32 + lane;
+      const bool row_ok = row < args.M;
+      OutT* Db = reinterpret_cast<OutT*>(args.D) + (int64_t)b * args.strideD;
+      const CT* Cb = args.C ? reinterpret_cast<const CT*>(args.C) + (int64_t)b * args.strideC : nullptr;
+
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + c * 32, r);
+        tmem_wait_ld();
+        const int col0 = tn * BN + c * 32;
+        if (!row_ok || col0 >= args.N) continue;
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = alpha * __uint_as_float(r[i]);
+        const bool full = col0 + 32 <= args.N;
+        if (Cb != nullptr && beta != 0.f) {
+          const CT* crow = Cb + (int64_t)row * args.ldc + col0;
+          if (full) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              float cv[8];
+              load8(crow + i, cv);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) v[i + j] += beta * cv[j];
+            }
+          } else {
+            for (int i = 0; i < 32; ++i)
+              if (col0 + i < args.N) v[i] += beta * to_f<CT>(crow[i]);
+          }
+        }
+        OutT* drow = Db + (int64_t)row * args.ldd + col0;
+        if (PARAM) {
+          if (full) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              float pv[8];
+              load8(drow + i, pv);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) pv[j] = args.gamma * pv[j] + args.delta * v[i + j];
+              store8(drow + i, pv);
+            }
+          } else {
+            for (int i = 0; i < 32; ++i)
+              if (col0 + i < args.N) drow[i] = from_f<OutT>(args.gamma * to_f<OutT>(drow[i]) + args.delta * v[i]);
+          }
+        } else if (!args.sym) {
+          if (full) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) store8(drow + i, v + i);
+          } else {
+            for (int i = 0; i < 32; ++i)
+              if (col0 + i < args.N) drow[i] = from_f<OutT>(v[i]);
+          }
+        } else {
+          // symmetric: write (row, j) for j >= row and mirror (j, row) for j > row
+          if (col0 > row && full) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) store8(drow + i, v + i);
+#pragma unroll 4
+            for (int i = 0; i < 32; ++i) Db[(int64_t)(col0 + i) * args.ldd + row] = from_f<OutT>(v[i]);
+          } else if (col0 + 31 >= row) {
+            for (int i = 0; i < 32; ++i) {
+              const int j = col0 + i;
+              if (j >= args.N || j < row) continue;
+              drow[i] = from_f<OutT>(v[i]);
+              if (j > row) Db[(int64_t)j * args.ldd + row] = from_f<OutT>(v[i]);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, Cfg::kTmemCols);
+}
+
+}  // namespace bdion

@@ -1,0 +1,285 @@
+"""Device ops of dion_b200.
+
+CUDA tensors run the hand-written sm_100a kernels of the ``dion_b200._C``
+extension; CPU tensors run the plain PyTorch definition of the same op (the
+oracle used by the tests). A CUDA tensor never falls back silently: if the
+extension is missing the op raises.
+"""
+from __future__ import annotations
+
+import math
+from typing import List, Optional, Sequence, Tuple
+
+import torch
+from torch import Tensor
+
+from ._ext import ext, has_ext, check_status, clear_status, StatusError  # noqa: F401
+
+__all__ = [
+    "matmul",
+    "newton_schulz",
+    "muon_momentum_",
+    "scaled_update_",
+    "adamw_",
+    "lion_",
+    "multi_sumsq",
+    "check_status",
+    "clear_status",
+    "StatusError",
+    "has_ext",
+    "KELLER_NS_COEFFS",
+    "DION_NS_COEFFS",
+]
+
+# Keller Jordan's fixed quintic coefficients (used 5x).
+KELLER_NS_COEFFS: Tuple[Tuple[float, float, float], ...] = ((3.4445, -4.7750, 2.0315),) * 5
+# Per-iteration schedule used by the dion package's Muon
+# (DION/muon.py:676-703 zeropower_via_newtonschulz5).
+DION_NS_COEFFS: Tuple[Tuple[float, float, float], ...] = (
+    (4.0848, -6.8946, 2.9270),
+    (3.9505, -6.3029, 2.6377),
+    (3.7418, -5.5913, 2.3037),
+    (2.8769, -3.1427, 1.2046),
+    (2.8366, -3.0525, 1.2012),
+)
+
+
+def _as3d(t: Tensor) -> Tensor:
+    return t if t.dim() == 3 else t.unsqueeze(0)
+
+
+def _tma_ok(t: Tensor) -> bool:
+    """True if a bf16 3-D view has one unit stride and 16-byte aligned other strides."""
+    if t.data_ptr() % 16:
+        return False
+    s = t.stride()
+    if s[2] == 1:
+        inner_ok = s[1] % 8 == 0 or t.size(1) == 1
+    elif s[1] == 1:
+        inner_ok = s[2] % 8 == 0 or t.size(2) == 1
+    else:
+        return False
+    return inner_ok and (t.size(0) == 1 or s[0] % 8 == 0)
+
+
+def matmul(
+    A: Tensor,
+    B: Tensor,
+    out: Optional[Tensor] = None,
+    *,
+    C: Optional[Tensor] = None,
+    alpha: float = 1.0,
+    beta: float = 0.0,
+    symmetric: bool = False,
+    out_dtype: torch.dtype = torch.bfloat16,
+) -> Tensor:
+    """``out = alpha * A @ B + beta * C`` for (batched) bf16 ``A`` and ``B``.
+
+    ``A`` is ``[..., M, K]`` and ``B`` is ``[..., K, N]``; either may be a
+    transposed view (K- or MN-major storage). With ``symmetric=True`` the
+    product is known to be symmetric and only its upper triangle is computed
+    on the tensor cores (then mirrored).
+    """
+    squeeze = A.dim() == 2
+    A3, B3 = _as3d(A), _as3d(B)
+    batch, M, K = A3.shape
+    N = B3.size(-1)
+    if out is None:
+        out = torch.empty((batch, M, N), device=A.device, dtype=out_dtype)
+    out3 = _as3d(out)
+    C3 = _as3d(C) if C is not None else None
+    if not A.is_cuda:
+        res = alpha * torch.matmul(A3.float(), B3.float())
+        if C3 is not None and beta != 0.0:
+            res = res + beta * C3.float()
+        out3.copy_(res.to(out3.dtype))
+        return out3.squeeze(0) if squeeze else out3
+    if not (_tma_ok(A3) and _tma_ok(B3)):
+        A3 = A3.contiguous()
+        B3 = B3.contiguous()
+        if not (_tma_ok(A3) and _tma_ok(B3)):
+            # rows shorter than 16 bytes / unaligned: pad K to a multiple of 8
+            pad = (-K) % 8
+            A3 = torch.nn.functional.pad(A3, (0, pad))
+            B3 = torch.nn.functional.pad(B3.transpose(1, 2), (0, pad)).transpose(1, 2)
+            if not (_tma_ok(A3) and _tma_ok(B3)):
+                raise ValueError("dion_b200.ops.matmul: operand layout not supported by TMA")
+    ext().gemm(A3, B3, out3, C3, float(alpha), float(beta), None, 0, 0, bool(symmetric), False, 1.0, 1.0, 0)
+    return out3.squeeze(0) if squeeze else out3
+
+
+def _ns_reference(U: Tensor, coeffs: Sequence[Tuple[float, float, float]], eps: float) -> Tensor:
+    """Plain PyTorch quintic Newton-Schulz in fp32 (oracle / CPU path)."""
+    X = U.float()
+    tall = X.size(-2) > X.size(-1)
+    if tall:
+        X = X.mT
+    X = X / (X.norm(dim=(-2, -1), keepdim=True) + eps)
+    for a, b, c in coeffs:
+        A = X @ X.mT
+        Bm = b * A + c * (A @ A)
+        X = a * X + Bm @ X
+    if tall:
+        X = X.mT
+    return X
+
+
+def newton_schulz(
+    U: Tensor,
+    coeffs: Sequence[Tuple[float, float, float]] = KELLER_NS_COEFFS,
+    eps: float = 1e-7,
+    *,
+    scale: Optional[Tensor] = None,
+    out: Optional[Tensor] = None,
+    clobber_input: bool = False,
+) -> Tensor:
+    """Orthogonalise each matrix of ``U`` (``[batch, m, n]`` or ``[m, n]``).
+
+    ``scale`` (fp32, one value per matrix) is ``1/(||U_b||_F + eps)``; it is
+    computed here when not given (the Muon momentum kernel produces it for
+    free). Returns bf16.
+    """
+    squeeze = U.dim() == 2
+    U3 = _as3d(U)
+    if not U.is_cuda:
+        res = _ns_reference(U3, coeffs, eps).to(torch.bfloat16)
+        if out is not None:
+            _as3d(out).copy_(res)
+            return out
+        return res.squeeze(0) if squeeze else res
+    if U3.dtype != torch.bfloat16 or not U3.is_contiguous():
+        U3 = U3.to(torch.bfloat16).contiguous()
+        clobber_input = True
+    m, n = U3.shape[-2:]
+    if (m % 8) or (n % 8):
+        # pad both dims with zeros: orthogonalisation of [[X, 0], [0, 0]] keeps X's block
+        pm, pn = (-m) % 8, (-n) % 8
+        Up = torch.nn.functional.pad(U3, (0, pn, 0, pm)).contiguous()
+        res = newton_schulz(Up, coeffs, eps, scale=scale, clobber_input=True)[..., :m, :n]
+        res = res.contiguous()
+        if out is not None:
+            _as3d(out).copy_(res)
+            return out
+        return res.squeeze(0) if squeeze else res
+    if scale is None:
+        ss = multi_sumsq(list(U3.unbind(0)))
+        scale = 1.0 / (ss.sqrt() + eps)
+    out3 = _as3d(out) if out is not None else torch.empty_like(U3)
+    flat = [float(x) for abc in coeffs for x in abc]
+    ext().newton_schulz(U3, scale.float().contiguous(), flat, out3, bool(clobber_input))
+    return out3.squeeze(0) if (squeeze and out is None) else out3
+
+
+def multi_sumsq(X: List[Tensor]) -> Tensor:
+    """fp32 sum of squares of each tensor (deterministic order)."""
+    if not X:
+        return torch.empty(0)
+    if not X[0].is_cuda:
+        return torch.stack([x.float().square().sum() for x in X])
+    out = torch.empty(len(X), device=X[0].device, dtype=torch.float32)
+    ext().multi_sumsq([x.contiguous() for x in X], out)
+    return out
+
+
+def muon_momentum_(
+    M: List[Tensor], G: List[Tensor], U: List[Tensor], mu: float, nesterov: bool, eps: float = 1e-7
+) -> Tuple[Tensor, Tensor]:
+    """``M = mu*M + G``; ``U = bf16(nesterov ? mu*M + G : M)``.
+
+    Returns ``(sumsq, scale)`` per tensor with ``scale = 1/(||U||_F + eps)``.
+    """
+    n = len(M)
+    if n == 0:
+        return torch.empty(0), torch.empty(0)
+    if not M[0].is_cuda:
+        sumsq = []
+        for m, g, u in zip(M, G, U):
+            m.mul_(mu).add_(g.to(m.dtype))
+            src = m * mu + g.to(m.dtype) if nesterov else m
+            u.copy_(src.to(torch.bfloat16))
+            sumsq.append(u.float().square().sum())
+        ss = torch.stack(sumsq)
+        return ss, 1.0 / (ss.sqrt() + eps)
+    dev = M[0].device
+    sumsq = torch.empty(n, device=dev, dtype=torch.float32)
+    scale = torch.empty(n, device=dev, dtype=torch.float32)
+    ext().muon_momentum(M, [g.contiguous() for g in G], U, float(mu), bool(nesterov), sumsq, scale, float(eps))
+    return sumsq, scale
+
+
+def scaled_update_(X: List[Tensor], U: List[Tensor], decay: float, lrs: Sequence[float] | Tensor) -> None:
+    """``X[i] = decay * X[i] - lrs[i] * U[i]`` in place."""
+    if not X:
+        return
+    if not X[0].is_cuda:
+        for i, (x, u) in enumerate(zip(X, U)):
+            lr = float(lrs[i])
+            x.copy_((decay * x.float() - lr * u.float()).to(x.dtype))
+        return
+    if not isinstance(lrs, Tensor):
+        lrs = torch.tensor([float(v) for v in lrs], dtype=torch.float32).to(X[0].device, non_blocking=True)
+    ext().scaled_update(X, [u.contiguous() for u in U], float(decay), lrs.float())
+
+
+def adamw_(
+    X: List[Tensor],
+    G: List[Tensor],
+    M: List[Tensor],
+    V: List[Tensor],
+    lr: float,
+    beta1: float,
+    beta2: float,
+    weight_decay: float,
+    epsilon: float,
+    step: int,
+    cautious_wd: bool = False,
+) -> None:
+    """Fused multi-tensor AdamW (decoupled weight decay, bias-corrected)."""
+    if not X:
+        return
+    if not X[0].is_cuda:
+        bc1 = 1 - beta1**step
+        bc2s = math.sqrt(1 - beta2**step)
+        for x, g, m, v in zip(X, G, M, V):
+            gf = g.to(m.dtype)
+            m.lerp_(gf, 1 - beta1)
+            v.lerp_((gf * gf).to(v.dtype), 1 - beta2)
+            upd = m / (v.sqrt() / bc2s + epsilon)
+            if cautious_wd:
+                mask = (upd * x >= 0).to(x.dtype)
+                x.sub_(x * mask * (lr * weight_decay))
+            else:
+                x.mul_(1 - lr * weight_decay)
+            x.sub_((upd * (lr / bc1)).to(x.dtype))
+        return
+    ext().adamw(X, [g.contiguous() for g in G], M, V, float(lr), float(beta1), float(beta2), float(weight_decay),
+                float(epsilon), int(step), bool(cautious_wd))
+
+
+def lion_(
+    X: List[Tensor],
+    G: List[Tensor],
+    M: List[Tensor],
+    lr: float,
+    beta1: float,
+    beta2: float,
+    weight_decay: float,
+    cautious_wd: bool = False,
+) -> None:
+    """Fused multi-tensor Lion."""
+    if not X:
+        return
+    if not X[0].is_cuda:
+        for x, g, m in zip(X, G, M):
+            gf = g.to(m.dtype)
+            u = m.lerp(gf, 1 - beta1).sign_()
+            m.lerp_(gf, 1 - beta2)
+            if cautious_wd:
+                mask = (u * x >= 0).to(x.dtype)
+                x.sub_(x * mask * (lr * weight_decay))
+            else:
+                x.mul_(1 - lr * weight_decay)
+            x.sub_((u * lr).to(x.dtype))
+        return
+    ext().lion(X, [g.contiguous() for g in G], M, float(lr), float(beta1), float(beta2), float(weight_decay),
+               bool(cautious_wd))

@@ -1,0 +1,69 @@
+"""tcgen05 GEMM kernel vs a plain PyTorch fp32 reference."""
+import pytest
+import torch
+
+from dion_b200 import ops
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref(A, B, C=None, alpha=1.0, beta=0.0):
+    r = alpha * (A.float() @ B.float())
+    if C is not None:
+        r = r + beta * C.float()
+    return r
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).norm() / (b.float().norm() + 1e-12)).item()
+
+
+@pytest.mark.parametrize("a_t", [False, True])
+@pytest.mark.parametrize("b_t", [False, True])
+@pytest.mark.parametrize("shape", [(256, 512, 384), (200, 296, 72), (128, 128, 64), (3, 520, 1032, 264)])
+def test_gemm_layouts(a_t, b_t, shape):
+    torch.manual_seed(0)
+    if len(shape) == 3:
+        batch, (M, N, K) = 1, shape
+    else:
+        batch, M, N, K = shape
+    dev = "cuda"
+    A = torch.randn(batch, K, M, device=dev).bfloat16().transpose(1, 2) if a_t else torch.randn(batch, M, K, device=dev).bfloat16()
+    B = torch.randn(batch, N, K, device=dev).bfloat16().transpose(1, 2) if b_t else torch.randn(batch, K, N, device=dev).bfloat16()
+    out = ops.matmul(A, B, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    ops.check_status()
+    assert _rel(out, _ref(A, B)) < 1e-5
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_gemm_epilogue_beta(dtype):
+    torch.manual_seed(1)
+    A = torch.randn(2, 384, 256, device="cuda").bfloat16()
+    B = torch.randn(2, 256, 640, device="cuda").bfloat16()
+    C = torch.randn(2, 384, 640, device="cuda").to(dtype)
+    out = ops.matmul(A, B, C=C, alpha=0.5, beta=-1.5, out_dtype=dtype)
+    torch.cuda.synchronize()
+    tol = 1e-2 if dtype == torch.bfloat16 else 1e-5
+    assert _rel(out, _ref(A, B, C, 0.5, -1.5)) < tol
+
+
+@pytest.mark.parametrize("n", [128, 384, 520, 1024])
+def test_gemm_symmetric(n):
+    torch.manual_seed(2)
+    X = torch.randn(2, n, 328, device="cuda").bfloat16()
+    out = torch.full((2, n, n), float("nan"), device="cuda", dtype=torch.float32)
+    ops.matmul(X, X.transpose(1, 2), out, symmetric=True)
+    torch.cuda.synchronize()
+    assert not torch.isnan(out).any()
+    assert _rel(out, _ref(X, X.transpose(1, 2))) < 1e-5
+
+
+def test_gemm_large_bf16():
+    torch.manual_seed(3)
+    A = torch.randn(2048, 4096, device="cuda").bfloat16()
+    B = torch.randn(4096, 3072, device="cuda").bfloat16()
+    out = ops.matmul(A, B)
+    torch.cuda.synchronize()
+    ops.check_status()
+    assert _rel(out, _ref(A, B)) < 1e-2
