@@ -6,7 +6,8 @@
 namespace bdion {
 void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10::optional<at::Tensor>& C, double alpha,
           double beta, const c10::optional<at::Tensor>& scale, int64_t alpha_pow, int64_t beta_pow, bool sym,
-          bool param_mode, double gamma, double delta, int64_t bn_pref);
+          bool param_mode, double gamma, double delta, int64_t bn_pref, const c10::optional<at::Tensor>& D_ptrs,
+          int64_t ldd_ptrs, int64_t out_dtype_ptrs);
 void newton_schulz(at::Tensor& U, const at::Tensor& scale, const std::vector<double>& coeffs, at::Tensor& out,
                    bool clobber_input);
 void muon_momentum(const std::vector<at::Tensor>& M, const std::vector<at::Tensor>& G,
@@ -20,6 +21,19 @@ void adamw(const std::vector<at::Tensor>& X, const std::vector<at::Tensor>& G, c
            int64_t step, bool cautious);
 void lion(const std::vector<at::Tensor>& X, const std::vector<at::Tensor>& G, const std::vector<at::Tensor>& M,
           double lr, double beta1, double beta2, double wd, bool cautious);
+void rms_norm_fwd(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, at::Tensor& rstd, double eps);
+void rms_norm_bwd(const at::Tensor& gy, const at::Tensor& x, const at::Tensor& w, const at::Tensor& rstd,
+                  at::Tensor& gx, at::Tensor& gw);
+void rope_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& tab, at::Tensor& qo, at::Tensor& ko,
+              bool inverse);
+void swiglu_fwd(const at::Tensor& a, const at::Tensor& b, at::Tensor& o);
+void swiglu_bwd(const at::Tensor& g, const at::Tensor& a, const at::Tensor& b, at::Tensor& ga, at::Tensor& gb);
+void cross_entropy_fwd_bwd(const at::Tensor& logits, const at::Tensor& labels, at::Tensor& grad, at::Tensor& loss,
+                           double scale);
+void dion_momentum_add(const std::vector<at::Tensor>& M, const std::vector<at::Tensor>& G, at::Tensor& nz);
+void dion_fixup(at::Tensor& P, at::Tensor& R, const at::Tensor& Q0, const at::Tensor& nz);
+void col_sumsq(const at::Tensor& R, at::Tensor& out);
+void col_normalize(const at::Tensor& R, const at::Tensor& sumsq, double eps, at::Tensor& Q);
 }  // namespace bdion
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -27,7 +41,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &bdion::gemm, "tcgen05 batched bf16 GEMM with fused epilogue", py::arg("A"), py::arg("B"),
         py::arg("D"), py::arg("C") = py::none(), py::arg("alpha") = 1.0, py::arg("beta") = 0.0,
         py::arg("scale") = py::none(), py::arg("alpha_pow") = 0, py::arg("beta_pow") = 0, py::arg("sym") = false,
-        py::arg("param_mode") = false, py::arg("gamma") = 1.0, py::arg("delta") = 1.0, py::arg("bn") = 0);
+        py::arg("param_mode") = false, py::arg("gamma") = 1.0, py::arg("delta") = 1.0, py::arg("bn") = 0,
+        py::arg("D_ptrs") = py::none(), py::arg("ldd_ptrs") = 0, py::arg("out_dtype_ptrs") = 0);
   m.def("newton_schulz", &bdion::newton_schulz, "batched quintic Newton-Schulz", py::arg("U"), py::arg("scale"),
         py::arg("coeffs"), py::arg("out"), py::arg("clobber_input") = false);
   m.def("muon_momentum", &bdion::muon_momentum);
@@ -35,8 +50,19 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("scaled_update", &bdion::scaled_update);
   m.def("adamw", &bdion::adamw);
   m.def("lion", &bdion::lion);
+  m.def("rms_norm_fwd", &bdion::rms_norm_fwd);
+  m.def("rms_norm_bwd", &bdion::rms_norm_bwd);
+  m.def("rope_fwd", &bdion::rope_fwd);
+  m.def("swiglu_fwd", &bdion::swiglu_fwd);
+  m.def("swiglu_bwd", &bdion::swiglu_bwd);
+  m.def("cross_entropy_fwd_bwd", &bdion::cross_entropy_fwd_bwd);
+  m.def("dion_momentum_add", &bdion::dion_momentum_add);
+  m.def("dion_fixup", &bdion::dion_fixup);
+  m.def("col_sumsq", &bdion::col_sumsq);
+  m.def("col_normalize", &bdion::col_normalize);
   m.def("status_read", &bdion::status_read);
   m.def("status_clear", &bdion::status_clear);
   m.def("set_wait_limit_ns", &bdion::set_wait_limit_ns);
   m.def("wait_limit_ns", &bdion::wait_limit_ns);
+  m.def("launch_count", &bdion::launch_count);
 }

@@ -1,0 +1,216 @@
+// Dion power-iteration helpers (fp32 math):
+//   * multi-tensor momentum accumulate M += G with a per-matrix "not all
+//     zero" flag (max |M|), feeding the all-zero/NaN guard;
+//   * the guard itself: P = nan_to_num(P) * nz ; R = nan_to_num(R) * nz + Q0 * !nz
+//   * per-column sum of squares of a batch of (rows x r) matrices, and the
+//     column normalisation Q = R / (sqrt(sumsq) + eps) written in Q's dtype.
+// Reference behaviour: ada_dion/optim/adadion_v2.py:1795-1869
+// (fix_all_zero_or_nan, local_column_sum_sq, column_normalize).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+#include "host_utils.h"
+
+namespace bdion {
+
+namespace {
+
+constexpr int kMax = 48;
+constexpr int kChunk = 16384;
+constexpr int kThreads = 256;
+
+struct AddArgs {
+  int n;
+  void* m[kMax];
+  const void* g[kMax];
+  int64_t numel[kMax];
+  int chunk_start[kMax + 1];
+};
+
+__device__ __forceinline__ float nan0(float v) { return (v != v) ? 0.f : (isinf(v) ? copysignf(3.402823466e38f, v) : v); }
+
+template <typename MT, typename GT>
+__global__ void __launch_bounds__(kThreads) momentum_add_kernel(AddArgs a, float* partial_max) {
+  __shared__ float sh[32];
+  const int blk = blockIdx.x;
+  int t = 0;
+  while (t + 1 < a.n && a.chunk_start[t + 1] <= blk) ++t;
+  const int64_t lo = (int64_t)(blk - a.chunk_start[t]) * kChunk;
+  const int64_t hi = min(a.numel[t], lo + kChunk);
+  MT* M = reinterpret_cast<MT*>(a.m[t]);
+  const GT* G = reinterpret_cast<const GT*>(a.g[t]);
+  float mx = 0.f;
+  for (int64_t i = lo + threadIdx.x; i < hi; i += kThreads) {
+    const float v = to_f<MT>(M[i]) + to_f<GT>(G[i]);
+    M[i] = from_f<MT>(v);
+    mx = fmaxf(mx, fabsf(v) + (v != v ? 1.f : 0.f));
+  }
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffff, mx, o));
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x / 32] = mx;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float r = 0.f;
+    for (int i = 0; i < kThreads / 32; ++i) r = fmaxf(r, sh[i]);
+    partial_max[blk] = r;
+  }
+}
+
+__global__ void finalize_nz_kernel(AddArgs a, const float* partial_max, float* nz) {
+  const int t = blockIdx.x;
+  float r = 0.f;
+  for (int b = a.chunk_start[t] + threadIdx.x; b < a.chunk_start[t + 1]; b += blockDim.x) r = fmaxf(r, partial_max[b]);
+  for (int o = 16; o > 0; o >>= 1) r = fmaxf(r, __shfl_xor_sync(0xffffffff, r, o));
+  if (threadIdx.x == 0) nz[t] = r > 0.f ? 1.f : 0.f;
+}
+
+// P: [b, pn] , R: [b, rn], Q0: [b, rn] (may differ in dtype: QT), nz: [b]
+template <typename QT>
+__global__ void fixup_kernel(float* P, int64_t pn, float* R, const QT* Q0, int64_t rn, const float* nz) {
+  const int b = blockIdx.y;
+  const bool keep = nz[b] != 0.f;
+  float* Pb = P + (int64_t)b * pn;
+  float* Rb = R + (int64_t)b * rn;
+  const QT* Qb = Q0 + (int64_t)b * rn;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < max(pn, rn); i += (int64_t)gridDim.x * blockDim.x) {
+    if (i < pn) Pb[i] = keep ? nan0(Pb[i]) : 0.f;
+    if (i < rn) Rb[i] = keep ? nan0(Rb[i]) : to_f<QT>(Qb[i]);
+  }
+}
+
+// column sum of squares: R [b, rows, r] row-major -> partial [b, chunks, r]
+constexpr int kRowsPerChunk = 256;
+__global__ void col_sumsq_kernel(const float* R, int rows, int r, float* partial, int chunks) {
+  const int b = blockIdx.z, ch = blockIdx.y;
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= r) return;
+  const float* Rb = R + (int64_t)b * rows * r;
+  const int r0 = ch * kRowsPerChunk, r1 = min(rows, r0 + kRowsPerChunk);
+  float s = 0.f;
+  for (int i = r0; i < r1; ++i) {
+    const float v = Rb[(int64_t)i * r + c];
+    s += v * v;
+  }
+  partial[((int64_t)b * chunks + ch) * r + c] = s;
+}
+
+__global__ void col_sumsq_finalize(const float* partial, int chunks, int r, int batch, float* out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)batch * r) return;
+  const int b = (int)(i / r), c = (int)(i % r);
+  float s = 0.f;
+  for (int ch = 0; ch < chunks; ++ch) s += partial[((int64_t)b * chunks + ch) * r + c];
+  out[i] = s;
+}
+
+template <typename QT>
+__global__ void col_normalize_kernel(const float* R, const float* sumsq, int rows, int r, float eps, QT* Q,
+                                     int64_t q_bstride, int64_t q_ld) {
+  const int b = blockIdx.z;
+  const int64_t total = (int64_t)rows * r;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int row = (int)(i / r), c = (int)(i % r);
+    const float inv = 1.f / (sqrtf(sumsq[(int64_t)b * r + c]) + eps);
+    Q[(int64_t)b * q_bstride + (int64_t)row * q_ld + c] = from_f<QT>(R[(int64_t)b * total + i] * inv);
+  }
+}
+
+#define DISPATCH_FB(dt, T, ...)                           \
+  if ((dt) == at::kFloat) {                               \
+    using T = float;                                      \
+    __VA_ARGS__                                           \
+  } else if ((dt) == at::kBFloat16) {                     \
+    using T = __nv_bfloat16;                              \
+    __VA_ARGS__                                           \
+  } else {                                                \
+    TORCH_CHECK(false, "dion_b200: fp32 or bf16 expected"); \
+  }
+
+}  // namespace
+
+void dion_momentum_add(const std::vector<at::Tensor>& M, const std::vector<at::Tensor>& G, at::Tensor& nz) {
+  if (M.empty()) return;
+  c10::cuda::CUDAGuard guard(M[0].device());
+  auto s = at::cuda::getCurrentCUDAStream();
+  for (size_t b0 = 0; b0 < M.size(); b0 += kMax) {
+    const size_t e = std::min(M.size(), b0 + kMax);
+    AddArgs a{};
+    a.n = (int)(e - b0);
+    int chunks = 0;
+    for (size_t i = b0; i < e; ++i) {
+      TORCH_CHECK(M[i].is_contiguous() && G[i].is_contiguous() && M[i].numel() == G[i].numel(),
+                  "dion_b200 momentum_add: contiguous same-size tensors expected");
+      a.m[i - b0] = M[i].data_ptr();
+      a.g[i - b0] = G[i].data_ptr();
+      a.numel[i - b0] = M[i].numel();
+      a.chunk_start[i - b0] = chunks;
+      chunks += (int)((M[i].numel() + kChunk - 1) / kChunk);
+    }
+    a.chunk_start[a.n] = chunks;
+    auto part = at::empty({chunks}, M[0].options().dtype(at::kFloat));
+    DISPATCH_FB(M[0].scalar_type(), MT, DISPATCH_FB(G[0].scalar_type(), GT, {
+                  momentum_add_kernel<MT, GT><<<chunks, kThreads, 0, s>>>(a, part.data_ptr<float>());
+                }));
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    note_launch();
+    finalize_nz_kernel<<<a.n, 32, 0, s>>>(a, part.data_ptr<float>(), nz.data_ptr<float>() + b0);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    note_launch();
+  }
+}
+
+void dion_fixup(at::Tensor& P, at::Tensor& R, const at::Tensor& Q0, const at::Tensor& nz) {
+  TORCH_CHECK(P.is_contiguous() && R.is_contiguous() && Q0.is_contiguous() && P.scalar_type() == at::kFloat &&
+                  R.scalar_type() == at::kFloat,
+              "dion_b200 fixup: contiguous fp32 P/R expected");
+  c10::cuda::CUDAGuard guard(P.device());
+  const int b = (int)P.size(0);
+  const int64_t pn = P.numel() / b, rn = R.numel() / b;
+  dim3 grid((unsigned)std::min<int64_t>((std::max(pn, rn) + 255) / 256, 1024), b);
+  auto s = at::cuda::getCurrentCUDAStream();
+  DISPATCH_FB(Q0.scalar_type(), QT, {
+    fixup_kernel<QT><<<grid, 256, 0, s>>>(P.data_ptr<float>(), pn, R.data_ptr<float>(),
+                                          reinterpret_cast<const QT*>(Q0.data_ptr()), rn, nz.data_ptr<float>());
+  });
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  note_launch();
+}
+
+void col_sumsq(const at::Tensor& R, at::Tensor& out) {
+  TORCH_CHECK(R.dim() == 3 && R.is_contiguous() && R.scalar_type() == at::kFloat, "dion_b200 col_sumsq: [b,rows,r] fp32");
+  c10::cuda::CUDAGuard guard(R.device());
+  const int b = (int)R.size(0), rows = (int)R.size(1), r = (int)R.size(2);
+  const int chunks = (rows + kRowsPerChunk - 1) / kRowsPerChunk;
+  auto part = at::empty({b, chunks, r}, R.options());
+  auto s = at::cuda::getCurrentCUDAStream();
+  dim3 grid((r + 127) / 128, chunks, b);
+  col_sumsq_kernel<<<grid, 128, 0, s>>>(R.data_ptr<float>(), rows, r, part.data_ptr<float>(), chunks);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  note_launch();
+  const int64_t tot = (int64_t)b * r;
+  col_sumsq_finalize<<<(unsigned)((tot + 255) / 256), 256, 0, s>>>(part.data_ptr<float>(), chunks, r, b,
+                                                                     out.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  note_launch();
+}
+
+// Q (any [b, rows, r] view with unit column stride, fp32 or bf16) = R / (sqrt(sumsq) + eps)
+void col_normalize(const at::Tensor& R, const at::Tensor& sumsq, double eps, at::Tensor& Q) {
+  TORCH_CHECK(R.dim() == 3 && R.is_contiguous() && R.scalar_type() == at::kFloat, "dion_b200 col_normalize: R fp32");
+  TORCH_CHECK(Q.dim() == 3 && Q.stride(2) == 1 && Q.size(1) == R.size(1) && Q.size(2) == R.size(2),
+              "dion_b200 col_normalize: Q shape");
+  c10::cuda::CUDAGuard guard(R.device());
+  const int b = (int)R.size(0), rows = (int)R.size(1), r = (int)R.size(2);
+  const int64_t total = (int64_t)rows * r;
+  dim3 grid((unsigned)std::min<int64_t>((total + 255) / 256, 2048), 1, b);
+  auto s = at::cuda::getCurrentCUDAStream();
+  DISPATCH_FB(Q.scalar_type(), QT, {
+    col_normalize_kernel<QT><<<grid, 256, 0, s>>>(R.data_ptr<float>(), sumsq.data_ptr<float>(), rows, r, (float)eps,
+                                                  reinterpret_cast<QT*>(Q.data_ptr()), Q.stride(0), Q.stride(1));
+  });
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  note_launch();
+}
+
+}  // namespace bdion

@@ -347,9 +347,11 @@ void muon_momentum(const std::vector<at::Tensor>& M, const std::vector<at::Tenso
                             a, (float)mu, nesterov ? 1 : 0, vec ? 1 : 0, partial.data_ptr<float>());
                       }));
     C10_CUDA_KERNEL_LAUNCH_CHECK();
+  note_launch();
     finalize_sumsq_kernel<<<a.n, kThreads, 0, s>>>(a, partial.data_ptr<float>(), sumsq.data_ptr<float>() + b,
                                                      scale.data_ptr<float>() + b, (float)eps);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
+  note_launch();
   });
 }
 
@@ -365,9 +367,11 @@ void multi_sumsq(const std::vector<at::Tensor>& X, at::Tensor& sumsq) {
       sumsq_kernel<T><<<a.total_chunks, kThreads, 0, s>>>(a, vec ? 1 : 0, partial.data_ptr<float>());
     });
     C10_CUDA_KERNEL_LAUNCH_CHECK();
+  note_launch();
     finalize_sumsq_kernel<<<a.n, kThreads, 0, s>>>(a, partial.data_ptr<float>(), sumsq.data_ptr<float>() + b,
                                                      nullptr, 0.f);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
+  note_launch();
   });
 }
 
@@ -385,6 +389,7 @@ void scaled_update(const std::vector<at::Tensor>& X, const std::vector<at::Tenso
                             a, (float)decay, lrs.data_ptr<float>() + b, vec ? 1 : 0);
                       }));
     C10_CUDA_KERNEL_LAUNCH_CHECK();
+  note_launch();
   });
 }
 
@@ -405,6 +410,7 @@ void adamw(const std::vector<at::Tensor>& X, const std::vector<at::Tensor>& G, c
                             (float)bc2s, cautious ? 1 : 0, vec ? 1 : 0);
                       })));
     C10_CUDA_KERNEL_LAUNCH_CHECK();
+  note_launch();
   });
 }
 
@@ -421,6 +427,7 @@ void lion(const std::vector<at::Tensor>& X, const std::vector<at::Tensor>& G, co
                             a, (float)lr, (float)beta1, (float)beta2, (float)wd, cautious ? 1 : 0, vec ? 1 : 0);
                       })));
     C10_CUDA_KERNEL_LAUNCH_CHECK();
+  note_launch();
   });
 }
 

@@ -6,8 +6,7 @@
 
 #include <mutex>
 
-#include "gemm_tc.cuh"
-#include "host_utils.h"
+#include "gemm_launch.cuh"
 
 namespace bdion {
 
@@ -31,27 +30,33 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 3-D bf16 tensor map over storage [batch][rows][cols] (cols contiguous),
-// box = {64 cols, box_rows rows, 1}, 128-byte swizzle, zero fill out of bounds.
-CUtensorMap make_map_bf16(const void* base, int64_t cols, int64_t rows, int64_t batch, int64_t ld, int64_t bstride,
-                          int box_rows) {
+// 3-D tensor map over storage [batch][rows][cols] (cols contiguous), box =
+// {one 128-byte row of elements, box_rows, 1}, 128-byte swizzle, zero fill
+// out of bounds.
+CUtensorMap make_map(const void* base, bool fp32, int64_t cols, int64_t rows, int64_t batch, int64_t ld,
+                     int64_t bstride, int box_rows, bool mn_major) {
   CUtensorMap m;
+  const int esz = fp32 ? 4 : 2;
   cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)batch};
   if (batch <= 1) bstride = ld * rows;
-  cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), (cuuint64_t)(bstride * 2)};
-  cuuint32_t box[3] = {64u, (cuuint32_t)box_rows, 1u};
+  cuuint64_t strides[2] = {(cuuint64_t)(ld * esz), (cuuint64_t)(bstride * esz)};
+  cuuint32_t box[3] = {(cuuint32_t)(128 / esz), (cuuint32_t)box_rows, 1u};
   cuuint32_t estr[3] = {1u, 1u, 1u};
   TORCH_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "dion_b200 gemm: operand base must be 16-byte aligned");
-  TORCH_CHECK((ld * 2) % 16 == 0 && (bstride * 2) % 16 == 0,
-              "dion_b200 gemm: operand row/batch strides must be multiples of 16 bytes (ld % 8 == 0)");
-  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK((ld * esz) % 16 == 0 && (bstride * esz) % 16 == 0,
+              "dion_b200 gemm: operand row/batch strides must be multiples of 16 bytes");
+  CUresult r = encode_fn()(&m, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
+                           const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           (fp32 && mn_major) ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   TORCH_CHECK(r == CUDA_SUCCESS, "dion_b200 gemm: cuTensorMapEncodeTiled failed with ", (int)r);
   return m;
 }
 
-int sm_count() {
+}  // namespace
+
+int gemm_sm_count() {
   static int n = [] {
     int dev = 0, v = 0;
     cudaGetDevice(&dev);
@@ -61,81 +66,67 @@ int sm_count() {
   return n;
 }
 
-template <int BN, bool A_MN, bool B_MN, typename OutT, typename CT, bool PARAM>
-void launch_typed(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& args, cudaStream_t stream) {
-  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, OutT, CT, PARAM>;
-  constexpr int smem = GemmCfg<BN>::kSmemBytes;
-  static bool attr_set = false;
-  if (!attr_set) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr_set = true;
-  }
-  const int grid = std::min(args.total_tiles, sm_count());
-  kern<<<grid, 192, smem, stream>>>(ma, mb, args);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
-}
-
-template <bool A_MN, bool B_MN, typename OutT, typename CT, bool PARAM>
-void launch_bn(int bn, const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& args, cudaStream_t s) {
-  if (bn == 256)
-    launch_typed<256, A_MN, B_MN, OutT, CT, PARAM>(ma, mb, args, s);
-  else
-    launch_typed<128, A_MN, B_MN, OutT, CT, PARAM>(ma, mb, args, s);
-}
-
-template <typename OutT, typename CT, bool PARAM>
-void launch_major(bool a_mn, bool b_mn, int bn, const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& args,
-                  cudaStream_t s) {
-  if (!a_mn && !b_mn)
-    launch_bn<false, false, OutT, CT, PARAM>(bn, ma, mb, args, s);
-  else if (!a_mn && b_mn)
-    launch_bn<false, true, OutT, CT, PARAM>(bn, ma, mb, args, s);
-  else if (a_mn && !b_mn)
-    launch_bn<true, false, OutT, CT, PARAM>(bn, ma, mb, args, s);
-  else
-    launch_bn<true, true, OutT, CT, PARAM>(bn, ma, mb, args, s);
-}
-
-}  // namespace
-
-// A: [batch, M, K] bf16 view, B: [batch, K, N] bf16 view (any layout with one
-// unit stride in the last two dims); D: [batch, M, N] row-major output.
+// A: [batch, M, K] view, B: [batch, K, N] view (any layout with one unit
+// stride in the last two dims), both bf16 (tensor-core bf16) or both fp32
+// (tensor-core tf32). D: [batch, M, N] row-major output, or, when D_ptrs is
+// given (int64 device tensor of batch addresses), per-batch outputs with row
+// stride ldd_ptrs.
 // param_mode: D = gamma*D + delta*(alpha*A@B + beta*C) in place.
 void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10::optional<at::Tensor>& C, double alpha,
           double beta, const c10::optional<at::Tensor>& scale, int64_t alpha_pow, int64_t beta_pow, bool sym,
-          bool param_mode, double gamma, double delta, int64_t bn_pref) {
-  TORCH_CHECK(A.is_cuda() && B.is_cuda() && D.is_cuda(), "dion_b200 gemm: CUDA tensors expected");
-  TORCH_CHECK(A.dim() == 3 && B.dim() == 3 && D.dim() == 3, "dion_b200 gemm: 3-D [batch, rows, cols] views expected");
-  TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16,
-              "dion_b200 gemm: bf16 operands expected");
+          bool param_mode, double gamma, double delta, int64_t bn_pref, const c10::optional<at::Tensor>& D_ptrs,
+          int64_t ldd_ptrs, int64_t out_dtype_ptrs) {
+  TORCH_CHECK(A.is_cuda() && B.is_cuda(), "dion_b200 gemm: CUDA tensors expected");
+  TORCH_CHECK(A.dim() == 3 && B.dim() == 3, "dion_b200 gemm: 3-D [batch, rows, cols] views expected");
+  const bool fp32_in = A.scalar_type() == at::kFloat;
+  TORCH_CHECK((A.scalar_type() == at::kBFloat16 || fp32_in) && B.scalar_type() == A.scalar_type(),
+              "dion_b200 gemm: operands must both be bf16 or both fp32");
   const int64_t batch = A.size(0), M = A.size(1), K = A.size(2), N = B.size(2);
   TORCH_CHECK(B.size(0) == batch && B.size(1) == K, "dion_b200 gemm: shape mismatch");
-  TORCH_CHECK(D.size(0) == batch && D.size(1) == M && D.size(2) == N && D.stride(2) == 1,
-              "dion_b200 gemm: D must be [batch, M, N] with unit column stride");
   TORCH_CHECK(K > 0 && M > 0 && N > 0, "dion_b200 gemm: empty problem");
+  const bool use_ptrs = D_ptrs.has_value() && D_ptrs->defined();
+  if (!use_ptrs) {
+    TORCH_CHECK(D.is_cuda() && D.dim() == 3 && D.size(0) == batch && D.size(1) == M && D.size(2) == N &&
+                    D.stride(2) == 1,
+                "dion_b200 gemm: D must be [batch, M, N] with unit column stride");
+  } else {
+    TORCH_CHECK(D_ptrs->scalar_type() == at::kLong && D_ptrs->numel() >= batch && D_ptrs->is_cuda(),
+                "dion_b200 gemm: D_ptrs must be an int64 CUDA tensor of batch addresses");
+  }
   c10::cuda::CUDAGuard guard(A.device());
 
-  // Operand majors from strides.
   const bool a_mn = A.stride(2) != 1;  // A stored [K][M]
   const bool b_mn = B.stride(2) == 1;  // B stored [K][N] (N contiguous)
   TORCH_CHECK(a_mn ? A.stride(1) == 1 : A.stride(2) == 1, "dion_b200 gemm: A needs a unit stride");
   TORCH_CHECK(b_mn ? B.stride(2) == 1 : B.stride(1) == 1, "dion_b200 gemm: B needs a unit stride");
-  if (sym) TORCH_CHECK(M == N && !param_mode, "dion_b200 gemm: symmetric mode needs a square output");
+  if (sym) TORCH_CHECK(M == N && !param_mode && !use_ptrs, "dion_b200 gemm: symmetric mode needs a square output");
 
+  const int row_elems = fp32_in ? 32 : 64;  // elements per 128-byte swizzle row
   int bn = (bn_pref == 128 || bn_pref == 256) ? (int)bn_pref : (N > 128 ? 256 : 128);
-  CUtensorMap ma = a_mn ? make_map_bf16(A.data_ptr(), M, K, batch, A.stride(2), A.stride(0), 64)
-                        : make_map_bf16(A.data_ptr(), K, M, batch, A.stride(1), A.stride(0), kBM);
-  CUtensorMap mb = b_mn ? make_map_bf16(B.data_ptr(), N, K, batch, B.stride(1), B.stride(0), 64)
-                        : make_map_bf16(B.data_ptr(), K, N, batch, B.stride(2), B.stride(0), bn);
+  CUtensorMap ma = a_mn ? make_map(A.data_ptr(), fp32_in, M, K, batch, A.stride(2), A.stride(0), row_elems, true)
+                        : make_map(A.data_ptr(), fp32_in, K, M, batch, A.stride(1), A.stride(0), kBM, false);
+  CUtensorMap mb = b_mn ? make_map(B.data_ptr(), fp32_in, N, K, batch, B.stride(1), B.stride(0), row_elems, true)
+                        : make_map(B.data_ptr(), fp32_in, K, N, batch, B.stride(2), B.stride(0), bn, false);
 
   GemmArgs args{};
   args.M = (int)M;
   args.N = (int)N;
   args.K = (int)K;
   args.batch = (int)batch;
-  args.D = D.data_ptr();
-  args.ldd = D.stride(1);
-  args.strideD = D.stride(0);
+  at::ScalarType out_t;
+  if (use_ptrs) {
+    args.D = nullptr;
+    args.D_ptrs = reinterpret_cast<void* const*>(D_ptrs->data_ptr<int64_t>());
+    args.ldd = ldd_ptrs;
+    args.strideD = 0;
+    out_t = static_cast<at::ScalarType>(out_dtype_ptrs);
+  } else {
+    args.D = D.data_ptr();
+    args.D_ptrs = nullptr;
+    args.ldd = D.stride(1);
+    args.strideD = D.stride(0);
+    out_t = D.scalar_type();
+  }
   args.C = nullptr;
   if (C.has_value() && C->defined()) {
     TORCH_CHECK(C->dim() == 3 && C->size(0) == batch && C->size(1) == M && C->size(2) == N && C->stride(2) == 1,
@@ -169,37 +160,32 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10::op
   args.status = status_device_ptr();
   args.limit_ns = wait_limit_ns();
 
-  // vector epilogue accesses need 16-byte aligned rows
   auto aligned16 = [](const void* p, int64_t ld, int64_t bs, int esz) {
     return reinterpret_cast<uintptr_t>(p) % 16 == 0 && (ld * esz) % 16 == 0 && (bs * esz) % 16 == 0;
   };
-  const int dsz = D.element_size();
-  TORCH_CHECK(aligned16(args.D, args.ldd, batch > 1 ? args.strideD : 0, dsz), "dion_b200 gemm: D rows must be 16B aligned");
-  if (args.C) TORCH_CHECK(aligned16(args.C, args.ldc, batch > 1 ? args.strideC : 0, C->element_size()),
-                          "dion_b200 gemm: C rows must be 16B aligned");
+  const int dsz = (out_t == at::kFloat) ? 4 : 2;
+  if (!use_ptrs) {
+    TORCH_CHECK(aligned16(args.D, args.ldd, batch > 1 ? args.strideD : 0, dsz), "dion_b200 gemm: D rows must be 16B aligned");
+  } else {
+    TORCH_CHECK((args.ldd * dsz) % 16 == 0, "dion_b200 gemm: D rows must be 16B aligned");
+  }
+  if (args.C) {
+    TORCH_CHECK(aligned16(args.C, args.ldc, batch > 1 ? args.strideC : 0, C->element_size()),
+                "dion_b200 gemm: C rows must be 16B aligned");
+  }
+  if (args.C && !param_mode) {
+    TORCH_CHECK(C->scalar_type() == out_t, "dion_b200 gemm: C must match D dtype");
+  }
+  if (args.C && param_mode) {
+    TORCH_CHECK(C->scalar_type() == at::kBFloat16, "dion_b200 gemm: param mode expects a bf16 C");
+  }
+  TORCH_CHECK(out_t == at::kFloat || out_t == at::kBFloat16, "dion_b200 gemm: output dtype must be bf16 or fp32");
 
   cudaStream_t s = at::cuda::getCurrentCUDAStream();
-  const auto dt = D.scalar_type();
-  const bool c_bf16 = !args.C || C->scalar_type() == at::kBFloat16;
-  if (param_mode) {
-    TORCH_CHECK(c_bf16, "dion_b200 gemm: param mode expects a bf16 C");
-    if (dt == at::kFloat)
-      launch_major<float, __nv_bfloat16, true>(a_mn, b_mn, bn, ma, mb, args, s);
-    else if (dt == at::kBFloat16)
-      launch_major<__nv_bfloat16, __nv_bfloat16, true>(a_mn, b_mn, bn, ma, mb, args, s);
-    else
-      TORCH_CHECK(false, "dion_b200 gemm: param dtype must be fp32 or bf16");
-  } else {
-    if (dt == at::kBFloat16) {
-      TORCH_CHECK(c_bf16, "dion_b200 gemm: C must match D dtype");
-      launch_major<__nv_bfloat16, __nv_bfloat16, false>(a_mn, b_mn, bn, ma, mb, args, s);
-    } else if (dt == at::kFloat) {
-      TORCH_CHECK(!args.C || C->scalar_type() == at::kFloat, "dion_b200 gemm: C must match D dtype");
-      launch_major<float, float, false>(a_mn, b_mn, bn, ma, mb, args, s);
-    } else {
-      TORCH_CHECK(false, "dion_b200 gemm: output dtype must be bf16 or fp32");
-    }
-  }
+  if (fp32_in)
+    gemm_dispatch_tf32(a_mn, b_mn, bn, ma, mb, args, s, out_t, param_mode);
+  else
+    gemm_dispatch_bf16(a_mn, b_mn, bn, ma, mb, args, s, out_t, param_mode);
 }
 
 }  // namespace bdion

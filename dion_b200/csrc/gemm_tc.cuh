@@ -1,4 +1,6 @@
-// Persistent, warp-specialised bf16 GEMM on the sm_100a tensor cores.
+// Persistent, warp-specialised GEMM on the sm_100a tensor cores: bf16
+// operands (kind::f16) or fp32 operands on the tf32 path (kind::tf32), fp32
+// accumulation in TMEM.
 //
 //   D[b] = epilogue( alpha_b * A[b] @ B[b] , C[b] )
 //
@@ -34,6 +36,7 @@ namespace bdion {
 struct GemmArgs {
   int M, N, K, batch;
   void* D;
+  void* const* D_ptrs;  // optional per-batch output pointers (device array)
   int64_t ldd, strideD;
   const void* C;  // may be null
   int64_t ldc, strideC;
@@ -50,14 +53,31 @@ struct GemmArgs {
 };
 
 constexpr int kBM = 128;
-constexpr int kBK = 64;  // 64 bf16 = 128 bytes = one swizzle row
 constexpr int kGroupM = 8;
+
+// Per-input-type constants: one K block is one 128-byte swizzle row.
+template <typename TIn>
+struct InCfg;
+template <>
+struct InCfg<__nv_bfloat16> {
+  static constexpr int kBK = 64;      // elements per 128-byte row
+  static constexpr int kUmmaK = 16;   // K per tcgen05.mma
+  static constexpr uint32_t kFmt = 1; // bf16
+  static constexpr bool kTf32 = false;
+};
+template <>
+struct InCfg<float> {
+  static constexpr int kBK = 32;
+  static constexpr int kUmmaK = 8;
+  static constexpr uint32_t kFmt = 2; // tf32
+  static constexpr bool kTf32 = true;
+};
 
 template <int BN>
 struct GemmCfg {
   static constexpr int kStages = BN >= 256 ? 4 : 6;
-  static constexpr int kABytes = kBM * kBK * 2;
-  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kABytes = kBM * 128;
+  static constexpr int kBBytes = BN * 128;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = 2 * BN;
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
@@ -90,12 +110,20 @@ __device__ __forceinline__ void decode_tile(const GemmArgs& a, int local, int& t
   tn = in_g / gsize;
 }
 
-template <int BN, bool A_MN, bool B_MN, typename OutT, typename CT, bool PARAM>
+template <typename TIn, int BN, bool A_MN, bool B_MN, typename OutT, typename CT, bool PARAM>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const GemmArgs args) {
   using Cfg = GemmCfg<BN>;
+  using IC = InCfg<TIn>;
   constexpr int S = Cfg::kStages;
+  constexpr int kBK = IC::kBK;
+  constexpr int kBoxBytes = kBK * 128;           // one MN-major box: kBK MN elems x kBK K rows
+  constexpr int kKStepMN = IC::kUmmaK * 128;      // MN-major: K advance per MMA (rows x 128 B)
+  // MN-major smem layout: bf16 uses the 128B swizzle (8-row atoms, SBO 1024);
+  // tf32 must use the 128B swizzle with 32B atoms (4-row atoms, SBO 512).
+  constexpr uint32_t kMNLayout = IC::kTf32 ? 1u : 2u;
+  constexpr uint32_t kMNSbo = IC::kTf32 ? 512u : 1024u;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -138,7 +166,7 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int num_kb = (args.K + kBK - 1) / kBK;
+  const int num_kb = (args.K + IC::kBK - 1) / IC::kBK;
   const uint64_t limit = args.limit_ns;
 
   if (warp == 0) {
@@ -165,15 +193,15 @@ __global__ void __launch_bounds__(192, 1)
             tma_load_3d(&tmA, &full_bar[stage], a_dst, kb * kBK, tm * kBM, b);
           } else {
 #pragma unroll
-            for (int h = 0; h < kBM / 64; ++h)
-              tma_load_3d(&tmA, &full_bar[stage], a_dst + h * 8192, tm * kBM + h * 64, kb * kBK, b);
+            for (int h = 0; h < kBM / kBK; ++h)
+              tma_load_3d(&tmA, &full_bar[stage], a_dst + h * kBoxBytes, tm * kBM + h * kBK, kb * kBK, b);
           }
           if (!B_MN) {
             tma_load_3d(&tmB, &full_bar[stage], b_dst, kb * kBK, tn * BN, b);
           } else {
 #pragma unroll
-            for (int h = 0; h < BN / 64; ++h)
-              tma_load_3d(&tmB, &full_bar[stage], b_dst + h * 8192, tn * BN + h * 64, kb * kBK, b);
+            for (int h = 0; h < BN / kBK; ++h)
+              tma_load_3d(&tmB, &full_bar[stage], b_dst + h * kBoxBytes, tn * BN + h * kBK, kb * kBK, b);
           }
           ++issued;
           if (++stage == S) {
@@ -200,7 +228,7 @@ __global__ void __launch_bounds__(192, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc(kBM, BN, A_MN, B_MN, 1u);
+      constexpr uint32_t idesc = make_idesc(kBM, BN, A_MN, B_MN, IC::kFmt);
       int stage = 0;
       uint32_t phase = 0;
       int local_tile = 0;
@@ -226,12 +254,15 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t a_base = smem_u32(sA + stage * Cfg::kABytes);
           const uint32_t b_base = smem_u32(sB + stage * Cfg::kBBytes);
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k) {
-            const uint64_t adesc = A_MN ? make_sdesc_sw128(a_base + k * 2048, 8192, 1024)
+          for (int k = 0; k < kBK / IC::kUmmaK; ++k) {
+            const uint64_t adesc = A_MN ? make_sdesc_sw128(a_base + k * kKStepMN, kBoxBytes, kMNSbo, kMNLayout)
                                         : make_sdesc_sw128(a_base + k * 32, 16, 1024);
-            const uint64_t bdesc = B_MN ? make_sdesc_sw128(b_base + k * 2048, 8192, 1024)
+            const uint64_t bdesc = B_MN ? make_sdesc_sw128(b_base + k * kKStepMN, kBoxBytes, kMNSbo, kMNLayout)
                                         : make_sdesc_sw128(b_base + k * 32, 16, 1024);
-            umma_f16(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+            if (IC::kTf32)
+              umma_tf32(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+            else
+              umma_f16(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
           }
           issued_any = true;
           umma_commit(&empty_bar[stage]);
@@ -275,7 +306,8 @@ __global__ void __launch_bounds__(192, 1)
       }
       const int row = tm * kBM + q * 32 + lane;
       const bool row_ok = row < args.M;
-      OutT* Db = reinterpret_cast<OutT*>(args.D) + (int64_t)b * args.strideD;
+      OutT* Db = args.D_ptrs ? reinterpret_cast<OutT*>(args.D_ptrs[b])
+                             : reinterpret_cast<OutT*>(args.D) + (int64_t)b * args.strideD;
       const CT* Cb = args.C ? reinterpret_cast<const CT*>(args.C) + (int64_t)b * args.strideC : nullptr;
 
 #pragma unroll 1

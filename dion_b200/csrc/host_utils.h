@@ -9,5 +9,7 @@ int status_read();            // host read, no device synchronisation
 void status_clear();
 uint64_t wait_limit_ns();     // limit for every bounded device wait
 void set_wait_limit_ns(uint64_t ns);
+void note_launch(int n = 1);  // count of this extension's kernel launches
+uint64_t launch_count();
 
 }  // namespace bdion

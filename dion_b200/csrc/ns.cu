@@ -22,7 +22,8 @@ namespace bdion {
 
 void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10::optional<at::Tensor>& C, double alpha,
           double beta, const c10::optional<at::Tensor>& scale, int64_t alpha_pow, int64_t beta_pow, bool sym,
-          bool param_mode, double gamma, double delta, int64_t bn_pref);
+          bool param_mode, double gamma, double delta, int64_t bn_pref, const c10::optional<at::Tensor>& D_ptrs,
+          int64_t ldd_ptrs, int64_t out_dtype_ptrs);
 
 // U: [batch, m, n] bf16 contiguous (not normalised). scale: [batch] fp32.
 // out: [batch, m, n] bf16. If clobber_input, U may be used as scratch.
@@ -57,17 +58,17 @@ void newton_schulz(at::Tensor& U, const at::Tensor& scale, const std::vector<dou
     at::Tensor& dst = dst_of(i);
     if (!tall) {
       // A = X X^T : A-operand X [m,K=n] K-major; B-operand X^T [K=n, N=m] -> view of X, K-major
-      gemm(src, src.transpose(1, 2), A, none, 1.0, 0.0, sc, 2, 0, true, false, 0, 0, 0);
+      gemm(src, src.transpose(1, 2), A, none, 1.0, 0.0, sc, 2, 0, true, false, 0, 0, 0, none, 0, 0);
       // B = b A + c A A
-      gemm(A, A.transpose(1, 2), Bm, A, c, b, none, 0, 0, true, false, 0, 0, 0);
+      gemm(A, A.transpose(1, 2), Bm, A, c, b, none, 0, 0, true, false, 0, 0, 0, none, 0, 0);
       // X' = a X + B X : B-operand X [K=m, N=n] N-major
-      gemm(Bm, src, dst, src, 1.0, a, sc, 1, 1, false, false, 0, 0, 0);
+      gemm(Bm, src, dst, src, 1.0, a, sc, 1, 1, false, false, 0, 0, 0, none, 0, 0);
     } else {
       // A = X^T X : A-operand X^T [n, K=m] (MN-major view); B-operand X [K=m, N=n] N-major
-      gemm(src.transpose(1, 2), src, A, none, 1.0, 0.0, sc, 2, 0, true, false, 0, 0, 0);
-      gemm(A, A.transpose(1, 2), Bm, A, c, b, none, 0, 0, true, false, 0, 0, 0);
+      gemm(src.transpose(1, 2), src, A, none, 1.0, 0.0, sc, 2, 0, true, false, 0, 0, 0, none, 0, 0);
+      gemm(A, A.transpose(1, 2), Bm, A, c, b, none, 0, 0, true, false, 0, 0, 0, none, 0, 0);
       // X' = a X + X B : A-operand X [m, K=n] K-major; B-operand B [K=n, N=n] (symmetric) K-major view
-      gemm(src, Bm.transpose(1, 2), dst, src, 1.0, a, sc, 1, 1, false, false, 0, 0, 0);
+      gemm(src, Bm.transpose(1, 2), dst, src, 1.0, a, sc, 1, 1, false, false, 0, 0, 0, none, 0, 0);
     }
     src = dst;
   }

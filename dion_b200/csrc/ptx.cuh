@@ -176,13 +176,17 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
 //  bits [32,46) stride-dimension byte offset >> 4
 //  bits [46,48) version = 1
 //  bits [61,64) layout = 2 (SWIZZLE_128B)
-__device__ __forceinline__ uint64_t make_sdesc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+// layout 2 = SWIZZLE_128B (16-byte chunks permuted over 8 rows);
+// layout 1 = SWIZZLE_128B_BASE32B (32-byte chunks permuted over 4 rows), the
+// only layout the tf32 MN-major operand path accepts.
+__device__ __forceinline__ uint64_t make_sdesc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo,
+                                                    uint32_t layout = 2) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
   d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
   d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
   d |= static_cast<uint64_t>(1) << 46;
-  d |= static_cast<uint64_t>(2) << 61;
+  d |= static_cast<uint64_t>(layout & 7u) << 61;
   return d;
 }
 

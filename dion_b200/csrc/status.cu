@@ -16,6 +16,7 @@ volatile int* g_host_word = nullptr;
 int* g_dev_word = nullptr;
 std::once_flag g_once;
 std::atomic<uint64_t> g_limit_ns{2000000000ull};
+std::atomic<uint64_t> g_launches{0};
 
 void init_word() {
   void* h = nullptr;
@@ -42,5 +43,7 @@ void status_clear() {
 }
 uint64_t wait_limit_ns() { return g_limit_ns.load(); }
 void set_wait_limit_ns(uint64_t ns) { g_limit_ns.store(ns); }
+void note_launch(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
+uint64_t launch_count() { return g_launches.load(); }
 
 }  // namespace bdion

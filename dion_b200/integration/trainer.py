@@ -1,0 +1,160 @@
+"""Minimal Llama trainer (no torchtitan needed).
+
+One process per GPU; FSDP2/HSDP over the data-parallel mesh; the hybrid
+optimizer container; warmup + cosine LR schedule with a floor (as in
+ada_dion/integration/config_registry.py:161-184: warmup 200, cosine decay
+to 10 %, grad-norm clip 1.0); synthetic uniform tokens.
+
+``train_step`` is the public per-step API: it takes the step's host batch
+(pinned int64 tokens / labels), copies it to the device, runs forward,
+backward, clipping and the optimizer, and returns the loss tensor.
+"""
+from __future__ import annotations
+
+import math
+import os
+import time
+from dataclasses import dataclass, field
+from typing import Dict, Iterator, List, Optional, Tuple
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+
+from ..models.llama3 import Llama3Config, Transformer, llama3_config
+from ..parallel.fsdp import apply_fsdp
+from ..parallel.mesh import ParallelDims, build_mesh, init_distributed
+from .hybrid_optimizer import HybridOptimizersContainer
+
+__all__ = ["TrainerConfig", "Trainer", "SyntheticTokens", "lr_lambda"]
+
+
+@dataclass
+class TrainerConfig:
+    model: str = "1B"
+    model_overrides: Dict = field(default_factory=dict)
+    seq_len: int = 4096
+    local_batch_size: int = 8
+    steps: int = 100
+    warmup_steps: int = 200
+    decay_ratio: Optional[float] = None
+    min_lr_factor: float = 0.1
+    max_norm: float = 1.0
+    seed: int = 2
+    init_mode: str = "normal"
+    dp_replicate: int = 1
+    dp_shard: int = -1
+    tp: int = 1
+    use_fsdp: bool = True
+    optimizer: HybridOptimizersContainer.Config = field(default_factory=HybridOptimizersContainer.Config)
+    log_freq: int = 10
+
+
+def lr_lambda(step: int, warmup: int, total: int, min_factor: float) -> float:
+    """Linear warmup then cosine decay to ``min_factor`` (multiplier on the base lr)."""
+    if warmup > 0 and step < warmup:
+        return (step + 1) / (warmup + 1)
+    if total <= warmup:
+        return 1.0
+    prog = min(1.0, (step - warmup) / max(1, total - warmup))
+    return min_factor + (1 - min_factor) * 0.5 * (1 + math.cos(math.pi * prog))
+
+
+class SyntheticTokens:
+    """Uniform random tokens over the vocabulary from a fixed seed, produced
+    on the host in pinned memory (one [global_batch, seq+1] draw per step;
+    each rank keeps its slice)."""
+
+    def __init__(self, vocab: int, seq_len: int, local_batch: int, seed: int, rank: int = 0, world: int = 1):
+        self.vocab, self.seq, self.lb = vocab, seq_len, local_batch
+        self.rank, self.world = rank, world
+        self.gen = torch.Generator().manual_seed(seed)
+
+    def next(self) -> Tuple[torch.Tensor, torch.Tensor]:
+        full = torch.randint(0, self.vocab, (self.lb * self.world, self.seq + 1), generator=self.gen)
+        mine = full[self.rank * self.lb : (self.rank + 1) * self.lb]
+        t = mine[:, :-1].contiguous().pin_memory() if torch.cuda.is_available() else mine[:, :-1].contiguous()
+        l = mine[:, 1:].contiguous().pin_memory() if torch.cuda.is_available() else mine[:, 1:].contiguous()
+        return t, l
+
+    def __iter__(self) -> Iterator[Tuple[torch.Tensor, torch.Tensor]]:
+        while True:
+            yield self.next()
+
+
+class Trainer:
+    def __init__(self, cfg: TrainerConfig, device: Optional[torch.device] = None):
+        self.cfg = cfg
+        self.rank, self.world, self.local_rank = init_distributed()
+        if device is None:
+            device = torch.device("cuda", self.local_rank) if torch.cuda.is_available() else torch.device("cpu")
+        self.device = device
+        self.mesh = None
+        shard_mesh = replicate_mesh = None
+        dims = ParallelDims(cfg.dp_replicate, cfg.dp_shard, cfg.tp)
+        if cfg.use_fsdp:
+            self.mesh = build_mesh(dims, device.type)
+            names = self.mesh.mesh_dim_names
+            dp_names = tuple(n for n in ("dp_replicate", "dp_shard") if n in names)
+            self.dp_mesh = self.mesh[dp_names] if len(dp_names) > 1 else self.mesh[dp_names[0]]
+            shard_mesh = self.mesh["dp_shard"] if "dp_shard" in names else None
+            replicate_mesh = self.mesh["dp_replicate"] if "dp_replicate" in names else None
+        mcfg: Llama3Config = llama3_config(cfg.model, **cfg.model_overrides)
+        mcfg.max_seq_len = max(mcfg.max_seq_len, cfg.seq_len)
+        self.model_cfg = mcfg
+        torch.manual_seed(cfg.seed)
+        with torch.device(device):
+            model = Transformer(mcfg)
+        gen = torch.Generator(device=device).manual_seed(cfg.seed)
+        model.init_weights(cfg.init_mode, generator=gen)
+        if cfg.use_fsdp:
+            apply_fsdp(model, self.dp_mesh)
+        self.model = model
+        self.optimizers = HybridOptimizersContainer(
+            cfg.optimizer, model_parts=[model], shard_mesh=shard_mesh, replicate_mesh=replicate_mesh
+        )
+        self._base_lrs = [[g["lr"] for g in o.param_groups] for o in self.optimizers]
+        self.step_idx = 0
+        self.data = SyntheticTokens(mcfg.vocab_size, cfg.seq_len, cfg.local_batch_size, cfg.seed, self.rank,
+                                    self.world // max(1, cfg.tp))
+
+    def _set_lr(self) -> None:
+        c = self.cfg
+        total = c.steps
+        f = lr_lambda(self.step_idx, c.warmup_steps, total, c.min_lr_factor)
+        for opt, base in zip(self.optimizers, self._base_lrs):
+            for g, b in zip(opt.param_groups, base):
+                g["lr"] = b * f
+
+    def forward_backward(self, tokens: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
+        loss = self.model.loss(tokens, labels)
+        loss.backward()
+        return loss
+
+    def train_step(self, tokens: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
+        """One optimisation step on a host (or device) batch; returns the device loss."""
+        tokens = tokens.to(self.device, non_blocking=True)
+        labels = labels.to(self.device, non_blocking=True)
+        self._set_lr()
+        loss = self.forward_backward(tokens, labels)
+        if self.cfg.max_norm and self.cfg.max_norm > 0:
+            torch.nn.utils.clip_grad_norm_(self.model.parameters(), self.cfg.max_norm, foreach=True)
+        self.optimizers.step()
+        self.optimizers.zero_grad(set_to_none=True)
+        self.step_idx += 1
+        return loss.detach()
+
+    def train(self, steps: Optional[int] = None, log=print) -> List[float]:
+        steps = steps or self.cfg.steps
+        losses = []
+        t0 = time.perf_counter()
+        for i in range(steps):
+            t, l = self.data.next()
+            loss = self.train_step(t, l)
+            if (i + 1) % self.cfg.log_freq == 0 or i == steps - 1:
+                v = loss.item()
+                losses.append(v)
+                if self.rank == 0 and log:
+                    dt = time.perf_counter() - t0
+                    log(f"step {self.step_idx} loss {v:.4f} ({dt:.1f}s)")
+        return losses

@@ -1,0 +1,196 @@
+"""Llama-3 style decoder with torchtitan-compatible parameter names.
+
+FQNs match torchtitan's Llama3 (tok_embeddings, layers.<i>.attention.{wq,wk,
+wv,wo}, layers.<i>.attention_norm, layers.<i>.feed_forward.{w1,w2,w3},
+layers.<i>.ffn_norm, norm, output) so the param grouper, checkpoints and the
+hybrid optimizer container see the same names as with the reference's model
+(ada_dion/integration/config_registry.py:60-154 builds its Llama3 specs the
+same way).
+
+Compute is bf16 on the tensor cores: cuBLAS for the plain projections,
+torch SDPA (flash/cuDNN) for attention with native grouped-query heads, and
+the package's fused kernels for RMSNorm, rotary embedding, SwiGLU and the
+chunked cross-entropy when they are available on the device.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field, replace
+from typing import Dict, Optional
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import layers as L
+
+__all__ = ["Llama3Config", "Transformer", "LLAMA3_CONFIGS", "llama3_config"]
+
+
+@dataclass
+class Llama3Config:
+    dim: int = 4096
+    n_layers: int = 32
+    n_heads: int = 32
+    n_kv_heads: Optional[int] = None
+    vocab_size: int = 128256
+    ffn_dim: Optional[int] = None
+    multiple_of: int = 256
+    ffn_dim_multiplier: Optional[float] = None
+    norm_eps: float = 1e-5
+    rope_theta: float = 500000.0
+    max_seq_len: int = 8192
+    depth_init: bool = True
+
+    def hidden_dim(self) -> int:
+        if self.ffn_dim is not None:
+            return self.ffn_dim
+        h = int(2 * (4 * self.dim) / 3)
+        if self.ffn_dim_multiplier is not None:
+            h = int(self.ffn_dim_multiplier * h)
+        return self.multiple_of * ((h + self.multiple_of - 1) // self.multiple_of)
+
+    @property
+    def kv_heads(self) -> int:
+        return self.n_kv_heads or self.n_heads
+
+    @property
+    def head_dim(self) -> int:
+        return self.dim // self.n_heads
+
+    def num_params(self, include_embedding: bool = True) -> int:
+        d, h, kv, hd = self.dim, self.hidden_dim(), self.kv_heads, self.head_dim
+        attn = d * d * 2 + 2 * d * kv * hd
+        ffn = 3 * d * h
+        per_layer = attn + ffn + 2 * d
+        n = self.n_layers * per_layer + d + self.vocab_size * d  # + output
+        if include_embedding:
+            n += self.vocab_size * d
+        return n
+
+    def flops_per_token(self, seq_len: int) -> int:
+        """Training FLOPs per token: 6 * non-embedding params + attention (12*l*h*q*t)."""
+        nparams = self.num_params(include_embedding=False)
+        return 6 * nparams + 12 * self.n_layers * self.n_heads * self.head_dim * seq_len
+
+
+LLAMA3_CONFIGS: Dict[str, Llama3Config] = {
+    # BASELINE config 1 (CPU): 4 layers, d=256, 4 heads, SwiGLU 1024, vocab 4096
+    "tiny": Llama3Config(dim=256, n_layers=4, n_heads=4, n_kv_heads=4, vocab_size=4096, ffn_dim=1024,
+                         rope_theta=10000.0, max_seq_len=256),
+    "debug": Llama3Config(dim=256, n_layers=6, n_heads=16, n_kv_heads=16, vocab_size=2048, ffn_dim=768,
+                          rope_theta=500000.0, max_seq_len=2048),
+    # reference paper model (ada_dion/integration/config_registry.py:60-89)
+    "160M": Llama3Config(dim=768, n_layers=12, n_heads=12, n_kv_heads=4, vocab_size=128256, ffn_dim=2048,
+                         rope_theta=500000.0, max_seq_len=8192),
+    "320M": Llama3Config(dim=1024, n_layers=16, n_heads=16, n_kv_heads=4, vocab_size=128256, ffn_dim=2816,
+                         rope_theta=500000.0, max_seq_len=8192),
+    "1B": Llama3Config(dim=2048, n_layers=16, n_heads=32, n_kv_heads=8, vocab_size=128256, ffn_dim=8192,
+                       rope_theta=500000.0, max_seq_len=8192),
+    "8B": Llama3Config(dim=4096, n_layers=32, n_heads=32, n_kv_heads=8, vocab_size=128256, ffn_dim=14336,
+                       rope_theta=500000.0, max_seq_len=8192),
+}
+
+
+def llama3_config(name: str, **overrides) -> Llama3Config:
+    return replace(LLAMA3_CONFIGS[name], **overrides)
+
+
+class Attention(nn.Module):
+    def __init__(self, cfg: Llama3Config):
+        super().__init__()
+        self.n_heads = cfg.n_heads
+        self.n_kv_heads = cfg.kv_heads
+        self.head_dim = cfg.head_dim
+        self.wq = nn.Linear(cfg.dim, cfg.n_heads * self.head_dim, bias=False)
+        self.wk = nn.Linear(cfg.dim, self.n_kv_heads * self.head_dim, bias=False)
+        self.wv = nn.Linear(cfg.dim, self.n_kv_heads * self.head_dim, bias=False)
+        self.wo = nn.Linear(cfg.n_heads * self.head_dim, cfg.dim, bias=False)
+
+    def forward(self, x: torch.Tensor, rope: torch.Tensor) -> torch.Tensor:
+        bs, seqlen, _ = x.shape
+        q = self.wq(x).view(bs, seqlen, self.n_heads, self.head_dim)
+        k = self.wk(x).view(bs, seqlen, self.n_kv_heads, self.head_dim)
+        v = self.wv(x).view(bs, seqlen, self.n_kv_heads, self.head_dim)
+        q, k = L.apply_rope(q, k, rope)
+        o = L.causal_attention(q, k, v)  # [bs, seq, heads, hd]
+        return self.wo(o.reshape(bs, seqlen, -1))
+
+
+class FeedForward(nn.Module):
+    def __init__(self, dim: int, hidden: int):
+        super().__init__()
+        self.w1 = nn.Linear(dim, hidden, bias=False)
+        self.w2 = nn.Linear(hidden, dim, bias=False)
+        self.w3 = nn.Linear(dim, hidden, bias=False)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return self.w2(L.swiglu(self.w1(x), self.w3(x)))
+
+
+class TransformerBlock(nn.Module):
+    def __init__(self, layer_id: int, cfg: Llama3Config):
+        super().__init__()
+        self.layer_id = layer_id
+        self.attention = Attention(cfg)
+        self.feed_forward = FeedForward(cfg.dim, cfg.hidden_dim())
+        self.attention_norm = L.RMSNorm(cfg.dim, cfg.norm_eps)
+        self.ffn_norm = L.RMSNorm(cfg.dim, cfg.norm_eps)
+        self.weight_init_std = 0.02 / (2 * (layer_id + 1)) ** 0.5 if cfg.depth_init else 0.02 / (2 * cfg.n_layers) ** 0.5
+
+    def forward(self, x: torch.Tensor, rope: torch.Tensor) -> torch.Tensor:
+        h = x + self.attention(self.attention_norm(x), rope)
+        return h + self.feed_forward(self.ffn_norm(h))
+
+
+class Transformer(nn.Module):
+    def __init__(self, cfg: Llama3Config):
+        super().__init__()
+        self.cfg = cfg
+        self.tok_embeddings = nn.Embedding(cfg.vocab_size, cfg.dim)
+        self.layers = nn.ModuleDict({str(i): TransformerBlock(i, cfg) for i in range(cfg.n_layers)})
+        self.norm = L.RMSNorm(cfg.dim, cfg.norm_eps)
+        self.output = nn.Linear(cfg.dim, cfg.vocab_size, bias=False)
+        self.register_buffer("rope_cache", L.rope_table(cfg.head_dim, cfg.max_seq_len, cfg.rope_theta), persistent=False)
+
+    @torch.no_grad()
+    def init_weights(self, mode: str = "normal", std: float = 0.02, generator: Optional[torch.Generator] = None):
+        """``normal``: every weight ~ N(0, std) (norm weights = 1);
+        ``torchtitan``: truncated normal with depth-scaled output projections."""
+        for name, p in self.named_parameters():
+            if name.endswith("norm.weight") or name == "norm.weight":
+                p.fill_(1.0)
+                continue
+            if mode == "normal":
+                p.normal_(0.0, std, generator=generator)
+            elif mode == "torchtitan":
+                if name == "tok_embeddings.weight":
+                    nn.init.normal_(p, generator=generator)
+                elif name == "output.weight":
+                    s = self.cfg.dim ** -0.5
+                    nn.init.trunc_normal_(p, std=s, a=-3 * s, b=3 * s, generator=generator)
+                else:
+                    layer = self.layers[name.split(".")[1]]
+                    s = 0.02 if any(k in name for k in ("wq", "wk", "wv", "w1")) else layer.weight_init_std
+                    nn.init.trunc_normal_(p, std=s, a=-2.0, b=2.0, generator=generator)
+            else:
+                raise ValueError(mode)
+        self.rope_cache = L.rope_table(self.cfg.head_dim, self.cfg.max_seq_len, self.cfg.rope_theta).to(
+            self.rope_cache.device
+        )
+
+    def forward(self, tokens: torch.Tensor, return_hidden: bool = False) -> torch.Tensor:
+        seqlen = tokens.shape[1]
+        h = self.tok_embeddings(tokens)
+        rope = self.rope_cache[:seqlen].float()
+        for layer in self.layers.values():
+            h = layer(h, rope)
+        h = self.norm(h)
+        if return_hidden:
+            return h
+        return self.output(h)
+
+    def loss(self, tokens: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
+        """Mean next-token cross-entropy, computed without materialising fp32 logits."""
+        h = self.forward(tokens, return_hidden=True)
+        return L.linear_cross_entropy(h, self.output.weight, labels)

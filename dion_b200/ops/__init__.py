@@ -17,6 +17,7 @@ from ._ext import ext, has_ext, check_status, clear_status, StatusError  # noqa:
 
 __all__ = [
     "matmul",
+    "matmul_update_",
     "newton_schulz",
     "muon_momentum_",
     "scaled_update_",
@@ -49,17 +50,18 @@ def _as3d(t: Tensor) -> Tensor:
 
 
 def _tma_ok(t: Tensor) -> bool:
-    """True if a bf16 3-D view has one unit stride and 16-byte aligned other strides."""
+    """True if a 3-D view has one unit stride and 16-byte aligned other strides."""
     if t.data_ptr() % 16:
         return False
+    q = 16 // t.element_size()
     s = t.stride()
     if s[2] == 1:
-        inner_ok = s[1] % 8 == 0 or t.size(1) == 1
+        inner_ok = s[1] % q == 0 or t.size(1) == 1
     elif s[1] == 1:
-        inner_ok = s[2] % 8 == 0 or t.size(2) == 1
+        inner_ok = s[2] % q == 0 or t.size(2) == 1
     else:
         return False
-    return inner_ok and (t.size(0) == 1 or s[0] % 8 == 0)
+    return inner_ok and (t.size(0) == 1 or s[0] % q == 0)
 
 
 def matmul(
@@ -73,7 +75,10 @@ def matmul(
     symmetric: bool = False,
     out_dtype: torch.dtype = torch.bfloat16,
 ) -> Tensor:
-    """``out = alpha * A @ B + beta * C`` for (batched) bf16 ``A`` and ``B``.
+    """``out = alpha * A @ B + beta * C`` for (batched) ``A`` and ``B``.
+
+    bf16 operands run on the bf16 tensor cores; fp32 operands run on the
+    tf32 tensor cores (fp32 accumulate, fp32 output).
 
     ``A`` is ``[..., M, K]`` and ``B`` is ``[..., K, N]``; either may be a
     transposed view (K- or MN-major storage). With ``symmetric=True`` the
@@ -84,6 +89,8 @@ def matmul(
     A3, B3 = _as3d(A), _as3d(B)
     batch, M, K = A3.shape
     N = B3.size(-1)
+    if A.dtype == torch.float32:
+        out_dtype = torch.float32
     if out is None:
         out = torch.empty((batch, M, N), device=A.device, dtype=out_dtype)
     out3 = _as3d(out)
@@ -98,14 +105,60 @@ def matmul(
         A3 = A3.contiguous()
         B3 = B3.contiguous()
         if not (_tma_ok(A3) and _tma_ok(B3)):
-            # rows shorter than 16 bytes / unaligned: pad K to a multiple of 8
-            pad = (-K) % 8
+            # rows shorter than 16 bytes / unaligned: pad K to a 16-byte multiple
+            pad = (-K) % (16 // A3.element_size())
             A3 = torch.nn.functional.pad(A3, (0, pad))
             B3 = torch.nn.functional.pad(B3.transpose(1, 2), (0, pad)).transpose(1, 2)
             if not (_tma_ok(A3) and _tma_ok(B3)):
                 raise ValueError("dion_b200.ops.matmul: operand layout not supported by TMA")
     ext().gemm(A3, B3, out3, C3, float(alpha), float(beta), None, 0, 0, bool(symmetric), False, 1.0, 1.0, 0)
     return out3.squeeze(0) if squeeze else out3
+
+
+_SCALAR_TYPE = {torch.float32: 6, torch.bfloat16: 15}
+_PTR_CACHE: dict = {}
+
+
+def _ptr_tensor(ts: Sequence[Tensor]) -> Tensor:
+    key = (ts[0].device, tuple(t.data_ptr() for t in ts))
+    p = _PTR_CACHE.get(key)
+    if p is None:
+        if len(_PTR_CACHE) > 4096:
+            _PTR_CACHE.clear()
+        p = torch.tensor([t.data_ptr() for t in ts], dtype=torch.int64).to(ts[0].device, non_blocking=True)
+        _PTR_CACHE[key] = p
+    return p
+
+
+def matmul_update_(
+    outs: Sequence[Tensor],
+    A: Tensor,
+    B: Tensor,
+    *,
+    gamma: float = 1.0,
+    delta: float = 1.0,
+    alpha: float = 1.0,
+) -> None:
+    """In place, for every b: ``outs[b] = gamma * outs[b] + delta * alpha * A[b] @ B[b]``.
+
+    ``outs`` are separate tensors (e.g. parameters) of identical shape and
+    row stride; ``A``/``B`` are batched operands. One launch: the kernel
+    reads the output addresses from a device pointer array.
+    """
+    A3, B3 = _as3d(A), _as3d(B)
+    assert len(outs) == A3.size(0)
+    if not A.is_cuda:
+        for o, a, b in zip(outs, A3.unbind(0), B3.unbind(0)):
+            o.copy_((gamma * o.float() + delta * alpha * (a.float() @ b.float())).to(o.dtype))
+        return
+    o0 = outs[0]
+    assert all(o.shape == o0.shape and o.stride() == o0.stride() and o.dtype == o0.dtype for o in outs)
+    assert o0.dim() == 2 and o0.stride(1) == 1
+    if not (_tma_ok(A3) and _tma_ok(B3)):
+        A3, B3 = A3.contiguous(), B3.contiguous()
+    ptrs = _ptr_tensor(outs)
+    ext().gemm(A3, B3, o0.unsqueeze(0), None, float(alpha), 0.0, None, 0, 0, False, True, float(gamma), float(delta),
+               0, ptrs, o0.stride(0), _SCALAR_TYPE[o0.dtype])
 
 
 def _ns_reference(U: Tensor, coeffs: Sequence[Tuple[float, float, float]], eps: float) -> Tensor:
@@ -283,3 +336,71 @@ def lion_(
         return
     ext().lion(X, [g.contiguous() for g in G], M, float(lr), float(beta1), float(beta2), float(weight_decay),
                bool(cautious_wd))
+
+
+# ---------------------------------------------------------------- Dion helpers
+def dion_momentum_add_(M: List[Tensor], G: List[Tensor]) -> Tensor:
+    """``M += G`` for each pair; returns fp32 flags (1 if M is not all zero)."""
+    if not M:
+        return torch.empty(0)
+    if not M[0].is_cuda:
+        out = []
+        for m, g in zip(M, G):
+            m.add_(g.to(m.dtype))
+            out.append(float(bool((m != 0).any())))
+        return torch.tensor(out, dtype=torch.float32)
+    nz = torch.empty(len(M), device=M[0].device, dtype=torch.float32)
+    ext().dion_momentum_add([m for m in M], [g.contiguous() for g in G], nz)
+    return nz
+
+
+def dion_fixup_(P: Tensor, R: Tensor, Q0: Tensor, nz: Tensor) -> None:
+    """All-zero / NaN guard: ``P = nan_to_num(P)*nz``, ``R = nan_to_num(R)*nz + Q0*(1-nz)`` per matrix."""
+    if not P.is_cuda:
+        keep = nz.view(-1, 1, 1).to(P.dtype)
+        P.copy_(P.nan_to_num() * keep)
+        R.copy_(R.nan_to_num() * keep + Q0.to(R.dtype) * (1 - keep))
+        return
+    ext().dion_fixup(P, R, Q0.contiguous(), nz)
+
+
+def col_sumsq(R: Tensor) -> Tensor:
+    """Per-column sum of squares of each matrix of ``R`` ([b, rows, r] fp32) -> [b, r]."""
+    if not R.is_cuda:
+        return R.float().square().sum(dim=-2)
+    out = torch.empty(R.size(0), R.size(2), device=R.device, dtype=torch.float32)
+    ext().col_sumsq(R.contiguous(), out)
+    return out
+
+
+def col_normalize(R: Tensor, sumsq: Tensor, eps: float, out: Tensor) -> Tensor:
+    """``out = R / (sqrt(sumsq) + eps)`` column-wise, written in ``out``'s dtype."""
+    if not R.is_cuda:
+        out.copy_((R.float() / (sumsq.unsqueeze(-2).sqrt() + eps)).to(out.dtype))
+        return out
+    ext().col_normalize(R.contiguous(), sumsq.contiguous(), float(eps), out)
+    return out
+
+
+def as_batch(ts: Sequence[Tensor]) -> Optional[Tensor]:
+    """If the tensors are equally spaced views of one storage (an arena),
+    return the [n, ...] strided view covering them; else None."""
+    t0 = ts[0]
+    if len(ts) == 1:
+        return t0.unsqueeze(0)
+    if any(t.shape != t0.shape or t.stride() != t0.stride() or t.dtype != t0.dtype for t in ts):
+        return None
+    try:
+        if any(t.untyped_storage().data_ptr() != t0.untyped_storage().data_ptr() for t in ts):
+            return None
+    except RuntimeError:
+        return None
+    es = t0.element_size()
+    d = (ts[1].data_ptr() - t0.data_ptr())
+    if d <= 0 or d % es:
+        return None
+    step = d // es
+    for i, t in enumerate(ts):
+        if t.data_ptr() != t0.data_ptr() + i * d:
+            return None
+    return t0.as_strided((len(ts),) + tuple(t0.shape), (step,) + tuple(t0.stride()))

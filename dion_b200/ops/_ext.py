@@ -52,7 +52,7 @@ def check_status(clear: bool = True) -> None:
     an error surfaces at the first check after the failing kernel finished.
     """
     mod = _load()
-    if mod is None:
+    if mod is None or not _cuda_ok():
         return
     code = mod.status_read()
     if code:
@@ -61,7 +61,13 @@ def check_status(clear: bool = True) -> None:
         raise StatusError(f"dion_b200 device status 0x{code:x}: {_CODES.get(code, 'unknown')}")
 
 
+def _cuda_ok() -> bool:
+    import torch
+
+    return torch.cuda.is_available()
+
+
 def clear_status() -> None:
     mod = _load()
-    if mod is not None:
+    if mod is not None and _cuda_ok():
         mod.status_clear()

@@ -1,0 +1,606 @@
+"""Dion: distributed low-rank orthonormalised updates with error feedback.
+
+Public surface and state layout follow the dion package / the reference's
+copy of it (ada_dion/optim/adadion_v2.py:82-249 constructor and validation,
+:661-748 state, :857-1112 DDP and FSDP updates, :1298-1448 FSDP x TP update,
+:1645-1947 helpers): param-group ``algorithm`` in {"dion", "adamw", "lion"};
+per-matrix state ``momentum`` (error feedback folded in) and ``Q`` (DTensor
+``Shard(0)`` on the outer shard mesh, ``Shard(1)`` on the inner mesh);
+``r = ceil(rank_fraction * min(m, n) / multiple) * multiple``.
+
+One step for a matrix X with momentum M and right factor Q:
+    M += G
+    P = M Q                       (transposed orientation when m < n)
+    P = orthogonalize(P)          (randomised Cholesky QR)
+    R = M^T P
+    guard all-zero / NaN
+    M -= (1 - mu) P R^T           (error feedback)
+    Q = R / ||R_col||
+    X = (1 - lr*wd) X - sqrt(fan_out/fan_in) * lr * P Q^T
+
+B200 design:
+  * momentum and Q of every same-shape group live in one arena tensor
+    ([n, rows, cols]); the per-parameter state entries are views of it, so
+    every product above is ONE batched tcgen05 GEMM over the group (tf32
+    for fp32 state, bf16 for bf16 state) instead of a stack-and-copy;
+  * the error-feedback and weight updates run as in-place GEMM epilogues
+    (the weight update writes each parameter through a device pointer
+    array), so M and X are read and written exactly once;
+  * FSDP: arenas are laid out rank-major, so the batched P leaves the GEMM
+    already in reduce-scatter order and the gathered P lands in GEMM order.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Any, Dict, List, Optional, Tuple, Union
+
+import torch
+import torch.distributed as dist
+import torch.distributed._functional_collectives as funcol
+from torch import Tensor
+from torch.distributed import ProcessGroup
+from torch.distributed.device_mesh import DeviceMesh
+from torch.distributed.tensor import DTensor, Partial, Placement, Replicate, Shard
+from torch.optim.optimizer import Optimizer, ParamsT
+
+from .. import ops
+from ._utils import group_by_signature, scalar_update, to_local
+from .linalg import orthogonalize
+
+try:
+    from torch.distributed.tensor.placement_types import _StridedShard
+except ImportError:  # pragma: no cover
+    _StridedShard = None
+
+__all__ = ["Dion", "DionMixedPrecisionConfig", "DionParamConfig"]
+
+
+@dataclass
+class DionMixedPrecisionConfig:
+    """dtype overrides for optimizer state; ``None`` = the parameter's dtype."""
+
+    momentum_dtype: Optional[torch.dtype] = None
+    Q_dtype: Optional[torch.dtype] = None
+    variance_dtype: Optional[torch.dtype] = None
+
+
+@dataclass
+class DionParamConfig:
+    outer_shard_tensor_dim: Optional[int] = None
+    inner_shard_tensor_dim: Optional[int] = None
+    outer_shard_mesh_dim: Optional[int] = None
+    inner_shard_mesh_dim: Optional[int] = None
+    is_transposed: bool = False
+    compressed_all_reduce: bool = False
+    Q_sharded_placements: Optional[Tuple[Placement, ...]] = None
+    Q_inner_unsharded_placements: Optional[Tuple[Placement, ...]] = None
+
+
+def _group_of(mesh: Union[DeviceMesh, ProcessGroup, None]) -> Optional[ProcessGroup]:
+    if mesh is None:
+        return None
+    if isinstance(mesh, DeviceMesh):
+        return mesh.get_group()
+    return mesh
+
+
+class Dion(Optimizer):
+    """Dion optimizer (DDP, FSDP2, HSDP and FSDP x TP layouts)."""
+
+    def __init__(
+        self,
+        params: ParamsT,
+        replicate_mesh: Optional[Union[DeviceMesh, ProcessGroup]] = None,
+        outer_shard_mesh: Optional[DeviceMesh] = None,
+        inner_shard_mesh: Optional[DeviceMesh] = None,
+        replicate_mesh_grad_sync: bool = True,
+        rank_fraction: float = 1.0,
+        rank_multiple_of: int = 1,
+        lr: float = 0.01,
+        mu: float = 0.95,
+        betas: Tuple[float, float] = (0.9, 0.95),
+        weight_decay: float = 0.01,
+        epsilon: float = 1e-8,
+        power_iters: int = 1,
+        qr_method: str = "rcqr",
+        cqr_warmup_steps: int = 150,
+        rcqr_oversample: float = 1.25,
+        mixed_precision_config: Optional[DionMixedPrecisionConfig] = None,
+    ):
+        if lr < 0.0:
+            raise ValueError(f"Invalid learning rate: {lr}")
+        if mu < 0.0:
+            raise ValueError(f"Invalid momentum factor (mu): {mu}")
+        if len(betas) != 2 or betas[0] < 0.0 or betas[1] < 0.0:
+            raise ValueError(f"Invalid betas: {betas}")
+        if weight_decay < 0.0:
+            raise ValueError(f"Invalid weight_decay value: {weight_decay}")
+        if rank_fraction <= 0 or rank_fraction > 1:
+            raise ValueError(f"Invalid rank fraction: {rank_fraction}")
+        if rank_multiple_of <= 0:
+            raise ValueError(f"Invalid rank multiple of: {rank_multiple_of}")
+        if power_iters != 1:
+            raise ValueError("Async Dion only supports power_iters=1")
+        if qr_method != "rcqr":
+            raise ValueError("Async Dion only supports qr_method='rcqr'")
+        if replicate_mesh is not None and not isinstance(replicate_mesh, (DeviceMesh, ProcessGroup)):
+            raise TypeError(f"Replicate mesh must be a DeviceMesh or ProcessGroup, but got {type(replicate_mesh)}.")
+        for name, mesh in (("Outer", outer_shard_mesh), ("Inner", inner_shard_mesh)):
+            if mesh is not None:
+                if not isinstance(mesh, DeviceMesh):
+                    raise TypeError(f"{name} shard mesh must be a DeviceMesh, but got {type(mesh)}.")
+                if mesh.ndim != 1:
+                    raise ValueError(f"{name} shard mesh must be 1D, but got {mesh.ndim}D. Try using a 1D sub-mesh.")
+                if mesh == replicate_mesh:
+                    raise ValueError(f"{name} shard mesh must be different from replicate mesh.")
+        if inner_shard_mesh is not None and inner_shard_mesh == outer_shard_mesh:
+            raise ValueError("Outer and inner shard meshes must be different.")
+
+        defaults = dict(
+            rank_fraction=rank_fraction,
+            rank_multiple_of=rank_multiple_of,
+            lr=lr,
+            mu=mu,
+            beta1=betas[0],
+            beta2=betas[1],
+            weight_decay=weight_decay,
+            epsilon=epsilon,
+            oversample=rcqr_oversample,
+            algorithm="dion",
+            step=0,
+        )
+        super().__init__(params, defaults)
+        self._param_config: Dict[Tensor, DionParamConfig] = {}
+        self._replicate_mesh = replicate_mesh
+        self._outer_shard_mesh = outer_shard_mesh
+        self._inner_shard_mesh = inner_shard_mesh
+        self._replicate_mesh_grad_sync = replicate_mesh_grad_sync
+        if isinstance(replicate_mesh, DeviceMesh):
+            self._replicate_world_size = replicate_mesh.size()
+        elif isinstance(replicate_mesh, ProcessGroup):
+            self._replicate_world_size = dist.get_world_size(replicate_mesh)
+        else:
+            self._replicate_world_size = 1
+        self._outer_shard_ranks = (
+            dist.get_process_group_ranks(outer_shard_mesh.get_group()) if outer_shard_mesh is not None else None
+        )
+        self._inner_shard_ranks = (
+            dist.get_process_group_ranks(inner_shard_mesh.get_group()) if inner_shard_mesh is not None else None
+        )
+        self._mixed_precision_config = mixed_precision_config or DionMixedPrecisionConfig()
+        self._arenas: Dict[Tuple, Dict[str, Any]] = {}
+
+    # ------------------------------------------------------------------ step
+    @torch.no_grad()
+    def step(self, closure=None):
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        for group in self.param_groups:
+            group["step"] += 1
+        for group in self.param_groups:
+            algo = group["algorithm"]
+            params = [p for p in group["params"] if p.grad is not None]
+            if not params:
+                continue
+            if algo == "dion":
+                self._dion_group(group, params)
+            elif algo in ("adamw", "lion"):
+                states = [self._get_or_initialize_state(p, group) for p in params]
+                grads = [p.grad for p in params]
+                if self._replicate_mesh is not None and self._replicate_mesh_grad_sync:
+                    grads = self._all_reduce_replicate([to_local(g) for g in grads])
+                scalar_update(algo, params, grads, states, group)
+            else:
+                raise ValueError(f"Unknown algorithm: {algo}")
+        ops.check_status()
+        return loss
+
+    @torch.no_grad()
+    def synchronize_for_checkpoint(self):
+        """Average every state tensor over the replicate mesh (compressed sync
+        lets the momenta of DP replicas drift; a checkpoint needs one copy)."""
+        if self._replicate_mesh is None or not self._replicate_mesh_grad_sync:
+            return
+        tensors = [v for st in self.state.values() for v in st.values() if isinstance(v, Tensor)]
+        if tensors:
+            local = [to_local(t) for t in tensors]
+            reduced = self._all_reduce_replicate(local)
+            for t, r in zip(local, reduced):
+                t.copy_(r)
+
+    # ------------------------------------------------------------------ config / state
+    def _get_dion_param_config(self, x: Tensor) -> DionParamConfig:
+        if x in self._param_config:
+            return self._param_config[x]
+        if x.ndim > 2:
+            raise NotImplementedError(f"Tensors with more than 2 dimensions are not supported. Got {x.ndim}D tensor.")
+        using_mesh = any(isinstance(m, DeviceMesh) for m in (self._replicate_mesh, self._outer_shard_mesh,
+                                                               self._inner_shard_mesh))
+        if using_mesh and not isinstance(x, DTensor):
+            raise TypeError("When using DeviceMesh, all parameters must be DTensor.")
+        if isinstance(self._replicate_mesh, ProcessGroup) and isinstance(x, DTensor):
+            raise TypeError(
+                "When using DTensor parameters, the data parallel group must be specified by a DeviceMesh instead of ProcessGroup."
+            )
+        cfg = DionParamConfig()
+        if x.ndim == 2:
+            m, n = x.shape
+            cfg.is_transposed = m < n
+        if isinstance(x, DTensor) and x.ndim == 2:
+            mesh = x.device_mesh
+            used = [None] * x.ndim
+            for mdim, pl in enumerate(x.placements):
+                if _StridedShard is not None and isinstance(pl, _StridedShard):
+                    raise NotImplementedError(
+                        "StridedShard is not supported. Ensure that FSDP and TP shard different dimensions of each matrix."
+                    )
+                if not pl.is_shard():
+                    continue
+                tdim = pl.dim
+                if used[tdim] is not None:
+                    raise RuntimeError(f"Got double-sharded DTensor for tensor dimension {tdim}.")
+                used[tdim] = mdim
+                ranks = dist.get_process_group_ranks(mesh.get_group(mdim))
+                outer = ranks == self._outer_shard_ranks
+                inner = ranks == self._inner_shard_ranks
+                if outer:
+                    cfg.outer_shard_tensor_dim, cfg.outer_shard_mesh_dim = tdim, mdim
+                if inner:
+                    cfg.inner_shard_tensor_dim, cfg.inner_shard_mesh_dim = tdim, mdim
+                if outer and inner:
+                    raise RuntimeError("Cannot have outer and inner sharding over the same process group.")
+                if mesh.size(mdim) > 1 and not outer and not inner:
+                    raise RuntimeError(
+                        f"Got DTensor sharded on unrecognized mesh_dim={mdim}, which does not match outer_shard_mesh or inner_shard_mesh."
+                    )
+            if cfg.inner_shard_tensor_dim == 0 or cfg.outer_shard_tensor_dim == 1:
+                cfg.is_transposed = False
+            if cfg.outer_shard_tensor_dim == 0 or cfg.inner_shard_tensor_dim == 1:
+                cfg.is_transposed = True
+        self._param_config[x] = cfg
+        return cfg
+
+    def _rank_of(self, shape, group) -> int:
+        m, n = shape
+        r = group["rank_fraction"] * min(m, n)
+        mult = group["rank_multiple_of"]
+        r = mult * math.ceil(r / mult)
+        return int(min(r, m, n))
+
+    def _get_or_initialize_state(self, p: Tensor, group: dict) -> dict:
+        st = self.state[p]
+        if not st:
+            algo = group["algorithm"]
+            mp = self._mixed_precision_config
+            if algo == "dion":
+                self._init_dion_states([p], group)
+            elif algo == "adamw":
+                st["momentum"] = torch.zeros_like(p, dtype=mp.momentum_dtype)
+                st["variance"] = torch.zeros_like(p, dtype=mp.variance_dtype)
+            elif algo in ("lion", "clion"):
+                st["momentum"] = torch.zeros_like(p, dtype=mp.momentum_dtype)
+            else:
+                raise ValueError(f"Unknown algorithm: {algo}")
+        return st
+
+    def _q_placements(self, p: DTensor, cfg: DionParamConfig) -> None:
+        pl = [Replicate() for _ in range(p.device_mesh.ndim)]
+        if cfg.outer_shard_mesh_dim is not None:
+            pl[cfg.outer_shard_mesh_dim] = Shard(0)
+        if cfg.inner_shard_mesh_dim is not None:
+            pl[cfg.inner_shard_mesh_dim] = Shard(1)
+        cfg.Q_sharded_placements = tuple(pl)
+        if cfg.inner_shard_mesh_dim is not None:
+            pl[cfg.inner_shard_mesh_dim] = Replicate()
+            cfg.Q_inner_unsharded_placements = tuple(pl)
+
+    def _init_dion_states(self, params: List[Tensor], group: dict, order: Optional[List[int]] = None,
+                          slots: Optional[int] = None) -> None:
+        """Allocate momentum and Q for same-signature params as views of two
+        arenas; ``order[i]`` is the arena slot of ``params[i]`` (extra slots
+        are zero padding used by the rank-major FSDP layout)."""
+        mp = self._mixed_precision_config
+        p0 = params[0]
+        if p0.ndim != 2:
+            raise ValueError(
+                f"Expected Dion parameters to be 2D matrix, but got {p0.ndim}D. "
+                "For scalar parameters, set 'algorithm' to 'lion' or 'adamw' when creating param group."
+            )
+        cfg = self._get_dion_param_config(p0)
+        m, n = p0.shape
+        r = self._rank_of((m, n), group)
+        q_shape = (m, r) if cfg.is_transposed else (n, r)
+        if group["rank_fraction"] < 1 and (m + n) * r < m * n:
+            cfg.compressed_all_reduce = True
+        q_dtype = mp.Q_dtype or p0.dtype
+        m_dtype = mp.momentum_dtype or p0.dtype
+        order = list(range(len(params))) if order is None else order
+        slots = slots or (max(order) + 1)
+        local0 = to_local(p0)
+        dev = local0.device
+        mom_arena = torch.zeros((slots,) + tuple(local0.shape), device=dev, dtype=m_dtype)
+        if isinstance(p0, DTensor):
+            self._q_placements(p0, cfg)
+            locals_ = []
+            for _ in params:
+                # the global Q is drawn identically on every rank (same RNG
+                # state), then each rank keeps its shard
+                f = torch.randn(q_shape, device=dev, dtype=q_dtype)
+                qd = DTensor.from_local(f, p0.device_mesh, [Replicate()] * p0.device_mesh.ndim, run_check=False)
+                locals_.append(qd.redistribute(placements=cfg.Q_sharded_placements).to_local())
+            q_arena = torch.zeros((slots,) + tuple(locals_[0].shape), device=dev, dtype=q_dtype)
+            for i, ql in zip(order, locals_):
+                q_arena[i].copy_(ql)
+        else:
+            q_arena = torch.zeros((slots,) + q_shape, device=dev, dtype=q_dtype)
+            for i in order:
+                q_arena[i].normal_()
+                self._replicate_broadcast(q_arena[i])
+        self._bind_arena(params, order, mom_arena, q_arena, cfg, q_shape)
+
+    def _bind_arena(self, params, order, mom_arena, q_arena, cfg, q_shape) -> None:
+        key = tuple(id(p) for p in params)
+        self._arenas[key] = {"M": mom_arena, "Q": q_arena, "order": list(order)}
+        for p, slot in zip(params, order):
+            self._param_config[p] = cfg
+            st = self.state[p]
+            mom, q = mom_arena[slot], q_arena[slot]
+            if isinstance(p, DTensor):
+                st["momentum"] = DTensor.from_local(mom, p.device_mesh, p.placements, run_check=False, shape=p.shape,
+                                                    stride=p.stride())
+                st["Q"] = DTensor.from_local(q, p.device_mesh, cfg.Q_sharded_placements, run_check=False,
+                                             shape=torch.Size(q_shape), stride=(q_shape[1], 1))
+            else:
+                st["momentum"] = mom
+                st["Q"] = q
+
+    def _arena(self, params: List[Tensor], group: dict, order: List[int], slots: int) -> Tuple[Tensor, Tensor]:
+        """Arena views ([slots, ...]) backing momentum and Q of ``params``.
+        State created elsewhere (e.g. loaded from a checkpoint) is packed into
+        a fresh arena and re-pointed."""
+        if any(not self.state[p] for p in params):
+            if all(not self.state[p] for p in params):
+                self._init_dion_states(params, group, order, slots)
+            else:
+                for p in params:
+                    if not self.state[p]:
+                        self._init_dion_states([p], group)
+        key = tuple(id(p) for p in params)
+        a = self._arenas.get(key)
+        ok = a is not None and a["order"] == list(order) and a["M"].size(0) == slots
+        if ok:
+            for p, slot in zip(params, order):
+                st = self.state[p]
+                if (to_local(st["momentum"]).data_ptr() != a["M"][slot].data_ptr()
+                        or to_local(st["Q"]).data_ptr() != a["Q"][slot].data_ptr()):
+                    ok = False
+                    break
+        if not ok:
+            M0 = to_local(self.state[params[0]]["momentum"])
+            Q0 = to_local(self.state[params[0]]["Q"])
+            mom_arena = torch.zeros((slots,) + tuple(M0.shape), device=M0.device, dtype=M0.dtype)
+            q_arena = torch.zeros((slots,) + tuple(Q0.shape), device=Q0.device, dtype=Q0.dtype)
+            for p, slot in zip(params, order):
+                mom_arena[slot].copy_(to_local(self.state[p]["momentum"]))
+                q_arena[slot].copy_(to_local(self.state[p]["Q"]))
+            cfg = self._get_dion_param_config(params[0])
+            Qs = self.state[params[0]]["Q"]
+            q_shape = tuple(Qs.shape)
+            if isinstance(params[0], DTensor) and cfg.Q_sharded_placements is None:
+                self._q_placements(params[0], cfg)
+            self._bind_arena(params, order, mom_arena, q_arena, cfg, q_shape)
+            a = self._arenas[key]
+        return a["M"], a["Q"]
+
+    def _replicate_broadcast(self, t: Tensor) -> None:
+        rm = self._replicate_mesh
+        if rm is None:
+            return
+        if isinstance(rm, DeviceMesh):
+            for g in rm.get_all_groups():
+                dist.broadcast(t, group=g, group_src=0)
+        else:
+            dist.broadcast(t, group=rm, group_src=0)
+
+    def _all_reduce_replicate(self, ts: List[Tensor], op: str = "avg") -> List[Tensor]:
+        rm = self._replicate_mesh
+        if rm is None:
+            return ts
+        pg = _group_of(rm)
+        if len(ts) == 1:
+            return [funcol.all_reduce(ts[0], reduceOp=op, group=pg).wait()]
+        return [x.wait() if hasattr(x, "wait") else x for x in funcol.all_reduce_coalesced(ts, reduceOp=op, group=pg)]
+
+    # ------------------------------------------------------------------ dion
+    def _dion_group(self, group: dict, params: List[Tensor]) -> None:
+        for same in group_by_signature(params).values():
+            cfg = self._get_dion_param_config(same[0])
+            if cfg.inner_shard_mesh_dim is not None:
+                self._dion_fsdp_tp(group, same, cfg)
+            elif cfg.outer_shard_mesh_dim is not None and self._outer_shard_mesh.size() > 1:
+                self._dion_sharded(group, same, cfg)
+            else:
+                self._dion_replicated(group, same, cfg)
+
+    def _scaled_lr(self, shape, lr: float) -> float:
+        fan_out, fan_in = shape
+        return math.sqrt(fan_out / fan_in) * lr
+
+    @staticmethod
+    def _op_dtype(dt: torch.dtype) -> torch.dtype:
+        # bf16 state runs on the bf16 tensor cores, anything else on tf32
+        return torch.bfloat16 if dt == torch.bfloat16 else torch.float32
+
+    def _power_p(self, Mb: Tensor, Qb: Tensor, transposed: bool) -> Tensor:
+        """P = M Q (or M^T Q), fp32 result."""
+        dt = self._op_dtype(Mb.dtype)
+        A = Mb.transpose(1, 2) if transposed else Mb
+        P = torch.empty((Mb.size(0), A.size(1), Qb.size(-1)), device=Mb.device, dtype=torch.float32)
+        ops.matmul(A.to(dt), Qb.to(dt), out=P)
+        return P
+
+    def _power_r(self, Mb: Tensor, P: Tensor, transposed: bool) -> Tensor:
+        """R = M^T P (or M P), fp32 result."""
+        dt = self._op_dtype(Mb.dtype)
+        A = Mb if transposed else Mb.transpose(1, 2)
+        R = torch.empty((Mb.size(0), A.size(1), P.size(-1)), device=Mb.device, dtype=torch.float32)
+        ops.matmul(A.to(dt), P.to(dt), out=R)
+        return R
+
+    def _update(self, group, params, order, Mb, Qb, P, R, nz, transposed, sumsq) -> None:
+        """Guard, error feedback, Q <- colnorm(R), weight update (all batched)."""
+        lr, mu = float(group["lr"]), float(group["mu"])
+        wd, eps = float(group["weight_decay"]), float(group["epsilon"])
+        ops.dion_fixup_(P, R, Qb, nz)
+        dt = self._op_dtype(Mb.dtype)
+        Pm, Rm = P.to(dt), R.to(dt)
+        slots = list(Mb.unbind(0))
+        # M -= (1 - mu) * P R^T   (R P^T when transposed)
+        if transposed:
+            ops.matmul_update_(slots, Rm, Pm.transpose(1, 2), gamma=1.0, delta=-(1.0 - mu))
+        else:
+            ops.matmul_update_(slots, Pm, Rm.transpose(1, 2), gamma=1.0, delta=-(1.0 - mu))
+        if sumsq is None:
+            sumsq = ops.col_sumsq(R)
+        ops.col_normalize(R, sumsq, eps, Qb)
+        # X = (1 - lr*wd) X - sqrt(fan_out/fan_in) lr * P Q^T   (Q P^T when transposed)
+        X = to_local(params)
+        xdt = self._op_dtype(X[0].dtype)
+        idx = torch.tensor(order, device=Mb.device)
+        Qn = Qb.index_select(0, idx).to(xdt)
+        Px = P.index_select(0, idx).to(xdt)
+        s_lr = self._scaled_lr(params[0].shape, lr)
+        if transposed:
+            ops.matmul_update_(X, Qn, Px.transpose(1, 2), gamma=1.0 - lr * wd, delta=-s_lr)
+        else:
+            ops.matmul_update_(X, Px, Qn.transpose(1, 2), gamma=1.0 - lr * wd, delta=-s_lr)
+
+    # ---- single device / DDP (replicated parameters)
+    def _dion_replicated(self, group: dict, params: List[Tensor], cfg: DionParamConfig) -> None:
+        n = len(params)
+        order = list(range(n))
+        Mb, Qb = self._arena(params, group, order, n)
+        G = [to_local(p.grad) for p in params]
+        world = self._replicate_world_size
+        rm = self._replicate_mesh
+        multi = rm is not None and world > 1
+        compressed = self._replicate_mesh_grad_sync and cfg.compressed_all_reduce and multi
+        if self._replicate_mesh_grad_sync and not cfg.compressed_all_reduce and multi:
+            G = self._all_reduce_replicate(G)
+        nz = ops.dion_momentum_add_(list(Mb.unbind(0)), G)
+        t = cfg.is_transposed
+        P = self._power_p(Mb, Qb, t)
+        pd, r = P.shape[1:]
+        if multi:
+            # each replica orthogonalises every world-th matrix, then all-gather
+            pg = _group_of(rm)
+            rank = dist.get_rank(pg)
+            sets = (n + world - 1) // world
+            Pp = torch.zeros((sets * world, pd, r), device=P.device, dtype=P.dtype)
+            Pp[:n] = P
+            Pv = Pp.view(sets, world, pd, r).transpose(0, 1).contiguous()  # [world, sets, pd, r]
+            if compressed:
+                mine = torch.empty((sets, pd, r), device=P.device, dtype=P.dtype)
+                dist.reduce_scatter_tensor(mine, Pv, op=dist.ReduceOp.AVG, group=pg)
+            else:
+                mine = Pv[rank].contiguous()
+            mine = orthogonalize(mine, float(group["oversample"]))
+            allp = torch.empty((world, sets, pd, r), device=P.device, dtype=P.dtype)
+            dist.all_gather_into_tensor(allp, mine.contiguous(), group=pg)
+            P = allp.transpose(0, 1).reshape(sets * world, pd, r)[:n].contiguous()
+        else:
+            P = orthogonalize(P, float(group["oversample"]))
+        R = self._power_r(Mb, P, t)
+        if compressed:
+            R = self._all_reduce_replicate([R])[0]
+        self._update(group, params, order, Mb, Qb, P, R, nz, t, None)
+
+    # ---- FSDP (outer-sharded) parameters
+    def _dion_sharded(self, group: dict, params: List[Tensor], cfg: DionParamConfig) -> None:
+        mesh = self._outer_shard_mesh
+        pg = mesh.get_group()
+        W = mesh.size()
+        n = len(params)
+        sets = (n + W - 1) // W
+        # rank-major slots: slot (j, s) holds matrix s*W + j, which rank j orthogonalises
+        order = [(i % W) * sets + (i // W) for i in range(n)]
+        Mb, Qb = self._arena(params, group, order, sets * W)
+        G = [to_local(p.grad) for p in params]
+        rm = self._replicate_mesh
+        compressed = self._replicate_mesh_grad_sync and cfg.compressed_all_reduce and rm is not None
+        if self._replicate_mesh_grad_sync and not cfg.compressed_all_reduce and rm is not None:
+            G = self._all_reduce_replicate(G)
+        nz_p = ops.dion_momentum_add_([Mb[o] for o in order], G)
+        nz = torch.zeros(sets * W, device=Mb.device, dtype=torch.float32)
+        nz[torch.tensor(order, device=Mb.device)] = nz_p
+        t = cfg.is_transposed
+        P_part = self._power_p(Mb, Qb, t)  # partial sums over this rank's shard
+        pd, r = P_part.shape[1:]
+        mine = torch.empty((sets, pd, r), device=Mb.device, dtype=torch.float32)
+        dist.reduce_scatter_tensor(mine, P_part.view(W, sets, pd, r), op=dist.ReduceOp.SUM, group=pg)
+        if compressed:
+            mine = self._all_reduce_replicate([mine])[0]
+        mine = orthogonalize(mine, float(group["oversample"]))
+        P_all = torch.empty((sets * W, pd, r), device=Mb.device, dtype=torch.float32)
+        dist.all_gather_into_tensor(P_all.view(W, sets, pd, r), mine.contiguous(), group=pg)
+        R = self._power_r(Mb, P_all, t)
+        if compressed:
+            R = self._all_reduce_replicate([R])[0]
+        sumsq = ops.col_sumsq(R)
+        dist.all_reduce(sumsq, op=dist.ReduceOp.SUM, group=pg)
+        self._update(group, params, order, Mb, Qb, P_all, R, nz, t, sumsq)
+
+    # ---- FSDP x TP (inner-sharded) parameters
+    def _dion_fsdp_tp(self, group: dict, params: List[Tensor], cfg: DionParamConfig) -> None:
+        """Inner-sharded update: P = M Q reduced over the outer mesh, orthogonalised
+        across the inner mesh with a distributed randomised Cholesky QR."""
+        from .linalg import distributed_orthogonalize
+
+        for p in params:
+            if not self.state[p]:
+                self._init_dion_states([p], group)
+        lr, mu = float(group["lr"]), float(group["mu"])
+        wd, eps = float(group["weight_decay"]), float(group["epsilon"])
+        rm = self._replicate_mesh
+        for p in params:
+            st = self.state[p]
+            G = p.grad
+            if self._replicate_mesh_grad_sync and not cfg.compressed_all_reduce and rm is not None:
+                G = DTensor.from_local(self._all_reduce_replicate([to_local(G)])[0], G.device_mesh, G.placements,
+                                       run_check=False, shape=G.shape, stride=G.stride())
+            M = st["momentum"]
+            M.add_(G.to(M.dtype))
+            Qd = st["Q"]
+            if cfg.Q_inner_unsharded_placements is not None:
+                Qd = Qd.redistribute(placements=cfg.Q_inner_unsharded_placements)
+            Mt = M.mT if cfg.is_transposed else M
+            P = (Mt @ Qd.to(M.dtype)).redistribute(
+                placements=[Replicate() if pl.is_partial() else pl for pl in (Mt @ Qd.to(M.dtype)).placements]
+            )
+            P = distributed_orthogonalize(P.unsqueeze(0) if P.ndim == 2 else P, float(group["oversample"]),
+                                          cfg.inner_shard_mesh_dim).squeeze(0)
+            R = Mt.mT @ P
+            R = R.redistribute(placements=[Replicate() if pl.is_partial() else pl for pl in R.placements])
+            Pl, Rl = to_local(P).float().unsqueeze(0), to_local(R).float().unsqueeze(0).contiguous()
+            Pl = Pl.contiguous()
+            nz = torch.tensor([float(bool((to_local(M) != 0).any()))], device=Pl.device)
+            Q0 = to_local(Qd).float().unsqueeze(0).contiguous()
+            ops.dion_fixup_(Pl, Rl, Q0, nz)
+            Ml = to_local(M)
+            upd = (Pl[0] @ Rl[0].mT)
+            Ml.add_((upd.mT if cfg.is_transposed else upd).to(Ml.dtype), alpha=-(1.0 - mu))
+            sumsq = ops.col_sumsq(Rl)
+            if cfg.outer_shard_mesh_dim is not None:
+                dist.all_reduce(sumsq, group=R.device_mesh.get_group(cfg.outer_shard_mesh_dim))
+            Qn = torch.empty_like(Rl)
+            ops.col_normalize(Rl, sumsq, eps, Qn)
+            s_lr = self._scaled_lr(p.shape, lr)
+            Xl = to_local(p)
+            u = Pl[0] @ Qn[0].mT
+            Xl.mul_(1.0 - lr * wd).add_((u.mT if cfg.is_transposed else u).to(Xl.dtype), alpha=-s_lr)
+            Qfull = DTensor.from_local(Qn[0].to(to_local(Qd).dtype), Qd.device_mesh, Qd.placements, run_check=False,
+                                       shape=Qd.shape, stride=Qd.stride())
+            to_local(st["Q"]).copy_(to_local(Qfull.redistribute(placements=cfg.Q_sharded_placements)))

@@ -67,3 +67,36 @@ def test_gemm_large_bf16():
     torch.cuda.synchronize()
     ops.check_status()
     assert _rel(out, _ref(A, B)) < 1e-2
+
+
+@pytest.mark.parametrize("a_t", [False, True])
+@pytest.mark.parametrize("b_t", [False, True])
+@pytest.mark.parametrize("shape", [(256, 512, 384), (200, 296, 72), (2, 1000, 1024, 520)])
+def test_gemm_tf32_layouts(a_t, b_t, shape):
+    torch.manual_seed(0)
+    if len(shape) == 3:
+        batch, (M, N, K) = 1, shape
+    else:
+        batch, M, N, K = shape
+    A = torch.randn(batch, K, M, device="cuda").transpose(1, 2) if a_t else torch.randn(batch, M, K, device="cuda")
+    B = torch.randn(batch, N, K, device="cuda").transpose(1, 2) if b_t else torch.randn(batch, K, N, device="cuda")
+    out = ops.matmul(A, B)
+    torch.cuda.synchronize()
+    ref = A.double() @ B.double()
+    # tf32 operands: ~1e-3 relative
+    assert _rel(out.double(), ref) < 2e-3
+
+
+def test_gemm_ptr_array_param_update():
+    """Per-batch output pointers + in-place param update D = g*D + d*(A@B)."""
+    from dion_b200.ops import _ext
+
+    torch.manual_seed(4)
+    A = torch.randn(3, 256, 64, device="cuda")
+    B = torch.randn(3, 64, 320, device="cuda")
+    Xs = [torch.randn(256, 320, device="cuda") for _ in range(3)]
+    ref = [0.9 * x - 0.1 * (a @ b) for x, a, b in zip(Xs, A.unbind(0), B.unbind(0))]
+    ops.matmul_update_(Xs, A, B, gamma=0.9, delta=-0.1)
+    torch.cuda.synchronize()
+    for x, r in zip(Xs, ref):
+        assert _rel(x, r) < 2e-3

@@ -1,0 +1,128 @@
+"""Optimizer unit tests on CPU (reference test strategy: single-step
+invariants, weight decay, rank fractions, convergence on a quadratic, state
+keys) plus one-step comparisons against the float64 oracle."""
+import math
+
+import pytest
+import torch
+
+from dion_b200 import ops
+from dion_b200.optim import Dion, Muon, oracle
+
+
+def _quad_loss_decreases(opt_factory, steps=60):
+    torch.manual_seed(0)
+    p = torch.nn.Parameter(torch.randn(32, 48) * 0.5)
+    opt = opt_factory([p])
+    first = None
+    for _ in range(steps):
+        opt.zero_grad()
+        loss = (p**2).sum()
+        loss.backward()
+        opt.step()
+        first = first if first is not None else loss.item()
+    return first, (p**2).sum().item()
+
+
+@pytest.mark.parametrize("cls,kw", [(Muon, dict(lr=0.02)), (Dion, dict(lr=0.02, rank_fraction=0.5))])
+def test_single_step_finite_and_changes(cls, kw):
+    torch.manual_seed(0)
+    p = torch.nn.Parameter(torch.randn(64, 32))
+    before = p.detach().clone()
+    opt = cls([p], **kw)
+    p.grad = torch.randn_like(p)
+    opt.step()
+    assert torch.isfinite(p).all()
+    assert not torch.equal(before, p.detach())
+
+
+@pytest.mark.parametrize("cls,kw", [(Muon, dict(lr=0.02, weight_decay=0.5)),
+                                    (Dion, dict(lr=0.02, weight_decay=0.5, rank_fraction=0.25))])
+def test_weight_decay_shrinks(cls, kw):
+    torch.manual_seed(0)
+    p = torch.nn.Parameter(torch.randn(32, 32))
+    n0 = p.norm().item()
+    opt = cls([p], **kw)
+    for _ in range(5):
+        p.grad = torch.zeros_like(p)
+        opt.step()
+    assert p.norm().item() < n0
+
+
+@pytest.mark.parametrize("rf", [0.1, 0.25, 0.5, 1.0])
+def test_dion_rank_fractions(rf):
+    torch.manual_seed(0)
+    p = torch.nn.Parameter(torch.randn(40, 24))
+    opt = Dion([p], lr=0.01, rank_fraction=rf)
+    p.grad = torch.randn_like(p)
+    opt.step()
+    st = opt.state[p]
+    r = min(int(math.ceil(rf * 24)), 24)
+    assert st["Q"].shape == (24, r)
+    assert set(st.keys()) == {"momentum", "Q"}
+    assert torch.isfinite(p).all()
+
+
+@pytest.mark.parametrize("cls,kw", [(Muon, dict(lr=0.05)), (Dion, dict(lr=0.05, rank_fraction=0.5))])
+def test_quadratic_convergence(cls, kw):
+    first, last = _quad_loss_decreases(lambda ps: cls(ps, **kw))
+    assert last < first
+
+
+def test_muon_matches_oracle():
+    torch.manual_seed(1)
+    for shape in [(48, 32), (24, 40)]:
+        X = torch.randn(shape)
+        G = torch.randn(shape)
+        p = torch.nn.Parameter(X.clone())
+        opt = Muon([p], lr=0.02, mu=0.9, weight_decay=0.1, nesterov=True, ns_coeffs="keller")
+        p.grad = G.clone()
+        opt.step()
+        Xr, Mr = oracle.muon_step(X, G, torch.zeros(shape), 0.02, 0.9, 0.1, True, ops.KELLER_NS_COEFFS)
+        # bf16 Newton-Schulz input vs float64 oracle
+        assert (p.detach().double() - Xr).norm() / (Xr - X.double()).norm() < 0.05
+        torch.testing.assert_close(opt.state[p]["momentum"].double(), Mr, rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("shape", [(48, 32), (32, 48), (40, 40)])
+def test_dion_matches_oracle(shape):
+    torch.manual_seed(2)
+    X = torch.randn(shape)
+    G = torch.randn(shape)
+    p = torch.nn.Parameter(X.clone())
+    opt = Dion([p], lr=0.02, mu=0.9, weight_decay=0.1, rank_fraction=0.5)
+    p.grad = G.clone()
+    # capture the initial Q the optimizer draws
+    opt._get_or_initialize_state(p, opt.param_groups[0])
+    Q0 = opt.state[p]["Q"].clone()
+    opt.step()
+    Xr, Mr, Qr = oracle.dion_step(X, G, torch.zeros(shape), Q0, 0.02, 0.9, 0.1)
+    torch.testing.assert_close(p.detach().double(), Xr, rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(opt.state[p]["momentum"].double(), Mr, rtol=1e-4, atol=1e-4)
+    # Q columns agree up to sign
+    Qn = opt.state[p]["Q"].double()
+    torch.testing.assert_close(Qn.abs(), Qr.abs(), rtol=1e-4, atol=1e-4)
+
+
+def test_dion_zero_gradient_guard():
+    p = torch.nn.Parameter(torch.randn(16, 8))
+    opt = Dion([p], lr=0.01, weight_decay=0.0, rank_fraction=0.5)
+    p.grad = torch.zeros_like(p)
+    before = p.detach().clone()
+    opt.step()
+    assert torch.isfinite(p).all()
+    torch.testing.assert_close(p.detach(), before)
+
+
+def test_scalar_algorithms_route():
+    torch.manual_seed(0)
+    w = torch.nn.Parameter(torch.randn(16, 16))
+    b = torch.nn.Parameter(torch.randn(16))
+    e = torch.nn.Parameter(torch.randn(10, 16))
+    opt = Dion([{"params": [w]}, {"params": [b], "algorithm": "adamw"}, {"params": [e], "algorithm": "lion"}],
+               lr=0.01, rank_fraction=0.5)
+    for t in (w, b, e):
+        t.grad = torch.randn_like(t)
+    opt.step()
+    assert set(opt.state[b].keys()) == {"momentum", "variance"}
+    assert set(opt.state[e].keys()) == {"momentum"}

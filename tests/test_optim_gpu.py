@@ -1,0 +1,52 @@
+"""Muon and Dion on CUDA (tcgen05 kernels) vs the float64 oracle."""
+import pytest
+import torch
+
+from dion_b200 import ops
+from dion_b200.optim import Dion, Muon, oracle
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("shape", [(256, 128), (128, 384), (200, 96)])
+def test_muon_cuda_vs_oracle(shape):
+    torch.manual_seed(1)
+    X = torch.randn(shape, device="cuda")
+    G = torch.randn(shape, device="cuda")
+    ps = [torch.nn.Parameter(X.clone()) for _ in range(3)]
+    opt = Muon(ps, lr=0.02, mu=0.9, weight_decay=0.1, ns_coeffs="keller")
+    for p in ps:
+        p.grad = G.clone()
+    opt.step()
+    torch.cuda.synchronize()
+    ops.check_status()
+    Xr, Mr = oracle.muon_step(X.cpu(), G.cpu(), torch.zeros(shape), 0.02, 0.9, 0.1, False, ops.KELLER_NS_COEFFS)
+    for p in ps:
+        rel = (p.detach().cpu().double() - Xr).norm() / (Xr - X.cpu().double()).norm()
+        assert rel < 0.05, rel
+
+
+@pytest.mark.parametrize("shape", [(512, 256), (256, 768), (384, 384)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_dion_cuda_vs_oracle(shape, dtype):
+    torch.manual_seed(2)
+    X = torch.randn(shape, device="cuda")
+    G = torch.randn(shape, device="cuda")
+    ps = [torch.nn.Parameter(X.clone().to(dtype)) for _ in range(2)]
+    opt = Dion(ps, lr=0.02, mu=0.9, weight_decay=0.1, rank_fraction=0.25)
+    for p in ps:
+        p.grad = G.clone().to(dtype)
+    for p in ps:
+        opt._get_or_initialize_state(p, opt.param_groups[0])
+    Q0 = [opt.state[p]["Q"].detach().clone() for p in ps]
+    opt.step()
+    torch.cuda.synchronize()
+    ops.check_status()
+    tol = 2e-2 if dtype == torch.float32 else 6e-2
+    for p, q0 in zip(ps, Q0):
+        Xr, Mr, Qr = oracle.dion_step(X.to(dtype).cpu(), G.to(dtype).cpu(), torch.zeros(shape), q0.cpu(),
+                                      0.02, 0.9, 0.1)
+        dx = (p.detach().cpu().double() - Xr).norm() / (Xr - X.to(dtype).cpu().double()).norm()
+        assert dx < tol, dx
+        dm = (opt.state[p]["momentum"].cpu().double() - Mr).norm() / Mr.norm()
+        assert dm < tol, dm
