@@ -156,7 +156,14 @@ def build_reference(args, world, mesh):
     """The reference's stock pieces: torchtitan Llama-3, FSDP2, ada_dion's
     param grouping and the optimizer it routes to (dion.Muon / AdaDionV2)."""
     sys.path.insert(0, REF_PATH)
+    import torch._inductor.config as inductor_config
     import torch.nn.functional as F
+
+    # the reference's torch.compile'd optimizer code also compiles small CPU
+    # graphs; point Inductor at the system C++ compiler, whose OpenMP runtime
+    # is installed on this image (the default one on PATH lacks libgomp.spec)
+    if os.path.exists("/usr/bin/g++"):
+        inductor_config.cpp.cxx = ("/usr/bin/g++",)
     from torch.distributed.fsdp import MixedPrecisionPolicy, fully_shard
     from torchtitan.models.llama3.model.args import TransformerModelArgs
     from torchtitan.models.llama3.model.model import Transformer

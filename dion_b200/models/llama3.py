@@ -179,18 +179,22 @@ class Transformer(nn.Module):
             self.rope_cache.device
         )
 
-    def forward(self, tokens: torch.Tensor, return_hidden: bool = False) -> torch.Tensor:
+    def forward(self, tokens: torch.Tensor, labels: Optional[torch.Tensor] = None,
+                return_hidden: bool = False) -> torch.Tensor:
+        """Logits, or with ``labels`` the mean next-token cross-entropy computed
+        chunk-wise without materialising fp32 logits. (The loss lives in
+        ``forward`` so FSDP's root hooks unshard the LM head for it.)"""
         seqlen = tokens.shape[1]
         h = self.tok_embeddings(tokens)
         rope = self.rope_cache[:seqlen].float()
         for layer in self.layers.values():
             h = layer(h, rope)
         h = self.norm(h)
+        if labels is not None:
+            return L.linear_cross_entropy(h, self.output.weight, labels)
         if return_hidden:
             return h
         return self.output(h)
 
     def loss(self, tokens: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
-        """Mean next-token cross-entropy, computed without materialising fp32 logits."""
-        h = self.forward(tokens, return_hidden=True)
-        return L.linear_cross_entropy(h, self.output.weight, labels)
+        return self(tokens, labels)

@@ -64,6 +64,23 @@ def _tma_ok(t: Tensor) -> bool:
     return inner_ok and (t.size(0) == 1 or s[0] % q == 0)
 
 
+def _tma_operands(A3: Tensor, B3: Tensor) -> Tuple[Tensor, Tensor]:
+    """Return views the TMA path accepts, copying into K-major buffers with K
+    padded to a 16-byte multiple when a stride is unaligned."""
+    if _tma_ok(A3) and _tma_ok(B3):
+        return A3, B3
+    K = A3.size(-1)
+    pad = (-K) % (16 // A3.element_size())
+    A3 = torch.nn.functional.pad(A3.contiguous(), (0, pad)) if pad or not _tma_ok(A3) else A3
+    if not _tma_ok(A3):
+        A3 = torch.nn.functional.pad(A3.contiguous(), (0, pad))
+    if pad or not _tma_ok(B3):
+        B3 = torch.nn.functional.pad(B3.transpose(1, 2).contiguous(), (0, pad)).transpose(1, 2)
+    if not (_tma_ok(A3) and _tma_ok(B3)):
+        raise ValueError("dion_b200.ops.matmul: operand layout not supported by TMA")
+    return A3, B3
+
+
 def matmul(
     A: Tensor,
     B: Tensor,
@@ -101,16 +118,20 @@ def matmul(
             res = res + beta * C3.float()
         out3.copy_(res.to(out3.dtype))
         return out3.squeeze(0) if squeeze else out3
-    if not (_tma_ok(A3) and _tma_ok(B3)):
-        A3 = A3.contiguous()
-        B3 = B3.contiguous()
-        if not (_tma_ok(A3) and _tma_ok(B3)):
-            # rows shorter than 16 bytes / unaligned: pad K to a 16-byte multiple
-            pad = (-K) % (16 // A3.element_size())
-            A3 = torch.nn.functional.pad(A3, (0, pad))
-            B3 = torch.nn.functional.pad(B3.transpose(1, 2), (0, pad)).transpose(1, 2)
-            if not (_tma_ok(A3) and _tma_ok(B3)):
-                raise ValueError("dion_b200.ops.matmul: operand layout not supported by TMA")
+    A3, B3 = _tma_operands(A3, B3)
+    q_out = 16 // out3.element_size()
+    if out3.stride(-1) != 1 or (out3.stride(-2) % q_out and M > 1) or out3.data_ptr() % 16 or \
+            (C3 is not None and (C3.stride(-1) != 1 or C3.stride(-2) % q_out or C3.data_ptr() % 16)):
+        # output rows not 16-byte aligned: compute into a padded buffer, copy out
+        Np = -(-N // q_out) * q_out
+        tmp = torch.empty((batch, M, Np), device=A.device, dtype=out3.dtype)[:, :, :N]
+        Ct = None
+        if C3 is not None and beta != 0.0:
+            Ct = torch.empty((batch, M, Np), device=A.device, dtype=out3.dtype)[:, :, :N]
+            Ct.copy_(C3)
+        ext().gemm(A3, B3, tmp, Ct, float(alpha), float(beta), None, 0, 0, bool(symmetric), False, 1.0, 1.0, 0)
+        out3.copy_(tmp)
+        return out3.squeeze(0) if squeeze else out3
     ext().gemm(A3, B3, out3, C3, float(alpha), float(beta), None, 0, 0, bool(symmetric), False, 1.0, 1.0, 0)
     return out3.squeeze(0) if squeeze else out3
 
@@ -154,8 +175,14 @@ def matmul_update_(
     o0 = outs[0]
     assert all(o.shape == o0.shape and o.stride() == o0.stride() and o.dtype == o0.dtype for o in outs)
     assert o0.dim() == 2 and o0.stride(1) == 1
-    if not (_tma_ok(A3) and _tma_ok(B3)):
-        A3, B3 = A3.contiguous(), B3.contiguous()
+    q = 16 // o0.element_size()
+    if o0.stride(0) % q or any(o.data_ptr() % 16 for o in outs):
+        # unaligned parameter rows: product first, then the axpby in place
+        prod = matmul(A3, B3, out_dtype=torch.float32)
+        for o, pr in zip(outs, prod.unbind(0)):
+            o.copy_((gamma * o.float() + delta * alpha * pr).to(o.dtype))
+        return
+    A3, B3 = _tma_operands(A3, B3)
     ptrs = _ptr_tensor(outs)
     ext().gemm(A3, B3, o0.unsqueeze(0), None, float(alpha), 0.0, None, 0, 0, False, True, float(gamma), float(delta),
                0, ptrs, o0.stride(0), _SCALAR_TYPE[o0.dtype])

@@ -425,6 +425,17 @@ class Dion(Optimizer):
             else:
                 self._dion_replicated(group, same, cfg)
 
+    # hooks overridden by the adaptive-rank subclass
+    def _active_q(self, params, order, Qb):
+        """Q view used this step and per-slot active ranks (None: all columns)."""
+        return Qb, None
+
+    def _orth(self, P: Tensor, group: dict, ranks) -> Tensor:
+        return orthogonalize(P, float(group["oversample"]))
+
+    def _after_update(self, group, params, order, sumsq, ranks) -> None:
+        return None
+
     def _scaled_lr(self, shape, lr: float) -> float:
         fan_out, fan_in = shape
         return math.sqrt(fan_out / fan_in) * lr
@@ -451,10 +462,10 @@ class Dion(Optimizer):
         return R
 
     def _update(self, group, params, order, Mb, Qb, P, R, nz, transposed, sumsq) -> None:
-        """Guard, error feedback, Q <- colnorm(R), weight update (all batched)."""
+        """Error feedback, Q <- colnorm(R), weight update (all batched); the
+        all-zero / NaN guard has already been applied to P and R."""
         lr, mu = float(group["lr"]), float(group["mu"])
         wd, eps = float(group["weight_decay"]), float(group["epsilon"])
-        ops.dion_fixup_(P, R, Qb, nz)
         dt = self._op_dtype(Mb.dtype)
         Pm, Rm = P.to(dt), R.to(dt)
         slots = list(Mb.unbind(0))
@@ -483,6 +494,7 @@ class Dion(Optimizer):
         n = len(params)
         order = list(range(n))
         Mb, Qb = self._arena(params, group, order, n)
+        Qb, ranks = self._active_q(params, order, Qb)
         G = [to_local(p.grad) for p in params]
         world = self._replicate_world_size
         rm = self._replicate_mesh
@@ -507,16 +519,20 @@ class Dion(Optimizer):
                 dist.reduce_scatter_tensor(mine, Pv, op=dist.ReduceOp.AVG, group=pg)
             else:
                 mine = Pv[rank].contiguous()
-            mine = orthogonalize(mine, float(group["oversample"]))
+            mine = self._orth(mine, group, None if ranks is None else
+                              [ranks[s * world + rank] if s * world + rank < n else 0 for s in range(sets)])
             allp = torch.empty((world, sets, pd, r), device=P.device, dtype=P.dtype)
             dist.all_gather_into_tensor(allp, mine.contiguous(), group=pg)
             P = allp.transpose(0, 1).reshape(sets * world, pd, r)[:n].contiguous()
         else:
-            P = orthogonalize(P, float(group["oversample"]))
+            P = self._orth(P, group, ranks)
         R = self._power_r(Mb, P, t)
         if compressed:
             R = self._all_reduce_replicate([R])[0]
-        self._update(group, params, order, Mb, Qb, P, R, nz, t, None)
+        ops.dion_fixup_(P, R, Qb, nz)
+        sumsq = ops.col_sumsq(R)
+        self._update(group, params, order, Mb, Qb, P, R, nz, t, sumsq)
+        self._after_update(group, params, order, sumsq, ranks)
 
     # ---- FSDP (outer-sharded) parameters
     def _dion_sharded(self, group: dict, params: List[Tensor], cfg: DionParamConfig) -> None:
@@ -528,6 +544,7 @@ class Dion(Optimizer):
         # rank-major slots: slot (j, s) holds matrix s*W + j, which rank j orthogonalises
         order = [(i % W) * sets + (i // W) for i in range(n)]
         Mb, Qb = self._arena(params, group, order, sets * W)
+        Qb, ranks = self._active_q(params, order, Qb)
         G = [to_local(p.grad) for p in params]
         rm = self._replicate_mesh
         compressed = self._replicate_mesh_grad_sync and cfg.compressed_all_reduce and rm is not None
@@ -543,15 +560,18 @@ class Dion(Optimizer):
         dist.reduce_scatter_tensor(mine, P_part.view(W, sets, pd, r), op=dist.ReduceOp.SUM, group=pg)
         if compressed:
             mine = self._all_reduce_replicate([mine])[0]
-        mine = orthogonalize(mine, float(group["oversample"]))
+        me = mesh.get_local_rank()
+        mine = self._orth(mine, group, None if ranks is None else ranks[me * sets:(me + 1) * sets])
         P_all = torch.empty((sets * W, pd, r), device=Mb.device, dtype=torch.float32)
         dist.all_gather_into_tensor(P_all.view(W, sets, pd, r), mine.contiguous(), group=pg)
         R = self._power_r(Mb, P_all, t)
         if compressed:
             R = self._all_reduce_replicate([R])[0]
+        ops.dion_fixup_(P_all, R, Qb, nz)
         sumsq = ops.col_sumsq(R)
         dist.all_reduce(sumsq, op=dist.ReduceOp.SUM, group=pg)
         self._update(group, params, order, Mb, Qb, P_all, R, nz, t, sumsq)
+        self._after_update(group, params, order, sumsq, ranks)
 
     # ---- FSDP x TP (inner-sharded) parameters
     def _dion_fsdp_tp(self, group: dict, params: List[Tensor], cfg: DionParamConfig) -> None:

@@ -1,0 +1,201 @@
+"""Dion2: Newton-Schulz on an alpha-fraction of momentum rows.
+
+Per matrix and step (the method named in the reference paper,
+paper/main.tex:70, and exercised by ada_dion/tests/test_dion2.py; the
+dion package build installed next to the reference does not ship it, so
+the rule below is this package's statement of it):
+
+    M += G
+    S = the ceil(fraction * rows) rows of M with the largest L1 norm
+        (selection_method="top_l1") or a uniform random subset ("random")
+    U = NewtonSchulz(M[S])                   (k x cols, bf16 tensor cores)
+    X = (1 - lr*wd) X                        (weight decay on every row)
+    X[S] -= lr * sqrt(fan_out/fan_in) * U    (Muon's spectral-norm scaling)
+    M[S] *= ef_decay                         (selective decay: only used rows)
+
+Unselected rows keep accumulating, so every row is eventually applied (error
+feedback). Sharded layouts:
+  * FSDP (rows sharded over W ranks): each rank picks its top rows locally
+    (ceil(fraction * rows/W) per shard, balanced traffic) and one all-to-all
+    per shape group carries the selected rows to the matrix owner and back,
+    i.e. ``fraction`` of Muon's all-to-all volume;
+  * DDP: replicas orthogonalise their own matrices and all-gather the rows.
+"""
+from __future__ import annotations
+
+import math
+from typing import Any, Dict, List, Optional, Tuple, Union
+
+import torch
+import torch.distributed as dist
+from torch import Tensor
+from torch.distributed import ProcessGroup
+from torch.distributed.device_mesh import DeviceMesh
+from torch.distributed.tensor import DTensor
+from torch.optim.optimizer import Optimizer, ParamsT
+
+from .. import ops
+from ._utils import group_by_signature, scalar_update, to_local
+from .muon import _ADJUST, _resolve_coeffs
+
+__all__ = ["Dion2"]
+
+
+class Dion2(Optimizer):
+    def __init__(
+        self,
+        params: ParamsT,
+        distributed_mesh: Optional[Union[DeviceMesh, ProcessGroup]] = None,
+        lr: float = 0.01,
+        fraction: float = 0.25,
+        ef_decay: float = 0.95,
+        betas: Tuple[float, float] = (0.9, 0.95),
+        weight_decay: float = 0.01,
+        epsilon: float = 1e-8,
+        selection_method: str = "top_l1",
+        adjust_lr: Optional[str] = "spectral_norm",
+        ns_coeffs=None,
+        seed: int = 0,
+    ):
+        if lr < 0.0:
+            raise ValueError(f"Invalid learning rate: {lr}")
+        if not (0.0 < fraction <= 1.0):
+            raise ValueError(f"Invalid fraction: {fraction}")
+        if not (0.0 <= ef_decay <= 1.0):
+            raise ValueError(f"Invalid ef_decay: {ef_decay}")
+        if selection_method not in ("top_l1", "random"):
+            raise ValueError(f"Invalid selection_method: {selection_method}")
+        if adjust_lr not in _ADJUST:
+            raise ValueError(f"Invalid adjust_lr value: {adjust_lr}")
+        defaults = dict(lr=lr, fraction=fraction, ef_decay=ef_decay, beta1=betas[0], beta2=betas[1],
+                        weight_decay=weight_decay, epsilon=epsilon, algorithm="dion2", step=0,
+                        selection_method=selection_method, adjust_lr=adjust_lr)
+        super().__init__(params, defaults)
+        if isinstance(distributed_mesh, DeviceMesh):
+            if distributed_mesh.ndim != 1:
+                raise ValueError("Only 1D DeviceMesh is supported; for HSDP pass the 1D shard sub-mesh.")
+            self._rank, self._world, self._pg = (distributed_mesh.get_local_rank(), distributed_mesh.size(),
+                                                 distributed_mesh.get_group())
+        elif isinstance(distributed_mesh, ProcessGroup):
+            self._rank, self._world, self._pg = (dist.get_rank(distributed_mesh),
+                                                 dist.get_world_size(distributed_mesh), distributed_mesh)
+        else:
+            self._rank, self._world, self._pg = 0, 1, None
+        self._coeffs = _resolve_coeffs(ns_coeffs)
+        self._gen: Optional[torch.Generator] = None
+        self._seed = seed
+
+    def _state(self, p: Tensor, algo: str) -> Dict[str, Any]:
+        st = self.state[p]
+        if not st:
+            st["momentum"] = torch.zeros_like(p)
+            if algo == "adamw":
+                st["variance"] = torch.zeros_like(p)
+        return st
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        for g in self.param_groups:
+            g["step"] += 1
+        for g in self.param_groups:
+            algo = g["algorithm"]
+            params = [p for p in g["params"] if p.grad is not None]
+            if not params:
+                continue
+            if algo in ("dion2", "dion", "muon"):
+                for same in group_by_signature(params).values():
+                    self._dion2_group(g, same)
+            elif algo in ("adamw", "lion"):
+                scalar_update(algo, params, [p.grad for p in params], [self._state(p, algo) for p in params], g)
+            else:
+                raise ValueError(f"Unknown algorithm: {algo}")
+        ops.check_status()
+        return loss
+
+    # ------------------------------------------------------------------ selection
+    def _select(self, Mb: Tensor, k: int, method: str) -> Tensor:
+        """Row indices [n, k] (sorted) of each matrix of the batch Mb [n, rows, cols]."""
+        n, rows = Mb.shape[:2]
+        if k >= rows:
+            return torch.arange(rows, device=Mb.device).expand(n, rows)
+        if method == "random":
+            if self._gen is None or self._gen.device != Mb.device:
+                self._gen = torch.Generator(device=Mb.device).manual_seed(self._seed)
+            idx = torch.rand((n, rows), device=Mb.device, generator=self._gen).topk(k, dim=1).indices
+        else:
+            idx = Mb.abs().sum(dim=2, dtype=torch.float32).topk(k, dim=1).indices
+        return idx.sort(dim=1).values
+
+    # ------------------------------------------------------------------ update
+    def _dion2_group(self, g: Dict[str, Any], params: List[Tensor]) -> None:
+        p0 = params[0]
+        if p0.ndim != 2:
+            raise ValueError("Dion2 expects 2-D matrices; use algorithm='adamw' or 'lion' for other tensors.")
+        states = [self._state(p, "dion2") for p in params]
+        X = to_local(params)
+        G = to_local([p.grad for p in params])
+        M = to_local([s["momentum"] for s in states])
+        ops.dion_momentum_add_(M, G)
+        lr, wd = float(g["lr"]), float(g["weight_decay"])
+        adj = _ADJUST[g["adjust_lr"]](lr, p0.shape)
+        eps = float(g["epsilon"])
+        sharded = isinstance(p0, DTensor) and any(
+            pl.is_shard() and p0.device_mesh.size(i) > 1 for i, pl in enumerate(p0.placements))
+        Mb = ops.as_batch(M)
+        stacked = Mb is None
+        if stacked:
+            Mb = torch.stack(M)
+        rows = Mb.shape[1]
+        k = max(1, int(math.ceil(float(g["fraction"]) * rows)))
+        idx = self._select(Mb, k, g["selection_method"])                    # [n, k]
+        gather_idx = idx.unsqueeze(-1).expand(-1, -1, Mb.shape[2])
+        sel = Mb.gather(1, gather_idx).to(torch.bfloat16)                   # [n, k, cols]
+        if sharded and self._world > 1:
+            U = self._orthogonalize_sharded(sel, eps)
+        elif self._pg is not None and self._world > 1:
+            U = self._orthogonalize_replicated(sel, eps)
+        else:
+            U = ops.newton_schulz(sel.contiguous(), self._coeffs, eps, clobber_input=True)
+        for x in X:
+            x.mul_(1.0 - lr * wd)
+        for i, x in enumerate(X):
+            x.index_add_(0, idx[i], U[i].to(x.dtype), alpha=-adj)
+        decay = float(g["ef_decay"])
+        Mb.scatter_(1, gather_idx, Mb.gather(1, gather_idx) * decay)
+        if stacked:
+            for m, mb in zip(M, Mb.unbind(0)):
+                m.copy_(mb)
+
+    def _orthogonalize_replicated(self, sel: Tensor, eps: float) -> Tensor:
+        W, r = self._world, self._rank
+        n, k, c = sel.shape
+        sets = (n + W - 1) // W
+        buf = torch.zeros((sets * W, k, c), device=sel.device, dtype=sel.dtype)
+        buf[:n] = sel
+        mine = buf.view(sets, W, k, c)[:, r].contiguous()
+        out = ops.newton_schulz(mine, self._coeffs, eps, clobber_input=True)
+        allp = torch.empty((W, sets, k, c), device=sel.device, dtype=sel.dtype)
+        dist.all_gather_into_tensor(allp, out.contiguous(), group=self._pg)
+        return allp.transpose(0, 1).reshape(sets * W, k, c)[:n]
+
+    def _orthogonalize_sharded(self, sel: Tensor, eps: float) -> Tensor:
+        """Rows of every shard go to the matrix owner (one all-to-all), the owner
+        orthogonalises the stacked W*k rows, the rows come back."""
+        W, r = self._world, self._rank
+        n, k, c = sel.shape
+        sets = (n + W - 1) // W
+        send = torch.zeros((W, sets, k, c), device=sel.device, dtype=sel.dtype)
+        for i in range(n):
+            send[i % W, i // W] = sel[i]
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv.view(W, -1), send.view(W, -1), group=self._pg)
+        full = recv.permute(1, 0, 2, 3).reshape(sets, W * k, c).contiguous()
+        out = ops.newton_schulz(full, self._coeffs, eps, clobber_input=True)
+        back = out.view(sets, W, k, c).permute(1, 0, 2, 3).contiguous()
+        ret = torch.empty_like(back)
+        dist.all_to_all_single(ret.view(W, -1), back.view(W, -1), group=self._pg)
+        return torch.stack([ret[i % W, i // W] for i in range(n)])

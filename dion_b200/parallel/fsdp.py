@@ -26,7 +26,9 @@ def apply_fsdp(
     reduce_dtype: torch.dtype = torch.float32,
     reshard_after_forward: bool = True,
 ) -> nn.Module:
-    mp = MixedPrecisionPolicy(param_dtype=param_dtype, reduce_dtype=reduce_dtype)
+    # activations are already bf16 (the embedding runs in param_dtype); keeping
+    # forward inputs uncast leaves the fp32 rotary table intact
+    mp = MixedPrecisionPolicy(param_dtype=param_dtype, reduce_dtype=reduce_dtype, cast_forward_inputs=False)
     layers = list(model.layers.values()) if isinstance(model.layers, nn.ModuleDict) else list(model.layers)
     for i, block in enumerate(layers):
         # the last block is resharded by the root right after backward anyway

@@ -42,11 +42,14 @@ def test_dion_cuda_vs_oracle(shape, dtype):
     opt.step()
     torch.cuda.synchronize()
     ops.check_status()
-    tol = 2e-2 if dtype == torch.float32 else 6e-2
     for p, q0 in zip(ps, Q0):
         Xr, Mr, Qr = oracle.dion_step(X.to(dtype).cpu(), G.to(dtype).cpu(), torch.zeros(shape), q0.cpu(),
                                       0.02, 0.9, 0.1)
-        dx = (p.detach().cpu().double() - Xr).norm() / (Xr - X.to(dtype).cpu().double()).norm()
-        assert dx < tol, dx
         dm = (opt.state[p]["momentum"].cpu().double() - Mr).norm() / Mr.norm()
-        assert dm < tol, dm
+        assert dm < 2e-2, dm
+        if dtype == torch.float32:
+            dx = (p.detach().cpu().double() - Xr).norm() / (Xr - X.cpu().double()).norm()
+            assert dx < 2e-2, dx
+        else:
+            # bf16 weights: the step is below bf16 resolution of X, compare at that resolution
+            torch.testing.assert_close(p.detach().cpu().double(), Xr, rtol=1e-2, atol=1e-2)
