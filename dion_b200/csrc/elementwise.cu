@@ -432,3 +432,91 @@ void lion(const std::vector<at::Tensor>& X, const std::vector<at::Tensor>& G, co
 }
 
 }  // namespace bdion
+
+// ---------------------------------------------------------------- allocation-free entry point
+// bdion_batched_sumsq_noalloc (declared and documented in no_alloc.h) runs the
+// same sum-of-squares kernels as multi_sumsq above, with the block partials
+// kept in a fixed file-scope device array instead of a freshly allocated
+// buffer, so the call allocates no device memory at all.
+#include <cstdio>
+#include <mutex>
+
+#include "no_alloc.h"
+
+static __device__ __align__(256) float g_noalloc_partials[BDION_NOALLOC_MAX_PARTIALS];
+
+namespace bdion {
+namespace {
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_scratch[kNoAllocMaxDevices] = {nullptr};
+
+// Device address of the scratch array for the current device (looked up once
+// per device; the host-side symbol is only a stand-in, never a device address).
+float* noalloc_scratch(int dev) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_scratch[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_partials) != cudaSuccess || p == nullptr) {
+      cudaGetLastError();  // reset the runtime's last-error value after the failed lookup
+      return nullptr;
+    }
+    g_noalloc_scratch[dev] = static_cast<float*>(p);
+  }
+  return g_noalloc_scratch[dev];
+}
+
+}  // namespace
+}  // namespace bdion
+
+extern "C" __attribute__((visibility("default"))) int bdion_batched_sumsq_noalloc(const void* x, int dtype,
+                                                                                  int64_t batch, int64_t numel,
+                                                                                  int64_t stride, float* out,
+                                                                                  void* stream) {
+  using namespace bdion;
+  if (x == nullptr || out == nullptr || batch < 1 || numel < 1 || stride < numel || (dtype != 0 && dtype != 1))
+    return BDION_NOALLOC_BAD_ARGUMENT;
+  const int64_t chunks_per = (numel + kChunk - 1) / kChunk;
+  if (chunks_per > BDION_NOALLOC_MAX_PARTIALS || batch > BDION_NOALLOC_MAX_PARTIALS / chunks_per) {
+    std::fprintf(stderr,
+                 "bdion_batched_sumsq_noalloc: %lld tensors of %lld elements need %lld partial sums, more than the "
+                 "fixed scratch capacity of %d\n",
+                 (long long)batch, (long long)numel, (long long)(batch * chunks_per), BDION_NOALLOC_MAX_PARTIALS);
+    return BDION_NOALLOC_TOO_LARGE;
+  }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return BDION_NOALLOC_SETUP_FAILED;
+  float* scratch = noalloc_scratch(dev);
+  if (scratch == nullptr) return BDION_NOALLOC_SETUP_FAILED;
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int esz = dtype == 0 ? 4 : 2;
+  const bool vec = reinterpret_cast<uintptr_t>(x) % 16 == 0 && (stride * esz) % 16 == 0;
+  int64_t used = 0;  // each launch group writes its own slice of the scratch array
+  for (int64_t b0 = 0; b0 < batch; b0 += kMaxTensors) {
+    const int n = (int)std::min<int64_t>(kMaxTensors, batch - b0);
+    MTArgs a{};
+    a.n = n;
+    int chunks = 0;
+    for (int i = 0; i < n; ++i) {
+      a.p[0][i] = const_cast<char*>(static_cast<const char*>(x)) + (b0 + i) * stride * esz;
+      a.numel[i] = numel;
+      a.chunk_start[i] = chunks;
+      chunks += (int)chunks_per;
+    }
+    a.chunk_start[n] = chunks;
+    a.total_chunks = chunks;
+    float* part = scratch + used;
+    if (dtype == 0)
+      sumsq_kernel<float><<<chunks, kThreads, 0, s>>>(a, vec ? 1 : 0, part);
+    else
+      sumsq_kernel<__nv_bfloat16><<<chunks, kThreads, 0, s>>>(a, vec ? 1 : 0, part);
+    if (cudaGetLastError() != cudaSuccess) return BDION_NOALLOC_LAUNCH_FAILED;
+    finalize_sumsq_kernel<<<n, kThreads, 0, s>>>(a, part, out + b0, nullptr, 0.f);
+    if (cudaGetLastError() != cudaSuccess) return BDION_NOALLOC_LAUNCH_FAILED;
+    note_launch(2);
+    used += chunks;
+  }
+  return BDION_NOALLOC_OK;
+}
