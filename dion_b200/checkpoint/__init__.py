@@ -1,0 +1,89 @@
+"""Distributed checkpointing (torch.distributed.checkpoint, DCP).
+
+The optimizer state goes through the container's DCP-flattened
+``state_dict`` (keys ``state.<fqn>.<key>`` / ``param_groups.<fqn>.<hyper>``,
+as ada_dion/integration/hybrid_optimizer.py:288-307 produces), the model
+through ``get_model_state_dict``, so checkpoints reshard across world sizes
+like torchtitan's CheckpointManager (interval, optional model-only final
+save). Before every save, Dion-family optimizers with a replicate mesh
+average their state across replicas (``synchronize_for_checkpoint``), which
+the reference container never calls.
+"""
+from __future__ import annotations
+
+import os
+import re
+from typing import Any, Dict, Optional
+
+import torch
+import torch.distributed as dist
+import torch.distributed.checkpoint as dcp
+from torch.distributed.checkpoint.state_dict import StateDictOptions, get_model_state_dict, set_model_state_dict
+
+__all__ = ["CheckpointManager", "save", "load"]
+
+
+def _sync_for_checkpoint(optimizers) -> None:
+    for opt in getattr(optimizers, "optimizers", [optimizers]):
+        fn = getattr(opt, "synchronize_for_checkpoint", None)
+        if fn is not None:
+            fn()
+
+
+def save(folder: str, model, optimizers, step: int, model_only: bool = False) -> str:
+    path = os.path.join(folder, f"step-{step}")
+    _sync_for_checkpoint(optimizers)
+    sd: Dict[str, Any] = {"model": get_model_state_dict(model)}
+    if not model_only:
+        sd["optimizer"] = optimizers.state_dict()
+        sd["train_state"] = {"step": torch.tensor(step)}
+    dcp.save(sd, checkpoint_id=path)
+    return path
+
+
+def load(path: str, model, optimizers=None) -> int:
+    sd: Dict[str, Any] = {"model": get_model_state_dict(model)}
+    has_opt = optimizers is not None and os.path.exists(path)
+    if has_opt:
+        sd["optimizer"] = optimizers.state_dict()
+        sd["train_state"] = {"step": torch.tensor(0)}
+    try:
+        dcp.load(sd, checkpoint_id=path)
+    except Exception:
+        if not has_opt:
+            raise
+        sd = {"model": get_model_state_dict(model)}
+        dcp.load(sd, checkpoint_id=path)
+        has_opt = False
+    set_model_state_dict(model, sd["model"])
+    if has_opt:
+        optimizers.load_state_dict(sd["optimizer"])
+        return int(sd["train_state"]["step"])
+    return 0
+
+
+class CheckpointManager:
+    def __init__(self, folder: str, model, optimizers, interval: int = 1000, model_only_last: bool = True):
+        self.folder = folder
+        self.model = model
+        self.optimizers = optimizers
+        self.interval = interval
+        self.model_only_last = model_only_last
+
+    def latest(self) -> Optional[str]:
+        if not os.path.isdir(self.folder):
+            return None
+        steps = [int(m.group(1)) for d in os.listdir(self.folder) if (m := re.fullmatch(r"step-(\d+)", d))]
+        return os.path.join(self.folder, f"step-{max(steps)}") if steps else None
+
+    def maybe_load(self, trainer) -> None:
+        p = self.latest()
+        if p is not None:
+            trainer.step_idx = load(p, self.model, self.optimizers)
+
+    def maybe_save(self, trainer, step: int, final: bool = False) -> Optional[str]:
+        if final:
+            return save(self.folder, self.model, self.optimizers, step, model_only=self.model_only_last)
+        if self.interval > 0 and step % self.interval == 0:
+            return save(self.folder, self.model, self.optimizers, step)
+        return None

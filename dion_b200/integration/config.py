@@ -1,0 +1,181 @@
+"""Job configuration: a dataclass tree plus a ``--section.field value`` CLI.
+
+Section and field names follow the torchtitan-style config the reference
+registers (ada_dion/integration/config_registry.py:161-184 for training, lr
+scheduler and metrics; hybrid_optimizer.py:62-113 for the optimizer), so
+the reference's command lines carry over, e.g.
+
+    python -m dion_b200.train --config llama3_160m_dion --optimizer.lr 0.01 \\
+        --training.steps 500 --parallelism.data_parallel_shard_degree 4
+
+Booleans accept ``--section.use-x`` / ``--section.no-use-x`` as well as an
+explicit value.
+"""
+from __future__ import annotations
+
+import dataclasses
+from dataclasses import dataclass, field
+from typing import Any, Dict, List, Optional, Sequence
+
+from .hybrid_optimizer import HybridOptimizersContainer
+
+__all__ = [
+    "ModelConfig",
+    "TrainingConfig",
+    "LRSchedulerConfig",
+    "ParallelismConfig",
+    "CheckpointConfig",
+    "MetricsConfig",
+    "DataConfig",
+    "ValidatorConfig",
+    "ProfilingConfig",
+    "JobConfig",
+    "apply_overrides",
+]
+
+
+@dataclass
+class ModelConfig:
+    name: str = "llama3"
+    flavor: str = "160M"
+    overrides: Dict[str, Any] = field(default_factory=dict)
+    init: str = "normal"
+
+
+@dataclass
+class TrainingConfig:
+    local_batch_size: int = 8
+    seq_len: int = 2048
+    steps: int = 10000
+    dtype: str = "bfloat16"
+    max_norm: float = 1.0
+    seed: int = 0
+
+
+@dataclass
+class LRSchedulerConfig:
+    warmup_steps: int = 200
+    decay_type: str = "cosine"
+    min_lr_factor: float = 0.1
+
+
+@dataclass
+class ParallelismConfig:
+    data_parallel_replicate_degree: int = 1
+    data_parallel_shard_degree: int = -1
+    tensor_parallel_degree: int = 1
+    pipeline_parallel_degree: int = 1
+
+
+@dataclass
+class CheckpointConfig:
+    enable: bool = False
+    folder: str = "checkpoint"
+    interval: int = 1000
+    last_save_model_only: bool = True
+
+
+@dataclass
+class MetricsConfig:
+    log_freq: int = 10
+    enable_tensorboard: bool = False
+    enable_wandb: bool = False
+    save_jsonl: Optional[str] = None
+
+
+@dataclass
+class DataConfig:
+    dataset: str = "synthetic"
+    seed: int = 0
+
+
+@dataclass
+class ValidatorConfig:
+    enable: bool = False
+    freq: int = 100
+    steps: int = 20
+
+
+@dataclass
+class ProfilingConfig:
+    enable_profiling: bool = False
+    save_traces_folder: str = "profile_traces"
+    profile_freq: int = 100
+
+
+@dataclass
+class JobConfig:
+    model: ModelConfig = field(default_factory=ModelConfig)
+    optimizer: HybridOptimizersContainer.Config = field(default_factory=HybridOptimizersContainer.Config)
+    lr_scheduler: LRSchedulerConfig = field(default_factory=LRSchedulerConfig)
+    training: TrainingConfig = field(default_factory=TrainingConfig)
+    parallelism: ParallelismConfig = field(default_factory=ParallelismConfig)
+    checkpoint: CheckpointConfig = field(default_factory=CheckpointConfig)
+    metrics: MetricsConfig = field(default_factory=MetricsConfig)
+    dataloader: DataConfig = field(default_factory=DataConfig)
+    validator: ValidatorConfig = field(default_factory=ValidatorConfig)
+    profiling: ProfilingConfig = field(default_factory=ProfilingConfig)
+
+    def to_dict(self) -> Dict[str, Any]:
+        return dataclasses.asdict(self)
+
+
+def _coerce(cur: Any, text: str) -> Any:
+    if isinstance(cur, bool):
+        if text.lower() in ("1", "true", "yes", "on"):
+            return True
+        if text.lower() in ("0", "false", "no", "off"):
+            return False
+        raise ValueError(f"not a boolean: {text}")
+    if isinstance(cur, int) and not isinstance(cur, bool):
+        return int(text)
+    if isinstance(cur, float):
+        return float(text)
+    if cur is None:
+        for conv in (int, float):
+            try:
+                return conv(text)
+            except ValueError:
+                pass
+        return None if text.lower() == "none" else text
+    return text
+
+
+def apply_overrides(cfg: JobConfig, argv: Sequence[str]) -> List[str]:
+    """Apply ``--section.field value`` overrides in place; returns unknown args."""
+    rest: List[str] = []
+    i = 0
+    args = list(argv)
+    while i < len(args):
+        a = args[i]
+        if not a.startswith("--") or "." not in a:
+            rest.append(a)
+            i += 1
+            continue
+        key = a[2:]
+        val: Optional[str] = None
+        if "=" in key:
+            key, val = key.split("=", 1)
+        section, name = key.split(".", 1)
+        name = name.replace("-", "_")
+        sec = getattr(cfg, section, None)
+        if sec is None:
+            rest.append(a)
+            i += 1
+            continue
+        negate = False
+        if not hasattr(sec, name) and name.startswith("no_") and hasattr(sec, name[3:]):
+            name, negate = name[3:], True
+        if not hasattr(sec, name):
+            raise ValueError(f"unknown config field --{section}.{name}")
+        cur = getattr(sec, name)
+        if isinstance(cur, bool) and (val is None) and (i + 1 >= len(args) or args[i + 1].startswith("--")):
+            setattr(sec, name, not negate)
+            i += 1
+            continue
+        if val is None:
+            val = args[i + 1]
+            i += 1
+        setattr(sec, name, _coerce(cur, val) if not negate else not _coerce(cur, val))
+        i += 1
+    return rest

@@ -132,6 +132,13 @@ class HybridOptimizersContainer(Optimizer):
         from .. import optim
 
         name = cfg.name
+        if name == "AdamW":
+            # every group on the scalar rule; the matrix group takes the main lr / wd
+            for g in groups:
+                g.setdefault("lr", cfg.lr)
+                g.setdefault("weight_decay", cfg.weight_decay)
+                g.update(algorithm="adamw", beta1=cfg.scalar_beta1, beta2=cfg.scalar_beta2, epsilon=cfg.scalar_eps)
+            return optim.Muon(groups, distributed_mesh=shard_mesh, lr=cfg.lr, weight_decay=cfg.weight_decay)
         if name == "Muon":
             Muon = optim.Muon
             return Muon(groups, distributed_mesh=shard_mesh, lr=cfg.lr, mu=cfg.mu, weight_decay=cfg.weight_decay,
@@ -159,7 +166,7 @@ class HybridOptimizersContainer(Optimizer):
             return optim.SDion(groups, device_mesh=shard_mesh, lr=cfg.lr, mu=cfg.mu, init_rank=cfg.init_rank,
                          rank_min=cfg.rank_min, rank_max=cfg.rank_max, qbuf_max_cols=cfg.qbuf_max_cols,
                          weight_decay=cfg.weight_decay, **mode_kw)
-        raise ValueError(f"Unknown matrix optimizer: {name!r}. Supported: 'Muon', 'Dion', 'Dion2', 'AdaDion', 'AdaDionV2'")
+        raise ValueError(f"Unknown matrix optimizer: {name!r}. Supported: 'AdamW', 'Muon', 'Dion', 'Dion2', 'AdaDion', 'AdaDionV2'")
 
     def __iter__(self) -> Iterator[Optimizer]:
         return iter(self.optimizers)

@@ -118,6 +118,14 @@ class Trainer:
         self.data = SyntheticTokens(mcfg.vocab_size, cfg.seq_len, cfg.local_batch_size, cfg.seed, self.rank,
                                     self.world // max(1, cfg.tp))
 
+    @property
+    def last_grad_norm(self) -> float:
+        gn = getattr(self, "_grad_norm", None)
+        if gn is None:
+            return float("nan")
+        gn = gn.full_tensor() if hasattr(gn, "full_tensor") else gn
+        return float(gn)
+
     def _set_lr(self) -> None:
         c = self.cfg
         total = c.steps
@@ -138,7 +146,7 @@ class Trainer:
         self._set_lr()
         loss = self.forward_backward(tokens, labels)
         if self.cfg.max_norm and self.cfg.max_norm > 0:
-            torch.nn.utils.clip_grad_norm_(self.model.parameters(), self.cfg.max_norm, foreach=True)
+            self._grad_norm = torch.nn.utils.clip_grad_norm_(self.model.parameters(), self.cfg.max_norm, foreach=True)
         self.optimizers.step()
         self.optimizers.zero_grad(set_to_none=True)
         self.step_idx += 1

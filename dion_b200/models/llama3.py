@@ -83,7 +83,8 @@ LLAMA3_CONFIGS: Dict[str, Llama3Config] = {
     # reference paper model (ada_dion/integration/config_registry.py:60-89)
     "160M": Llama3Config(dim=768, n_layers=12, n_heads=12, n_kv_heads=4, vocab_size=128256, ffn_dim=2048,
                          rope_theta=500000.0, max_seq_len=8192),
-    "320M": Llama3Config(dim=1024, n_layers=16, n_heads=16, n_kv_heads=4, vocab_size=128256, ffn_dim=2816,
+    # reference 320M model: 18 layers, full multi-head attention (config_registry.py:109-140)
+    "320M": Llama3Config(dim=768, n_layers=18, n_heads=12, n_kv_heads=12, vocab_size=128256, ffn_dim=2048,
                          rope_theta=500000.0, max_seq_len=8192),
     "1B": Llama3Config(dim=2048, n_layers=16, n_heads=32, n_kv_heads=8, vocab_size=128256, ffn_dim=8192,
                        rope_theta=500000.0, max_seq_len=8192),

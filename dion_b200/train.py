@@ -1,0 +1,112 @@
+"""Training entry point.
+
+    python -m dion_b200.train --config llama3_160m_dion [--section.field value ...]
+    torchrun --nproc-per-node 8 --master-addr 127.0.0.1 -m dion_b200.train --config llama3_1b_muon
+
+Builds the model, FSDP2/HSDP mesh, hybrid optimizer and LR schedule from a
+registered :class:`~dion_b200.integration.config.JobConfig`, trains on
+synthetic uniform tokens, logs torchtitan-style lines (step, loss,
+grad_norm, memory, tps, tflops, mfu) and optionally writes JSONL metrics and
+DCP checkpoints.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import time
+from typing import List, Optional
+
+import torch
+import torch.distributed as dist
+
+from .integration.config import JobConfig, apply_overrides
+from .integration.config_registry import get_config
+from .integration.trainer import Trainer, TrainerConfig
+
+__all__ = ["trainer_config_from_job", "main"]
+
+# bf16 dense peak used for MFU (measured B200 figure is in the bench outputs)
+PEAK_FLOPS = {"bfloat16": 2.25e15}
+
+
+def trainer_config_from_job(job: JobConfig) -> TrainerConfig:
+    par = job.parallelism
+    return TrainerConfig(
+        model=job.model.flavor,
+        model_overrides=dict(job.model.overrides),
+        seq_len=job.training.seq_len,
+        local_batch_size=job.training.local_batch_size,
+        steps=job.training.steps,
+        warmup_steps=job.lr_scheduler.warmup_steps,
+        min_lr_factor=job.lr_scheduler.min_lr_factor,
+        max_norm=job.training.max_norm,
+        seed=job.training.seed if job.training.seed else job.dataloader.seed,
+        init_mode=job.model.init,
+        dp_replicate=par.data_parallel_replicate_degree,
+        dp_shard=par.data_parallel_shard_degree,
+        tp=par.tensor_parallel_degree,
+        optimizer=job.optimizer,
+        log_freq=job.metrics.log_freq,
+    )
+
+
+def main(argv: Optional[List[str]] = None) -> List[float]:
+    argv = list(sys.argv[1:] if argv is None else argv)
+    p = argparse.ArgumentParser(add_help=True)
+    p.add_argument("--config", required=True)
+    p.add_argument("--job.config_file", dest="unused", default=None)
+    known, rest = p.parse_known_args(argv)
+    job = get_config(known.config)
+    leftover = apply_overrides(job, rest)
+    if leftover:
+        raise SystemExit(f"unrecognised arguments: {leftover}")
+    tc = trainer_config_from_job(job)
+    tr = Trainer(tc)
+    from .benchmarks.metrics_collector import OptimizerMetricsCollector
+
+    collector = None
+    if job.metrics.save_jsonl and tr.rank == 0:
+        collector = OptimizerMetricsCollector(tr.optimizers, output_dir=job.metrics.save_jsonl)
+    ckpt = None
+    if job.checkpoint.enable:
+        from .checkpoint import CheckpointManager
+
+        ckpt = CheckpointManager(job.checkpoint.folder, tr.model, tr.optimizers, interval=job.checkpoint.interval,
+                                 model_only_last=job.checkpoint.last_save_model_only)
+        ckpt.maybe_load(tr)
+    flops_tok = tr.model_cfg.flops_per_token(tc.seq_len)
+    tokens_step = tc.local_batch_size * tc.seq_len
+    losses: List[float] = []
+    t_last = time.perf_counter()
+    for step in range(tr.step_idx, tc.steps):
+        t, l = tr.data.next()
+        loss = tr.train_step(t, l)
+        s = step + 1
+        if s % tc.log_freq == 0 or s == tc.steps:
+            v = float(loss.item())
+            losses.append(v)
+            torch.cuda.synchronize() if torch.cuda.is_available() else None
+            now = time.perf_counter()
+            dt = (now - t_last) / max(1, tc.log_freq)
+            t_last = now
+            tps = tokens_step / dt
+            tflops = flops_tok * tps / 1e12
+            mem = torch.cuda.max_memory_allocated() / 2**30 if torch.cuda.is_available() else 0.0
+            mfu = 100.0 * flops_tok * tps / PEAK_FLOPS["bfloat16"]
+            gn = tr.last_grad_norm
+            if tr.rank == 0:
+                print(f"step: {s:5d}  loss: {v:8.4f}  grad_norm: {gn:7.4f}  memory: {mem:5.2f}GiB  "
+                      f"tps: {tps:,.0f}  tflops: {tflops:,.2f}  mfu: {mfu:.2f}%", flush=True)
+            if collector is not None:
+                collector.collect(s, loss=v, grad_norm=gn, tps=tps)
+        if ckpt is not None:
+            ckpt.maybe_save(tr, s, final=(s == tc.steps))
+    if dist.is_initialized():
+        dist.barrier()
+    return losses
+
+
+if __name__ == "__main__":
+    main()

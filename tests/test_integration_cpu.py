@@ -1,0 +1,142 @@
+"""Integration layer on CPU: param grouping, hybrid container, config
+registry and CLI overrides, trainer steps, metrics JSONL and DCP checkpoint
+round trip (reference tests: test_param_grouper.py, test_hybrid_optimizer.py,
+test_adadion_e2e.py config/metrics sections)."""
+import json
+import math
+import os
+
+import pytest
+import torch
+import torch.nn as nn
+
+from dion_b200.integration.config import apply_overrides
+from dion_b200.integration.config_registry import REGISTRY, get_config
+from dion_b200.integration.hybrid_optimizer import HybridOptimizersContainer, build_param_groups
+from dion_b200.integration.param_grouper import count_params, group_params_for_hybrid
+from dion_b200.models.llama3 import Transformer, llama3_config
+
+
+class _MockLlama(nn.Module):
+    def __init__(self, d=16, n_layers=2, vocab=64):
+        super().__init__()
+        self.tok_embeddings = nn.Embedding(vocab, d)
+        self.layers = nn.ModuleDict()
+        for i in range(n_layers):
+            blk = nn.Module()
+            blk.attention = nn.Module()
+            for n in ("wq", "wk", "wv", "wo"):
+                setattr(blk.attention, n, nn.Linear(d, d, bias=False))
+            blk.feed_forward = nn.Module()
+            for n in ("w1", "w2", "w3"):
+                setattr(blk.feed_forward, n, nn.Linear(d, d, bias=False))
+            blk.attention_norm = nn.LayerNorm(d)
+            blk.ffn_norm = nn.LayerNorm(d)
+            self.layers[str(i)] = blk
+        self.norm = nn.LayerNorm(d)
+        self.output = nn.Linear(d, vocab, bias=False)
+
+
+def test_grouper_counts_and_disjoint():
+    m = _MockLlama()
+    g = group_params_for_hybrid(m)
+    assert len(g.matrix_params) == 2 * 7
+    assert len(g.embed_params) == 1 and len(g.output_params) == 1
+    ids = [id(p) for grp in g for p in grp]
+    assert len(ids) == len(set(ids)) == len(list(m.parameters()))
+    c = count_params(g)
+    assert c["total"] == sum(p.numel() for p in m.parameters())
+
+
+def test_grouper_hf_and_gpt_names():
+    class HF(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.embed_tokens = nn.Embedding(10, 8)
+            self.q_proj_holder = nn.Module()
+            self.self_attn = nn.Module()
+            self.self_attn.q_proj = nn.Linear(8, 8)
+            self.mlp = nn.Module()
+            self.mlp.c_fc = nn.Linear(8, 8)
+            self.lm_head = nn.Linear(8, 10)
+
+    g = group_params_for_hybrid(HF())
+    assert len(g.embed_params) == 1 and len(g.output_params) == 2  # lm_head weight + bias
+    assert len(g.matrix_params) == 2  # q_proj.weight, c_fc.weight
+    assert len(g.norm_params) == 2  # biases
+
+
+@pytest.mark.parametrize("name", ["Muon", "Dion", "Dion2", "AdaDion", "AdaDionV2", "AdamW"])
+def test_container_steps_each_optimizer(name):
+    torch.manual_seed(0)
+    m = _MockLlama()
+    cfg = HybridOptimizersContainer.Config(name=name, lr=0.01, rank_fraction=0.5, init_rank=4, rank_min=2,
+                                           rank_max=8)
+    c = HybridOptimizersContainer(cfg, model_parts=[m])
+    assert len(c) == 1 and len(list(iter(c))) == 1
+    before = [p.detach().clone() for p in m.parameters()]
+    x = torch.randint(0, 64, (3,))
+    out = m.output(m.layers["0"].attention.wq(m.tok_embeddings(x)))
+    (out.sum() + sum(p.sum() for p in m.parameters())).backward()
+    c.step()
+    c.zero_grad()
+    changed = sum(not torch.equal(a, b.detach()) for a, b in zip(before, m.parameters()))
+    assert changed == len(before)
+    groups = c.get_optimizers()[0].param_groups
+    out_group = [g for g in groups if any(p is m.output.weight for p in g["params"])][0]
+    if name != "AdamW":
+        assert math.isclose(out_group["lr"], cfg.scalar_lr / math.sqrt(16))
+    norm_group = [g for g in groups if any(p is m.norm.weight for p in g["params"])][0]
+    assert norm_group["weight_decay"] == 0.0
+
+
+def test_registry_names_and_fields():
+    for n in ["llama3_160m_adamw", "llama3_160m_muon", "llama3_160m_dion", "llama3_160m_dion2",
+              "llama3_160m_adadion", "llama3_320m_muon", "llama3_debug_muon", "llama3_debug_dion",
+              "llama3_320m_adadion_v2", "llama3_1b_muon", "llama3_8b_dion"]:
+        assert n in REGISTRY
+    c = get_config("llama3_160m_dion")
+    assert c.optimizer.name == "Dion" and c.optimizer.rank_fraction == 0.25
+    assert c.training.seq_len == 2048 and c.training.local_batch_size == 8 and c.training.max_norm == 1.0
+    assert c.lr_scheduler.warmup_steps == 200 and c.lr_scheduler.min_lr_factor == 0.1
+    assert get_config("llama3_320m_muon").lr_scheduler.warmup_steps == 610
+    assert get_config("llama3_debug_dion").checkpoint.interval == 10
+
+
+def test_cli_overrides():
+    c = get_config("llama3_160m_muon")
+    rest = apply_overrides(c, ["--optimizer.lr", "0.005", "--training.steps=50", "--parallelism.data_parallel_shard_degree",
+                               "4", "--optimizer.no-nesterov", "--checkpoint.enable", "--other"])
+    assert rest == ["--other"]
+    assert c.optimizer.lr == 0.005 and c.training.steps == 50
+    assert c.parallelism.data_parallel_shard_degree == 4
+    assert c.optimizer.nesterov is False and c.checkpoint.enable is True
+    with pytest.raises(ValueError):
+        apply_overrides(c, ["--optimizer.not_a_field", "1"])
+
+
+def test_train_entry_and_metrics(tmp_path):
+    from dion_b200 import train
+
+    out = tmp_path / "m"
+    losses = train.main(["--config", "llama3_debug_muon", "--training.steps", "4", "--metrics.log_freq", "2",
+                         "--training.seq_len", "32", "--training.local_batch_size", "2",
+                         "--metrics.save_jsonl", str(out)])
+    assert len(losses) == 2 and all(math.isfinite(v) for v in losses)
+    recs = [json.loads(l) for l in open(out / "optimizer_metrics.jsonl")]
+    assert [r["step"] for r in recs] == [2, 4] and recs[0]["opt_0/type"] == "Muon"
+
+
+def test_dcp_checkpoint_roundtrip(tmp_path):
+    from dion_b200 import train
+
+    ck = tmp_path / "ck"
+    args = ["--config", "llama3_debug_dion", "--training.seq_len", "32", "--training.local_batch_size", "2",
+            "--checkpoint.enable", "--checkpoint.folder", str(ck), "--checkpoint.interval", "2",
+            "--checkpoint.no-last_save_model_only"]
+    train.main(args + ["--training.steps", "2"])
+    assert (ck / "step-2").exists()
+    # resume: continues from step 2 to 4
+    losses = train.main(args + ["--training.steps", "4", "--metrics.log_freq", "1"])
+    assert len(losses) == 2
+    assert (ck / "step-4").exists()
