@@ -170,6 +170,7 @@ class Dion(Optimizer):
         )
         self._mixed_precision_config = mixed_precision_config or DionMixedPrecisionConfig()
         self._arenas: Dict[Tuple, Dict[str, Any]] = {}
+        self._q_init_calls = 0
 
     # ------------------------------------------------------------------ step
     @torch.no_grad()
@@ -321,6 +322,12 @@ class Dion(Optimizer):
         slots = slots or (max(order) + 1)
         local0 = to_local(p0)
         dev = local0.device
+        # Q draws come from a generator seeded by the process seed and the
+        # order of state creation: identical on every rank and independent of
+        # how much randomness earlier steps consumed (sketches, etc.)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed((torch.initial_seed() * 7919 + 104729 * self._q_init_calls) % (2**63 - 1))
+        self._q_init_calls += 1
         mom_arena = torch.zeros((slots,) + tuple(local0.shape), device=dev, dtype=m_dtype)
         if isinstance(p0, DTensor):
             self._q_placements(p0, cfg)
@@ -328,7 +335,7 @@ class Dion(Optimizer):
             for _ in params:
                 # the global Q is drawn identically on every rank (same RNG
                 # state), then each rank keeps its shard
-                f = torch.randn(q_shape, device=dev, dtype=q_dtype)
+                f = torch.randn(q_shape, device=dev, dtype=torch.float32, generator=gen).to(q_dtype)
                 qd = DTensor.from_local(f, p0.device_mesh, [Replicate()] * p0.device_mesh.ndim, run_check=False)
                 locals_.append(qd.redistribute(placements=cfg.Q_sharded_placements).to_local())
             q_arena = torch.zeros((slots,) + tuple(locals_[0].shape), device=dev, dtype=q_dtype)
@@ -337,7 +344,7 @@ class Dion(Optimizer):
         else:
             q_arena = torch.zeros((slots,) + q_shape, device=dev, dtype=q_dtype)
             for i in order:
-                q_arena[i].normal_()
+                q_arena[i].copy_(torch.randn(q_shape, device=dev, dtype=torch.float32, generator=gen))
                 self._replicate_broadcast(q_arena[i])
         self._bind_arena(params, order, mom_arena, q_arena, cfg, q_shape)
 
@@ -516,13 +523,13 @@ class Dion(Optimizer):
             Pv = Pp.view(sets, world, pd, r).transpose(0, 1).contiguous()  # [world, sets, pd, r]
             if compressed:
                 mine = torch.empty((sets, pd, r), device=P.device, dtype=P.dtype)
-                dist.reduce_scatter_tensor(mine, Pv, op=dist.ReduceOp.AVG, group=pg)
+                dist.reduce_scatter_tensor(mine, Pv.view(world * sets, pd, r), op=dist.ReduceOp.AVG, group=pg)
             else:
                 mine = Pv[rank].contiguous()
             mine = self._orth(mine, group, None if ranks is None else
                               [ranks[s * world + rank] if s * world + rank < n else 0 for s in range(sets)])
             allp = torch.empty((world, sets, pd, r), device=P.device, dtype=P.dtype)
-            dist.all_gather_into_tensor(allp, mine.contiguous(), group=pg)
+            dist.all_gather_into_tensor(allp.view(world * sets, pd, r), mine.contiguous(), group=pg)
             P = allp.transpose(0, 1).reshape(sets * world, pd, r)[:n].contiguous()
         else:
             P = self._orth(P, group, ranks)
@@ -557,13 +564,13 @@ class Dion(Optimizer):
         P_part = self._power_p(Mb, Qb, t)  # partial sums over this rank's shard
         pd, r = P_part.shape[1:]
         mine = torch.empty((sets, pd, r), device=Mb.device, dtype=torch.float32)
-        dist.reduce_scatter_tensor(mine, P_part.view(W, sets, pd, r), op=dist.ReduceOp.SUM, group=pg)
+        dist.reduce_scatter_tensor(mine, P_part, op=dist.ReduceOp.SUM, group=pg)
         if compressed:
             mine = self._all_reduce_replicate([mine])[0]
         me = mesh.get_local_rank()
         mine = self._orth(mine, group, None if ranks is None else ranks[me * sets:(me + 1) * sets])
         P_all = torch.empty((sets * W, pd, r), device=Mb.device, dtype=torch.float32)
-        dist.all_gather_into_tensor(P_all.view(W, sets, pd, r), mine.contiguous(), group=pg)
+        dist.all_gather_into_tensor(P_all, mine.contiguous(), group=pg)
         R = self._power_r(Mb, P_all, t)
         if compressed:
             R = self._all_reduce_replicate([R])[0]

@@ -179,7 +179,7 @@ class Dion2(Optimizer):
         mine = buf.view(sets, W, k, c)[:, r].contiguous()
         out = ops.newton_schulz(mine, self._coeffs, eps, clobber_input=True)
         allp = torch.empty((W, sets, k, c), device=sel.device, dtype=sel.dtype)
-        dist.all_gather_into_tensor(allp, out.contiguous(), group=self._pg)
+        dist.all_gather_into_tensor(allp.view(W * sets, k, c), out.contiguous(), group=self._pg)
         return allp.transpose(0, 1).reshape(sets * W, k, c)[:n]
 
     def _orthogonalize_sharded(self, sel: Tensor, eps: float) -> Tensor:

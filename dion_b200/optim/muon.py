@@ -284,7 +284,7 @@ class Muon(Optimizer):
         mine = U.view(sets, W, m, k)[:, r].contiguous()
         O_mine = self._ns(mine, full_scale.view(sets, W)[:, r].contiguous(), eps)
         gathered = torch.empty((W, sets, m, k), device=dev, dtype=torch.bfloat16)
-        dist.all_gather_into_tensor(gathered, O_mine.contiguous(), group=self._pg)
+        dist.all_gather_into_tensor(gathered.view(W * sets, m, k), O_mine.contiguous(), group=self._pg)
         O = gathered.transpose(0, 1).reshape(sets * W, m, k)[:n]
         ops.scaled_update_(X, [o.view(shape) for o in O.unbind(0)], decay, [adj_lr] * n)
 
