@@ -129,6 +129,101 @@ __global__ void rope_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bflo
   reinterpret_cast<__nv_bfloat162*>(dst)[p] = __floats2bfloat162_rn(f.x * c - f.y * s, f.x * s + f.y * c);
 }
 
+
+// Register-accumulating variant for D = NC * 256: each lane owns the columns
+// {lane*8 + c*256 + i}, keeps its share of the weight gradient in registers
+// across all rows of the block and writes one partial row at the end.
+template <typename WT, int NC>
+__global__ void __launch_bounds__(128) rms_bwd_reg_kernel(const __nv_bfloat16* __restrict__ gy,
+                                                          const __nv_bfloat16* __restrict__ x,
+                                                          const WT* __restrict__ w, const float* __restrict__ rstd,
+                                                          __nv_bfloat16* __restrict__ gx,
+                                                          float* __restrict__ gw_part, int R, int rows_per_block) {
+  constexpr int D = NC * 256;
+  extern __shared__ float red[];  // [4][D] partial weight gradients, one row per warp
+  const int wid = threadIdx.x / 32, lane = threadIdx.x % 32;
+  float acc[NC][8];
+  float wv[NC][8];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    load8(w + c * 256 + lane * 8, wv[c]);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[c][i] = 0.f;
+  }
+  const int r0 = blockIdx.x * rows_per_block;
+  const int r1 = min(R, r0 + rows_per_block);
+  for (int row = r0 + wid; row < r1; row += 4) {
+    const __nv_bfloat16* xr = x + (int64_t)row * D;
+    const __nv_bfloat16* gr = gy + (int64_t)row * D;
+    const float r = rstd[row];
+    float xv[NC][8], gv[NC][8];
+    float dot = 0.f;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      load8(xr + c * 256 + lane * 8, xv[c]);
+      load8(gr + c * 256 + lane * 8, gv[c]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        dot += gv[c][i] * wv[c][i] * xv[c][i];
+        acc[c][i] += gv[c][i] * xv[c][i] * r;
+      }
+    }
+    dot = warp_sum(dot);
+    const float k = r * r * r * dot / D;
+    __nv_bfloat16* gxr = gx + (int64_t)row * D;
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      float o[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = r * wv[c][i] * gv[c][i] - xv[c][i] * k;
+      store8(gxr + c * 256 + lane * 8, o);
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < NC; ++c)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) red[wid * D + c * 256 + lane * 8 + i] = acc[c][i];
+  __syncthreads();
+  for (int col = threadIdx.x; col < D; col += 128)
+    gw_part[(int64_t)blockIdx.x * D + col] = red[col] + red[D + col] + red[2 * D + col] + red[3 * D + col];
+}
+
+// RoPE over 8 consecutive elements (4 interleaved pairs) per thread; one
+// table row (cos, sin per pair) per position.
+__global__ void rope8_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
+                             const float2* __restrict__ tab, __nv_bfloat16* __restrict__ qo,
+                             __nv_bfloat16* __restrict__ ko, int64_t nq8, int64_t nk8, int S, int hq, int hk,
+                             int half, float sign) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const __nv_bfloat16* src;
+  __nv_bfloat16* dst;
+  int64_t v;
+  int h;
+  if (i < nq8) {
+    src = q; dst = qo; v = i; h = hq;
+  } else if (i < nq8 + nk8) {
+    src = k; dst = ko; v = i - nq8; h = hk;
+  } else {
+    return;
+  }
+  const int per_row = half / 4;              // 8-element groups per head row
+  const int64_t row = v / per_row;           // (b, s, head)
+  const int j0 = (int)(v - row * per_row) * 4;
+  const int pos = (int)((row / h) % S);
+  float x[8];
+  load8(src + v * 8, x);
+  const float2* t = tab + (int64_t)pos * half + j0;
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const float2 cs = t[p];
+    const float c = cs.x, s = sign * cs.y;
+    const float a = x[2 * p], b = x[2 * p + 1];
+    x[2 * p] = a * c - b * s;
+    x[2 * p + 1] = a * s + b * c;
+  }
+  store8(dst + v * 8, x);
+}
+
 // ------------------------------------------------------------ SwiGLU
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + __expf(-x)); }
 
@@ -274,6 +369,42 @@ void rms_norm_bwd(const at::Tensor& gy, const at::Tensor& x, const at::Tensor& w
   const int warps = 4;
   const size_t smem = (size_t)warps * D * sizeof(float);
   TORCH_CHECK(smem <= 200 * 1024, "dion_b200 rms_norm_bwd: D too large");
+  if (D % 256 == 0 && (D / 256 == 1 || D / 256 == 2 || D / 256 == 3 || D / 256 == 4 || D / 256 == 8 ||
+                       D / 256 == 16)) {
+    const int nblk_r = std::min((R + 3) / 4, sms * 4);
+    const int rpb = (R + nblk_r - 1) / nblk_r;
+    auto part_r = at::empty({nblk_r, D}, x.options().dtype(at::kFloat));
+    auto gyp = reinterpret_cast<const __nv_bfloat16*>(gy.data_ptr());
+    auto xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+    auto gxp = reinterpret_cast<__nv_bfloat16*>(gx.data_ptr());
+    auto launch = [&](auto tag_w, auto nc) {
+      using WT = decltype(tag_w);
+      constexpr int NC = decltype(nc)::value;
+      auto k = rms_bwd_reg_kernel<WT, NC>;
+      const int red_bytes = NC * 256 * 4 * (int)sizeof(float);
+      if (red_bytes > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, red_bytes);
+      k<<<nblk_r, 128, red_bytes, s>>>(gyp, xp, reinterpret_cast<const WT*>(w.data_ptr()), rstd.data_ptr<float>(), gxp,
+                               part_r.data_ptr<float>(), R, rpb);
+    };
+    auto by_nc = [&](auto tag_w) {
+      switch (D / 256) {
+        case 1: launch(tag_w, std::integral_constant<int, 1>{}); break;
+        case 2: launch(tag_w, std::integral_constant<int, 2>{}); break;
+        case 3: launch(tag_w, std::integral_constant<int, 3>{}); break;
+        case 4: launch(tag_w, std::integral_constant<int, 4>{}); break;
+        case 8: launch(tag_w, std::integral_constant<int, 8>{}); break;
+        default: launch(tag_w, std::integral_constant<int, 16>{}); break;
+      }
+    };
+    if (w.scalar_type() == at::kFloat)
+      by_nc(float{});
+    else
+      by_nc(__nv_bfloat16{});
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    note_launch();
+    at::sum_out(gw, part_r, 0);
+    return;
+  }
   const int nblk = std::min((R + warps - 1) / warps, sms * 2);
   const int rows_per_block = (R + nblk - 1) / nblk;
   auto part = at::empty({nblk, D}, x.options().dtype(at::kFloat));
@@ -301,6 +432,17 @@ void rope_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& tab, a
   TORCH_CHECK(q.dim() == 4 && q.is_contiguous() && k.is_contiguous(), "dion_b200 rope: [b,s,h,d] contiguous");
   c10::cuda::CUDAGuard guard(q.device());
   const int S = (int)q.size(1), hq = (int)q.size(2), hk = (int)k.size(2), d = (int)q.size(3);
+  if (d % 8 == 0) {
+    const int64_t nq8 = q.numel() / 8, nk8 = k.numel() / 8;
+    const int64_t grid8 = (nq8 + nk8 + 255) / 256;
+    rope8_kernel<<<(unsigned)grid8, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(k.data_ptr()),
+        reinterpret_cast<const float2*>(tab.data_ptr<float>()), reinterpret_cast<__nv_bfloat16*>(qo.data_ptr()),
+        reinterpret_cast<__nv_bfloat16*>(ko.data_ptr()), nq8, nk8, S, hq, hk, d / 2, inverse ? -1.f : 1.f);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    note_launch();
+    return;
+  }
   const int64_t nq = q.numel() / 2, nk = k.numel() / 2;
   const int threads = 256;
   const int64_t grid = (nq + nk + threads - 1) / threads;
