@@ -107,16 +107,43 @@ def bench_elementwise(small: bool):
     return out
 
 
+def bench_linalg(small: bool):
+    from ..optim import linalg as LA
+
+    out = []
+    b, m, r = (8, 1280, 1024) if not small else (4, 640, 512)
+    A = torch.randn(b, m, r, device="cuda")
+    ms = _time(lambda: LA.qr_r(A), warmup=1, iters=3)
+    ref = _time(lambda: torch.linalg.qr(A, mode="r"), warmup=1, iters=3)
+    out.append({"case": f"qr_r_{b}x{m}x{r}", "ms": ms, "ref_ms": ref})
+    G = A.mT @ A / m + torch.eye(r, device="cuda")
+    ms = _time(lambda: LA.cholesky_lower(G), warmup=1, iters=3)
+    ref = _time(lambda: torch.linalg.cholesky_ex(G), warmup=1, iters=3)
+    out.append({"case": f"cholesky_{b}x{r}", "ms": ms, "ref_ms": ref})
+    L = torch.linalg.cholesky(G)
+    ms = _time(lambda: LA.tri_inv_lower(L), warmup=1, iters=3)
+    eye = torch.eye(r, device="cuda").expand(b, r, r)
+    ref = _time(lambda: torch.linalg.solve_triangular(L, eye, upper=False), warmup=1, iters=3)
+    out.append({"case": f"tri_inv_{b}x{r}", "ms": ms, "ref_ms": ref})
+    P = torch.randn(b, 4 * r, r, device="cuda")
+    ms = _time(lambda: LA.orthogonalize(P), warmup=1, iters=3)
+    out.append({"case": f"orthogonalize_rcqr_{b}x{4 * r}x{r}", "ms": ms})
+    return out
+
+
 def main(argv=None):
     p = argparse.ArgumentParser()
     p.add_argument("--only", default="gemm,ns,elementwise")
     p.add_argument("--small", action="store_true")
     a = p.parse_args(argv)
     torch.manual_seed(0)
-    fns = {"gemm": bench_gemm, "ns": bench_ns, "elementwise": bench_elementwise}
+    fns = {"gemm": bench_gemm, "ns": bench_ns, "elementwise": bench_elementwise, "linalg": bench_linalg}
     for name in a.only.split(","):
-        for rec in fns[name](a.small):
-            print(json.dumps(rec), flush=True)
+        try:
+            for rec in fns[name](a.small):
+                print(json.dumps(rec), flush=True)
+        except Exception as e:  # keep going: one failing case must not hide the others
+            print(json.dumps({"case": name, "error": repr(e)[:300]}), flush=True)
 
 
 if __name__ == "__main__":

@@ -27,49 +27,68 @@ from torch.distributed.tensor import DTensor, Replicate, Shard
 
 from .. import ops
 
-__all__ = ["orthogonalize", "distributed_orthogonalize", "sketch_size", "tri_inv_upper", "cholesky_upper"]
+__all__ = ["orthogonalize", "distributed_orthogonalize", "sketch_size", "tri_inv_lower", "tri_inv_upper",
+           "cholesky_lower", "cholesky_upper", "qr_r"]
 
 
 def sketch_size(r: int, oversample: float) -> int:
     return int(math.ceil(oversample * r / 128.0) * 128)
 
 
+_MAX_KERNEL_DIM = 1600  # single-CTA kernels keep a 32-column panel of this many rows in shared memory
+
+
+def _use_kernels(t: Tensor, rows: int) -> bool:
+    return t.is_cuda and ops.has_ext() and rows <= _MAX_KERNEL_DIM
+
+
+def tri_inv_lower(S: Tensor, upper: bool = False) -> Tensor:
+    """Z = L^-1 (lower) for L = lower(S), or L = upper(S)^T when ``upper``."""
+    if _use_kernels(S, S.size(-1)):
+        Z = torch.empty(S.shape, device=S.device, dtype=S.dtype)
+        ops.ext().tri_inv_lower(S.contiguous(), Z, bool(upper))
+        return Z
+    L = S.mT if upper else S
+    eye = torch.eye(S.size(-1), device=S.device, dtype=S.dtype).expand_as(S)
+    return torch.linalg.solve_triangular(torch.tril(L), eye, upper=False)
+
+
 def tri_inv_upper(R: Tensor) -> Tensor:
-    """Inverse of a batch of upper-triangular matrices (fp32)."""
-    if R.is_cuda and ops.has_ext() and hasattr(ops.ext(), "tri_inv_upper"):
-        out = torch.empty_like(R)
-        ops.ext().tri_inv_upper(R.contiguous(), out)
-        return out
-    eye = torch.eye(R.size(-1), device=R.device, dtype=R.dtype).expand_as(R)
-    return torch.linalg.solve_triangular(R, eye, upper=True)
+    """Inverse of a batch of upper-triangular matrices."""
+    return tri_inv_lower(R, upper=True).mT
+
+
+def cholesky_lower(A: Tensor) -> Tensor:
+    """Lower Cholesky factor of a batch of SPD matrices; non-SPD matrices give
+    NaN entries that the Dion guard later discards (as cholesky_ex does)."""
+    if _use_kernels(A, A.size(-1)):
+        L = A.contiguous().clone()
+        info = torch.empty(A.size(0), dtype=torch.int32, device=A.device)
+        ops.ext().cholesky_lower(L, info)
+        return torch.tril(L)
+    L, _ = torch.linalg.cholesky_ex(A)
+    return L
 
 
 def cholesky_upper(A: Tensor) -> Tensor:
-    """Upper Cholesky factor of a batch of SPD matrices (fp32); non-SPD
-    entries give NaN/garbage that the Dion guard later zeroes."""
-    if A.is_cuda and ops.has_ext() and hasattr(ops.ext(), "cholesky_upper"):
-        out = torch.empty_like(A)
-        ops.ext().cholesky_upper(A.contiguous(), out)
-        return out
-    R, _ = torch.linalg.cholesky_ex(A, upper=True)
-    return R
+    return cholesky_lower(A).mT
 
 
 def qr_r(A: Tensor) -> Tensor:
-    """R factor of the QR decomposition of a batch of tall matrices (fp32)."""
-    if A.is_cuda and ops.has_ext() and hasattr(ops.ext(), "qr_r"):
-        out = torch.empty(A.size(0), A.size(-1), A.size(-1), device=A.device, dtype=A.dtype)
-        ops.ext().qr_r(A.contiguous(), out)
-        return out
+    """R factor (upper) of the Householder QR of a batch of tall matrices."""
+    if _use_kernels(A, A.size(-2)):
+        W = A.contiguous().clone()
+        R = torch.empty(A.size(0), A.size(-1), A.size(-1), device=A.device, dtype=A.dtype)
+        ops.ext().qr_r(W, R)
+        return R
     return torch.linalg.qr(A, mode="r")[1]
 
 
-def _right_solve(P: Tensor, R: Tensor) -> Tensor:
-    """P R^-1 for upper-triangular R: invert the r x r factor, then one GEMM."""
+def _apply_inv_lower_t(P: Tensor, Z: Tensor) -> Tensor:
+    """P Z^T (Z lower): the tensor-core GEMM reads Z's rows as a K-major operand."""
     if P.is_cuda:
-        Rinv = tri_inv_upper(R)
-        return ops.matmul(P, Rinv)
-    return torch.linalg.solve_triangular(R, P, upper=True, left=False)
+        return ops.matmul(P, Z.transpose(1, 2))
+    return P @ Z.mT
 
 
 def orthogonalize(P: Tensor, oversample: float = 1.25, generator: Optional[torch.Generator] = None) -> Tensor:
@@ -84,12 +103,27 @@ def orthogonalize(P: Tensor, oversample: float = 1.25, generator: Optional[torch
     S = torch.randn((b, k, d), device=P.device, dtype=torch.float32, generator=generator)
     S.mul_(math.sqrt(1.0 / k))
     SP = ops.matmul(S, Pf) if P.is_cuda else S @ Pf
+    if P.is_cuda:
+        # P <- P R1^-1 with R1 = qr(SP).R ; then CholeskyQR: P <- P chol(P^T P)^-T
+        R1 = qr_r(SP)
+        Pf = _apply_inv_lower_t(Pf, tri_inv_lower(R1, upper=True))
+        PP = ops.matmul(Pf.transpose(1, 2), Pf, symmetric=True)
+        L2 = cholesky_lower(PP)
+        Pf = _apply_inv_lower_t(Pf, tri_inv_lower(L2))
+        return Pf.to(dtype)
     R1 = qr_r(SP)
-    Pf = _right_solve(Pf, R1)
-    PP = ops.matmul(Pf.transpose(1, 2), Pf, symmetric=True) if P.is_cuda else Pf.mT @ Pf
+    Pf = torch.linalg.solve_triangular(R1, Pf, upper=True, left=False)
+    PP = Pf.mT @ Pf
     R2 = cholesky_upper(PP)
-    Pf = _right_solve(Pf, R2)
+    Pf = torch.linalg.solve_triangular(R2, Pf, upper=True, left=False)
     return Pf.to(dtype)
+
+
+def _right_solve(P: Tensor, R: Tensor) -> Tensor:
+    """P R^-1 for upper-triangular R."""
+    if P.is_cuda:
+        return _apply_inv_lower_t(P.contiguous(), tri_inv_lower(R.contiguous(), upper=True))
+    return torch.linalg.solve_triangular(R, P, upper=True, left=False)
 
 
 def distributed_orthogonalize(P: DTensor, oversample: float = 1.25, shard_mesh_dim: Optional[int] = None) -> DTensor:
@@ -126,7 +160,7 @@ def distributed_orthogonalize(P: DTensor, oversample: float = 1.25, shard_mesh_d
     PP_local = ops.matmul(P_local.transpose(1, 2), P_local, symmetric=True) if P_local.is_cuda else P_local.mT @ P_local
     PP = DTensor.from_local(PP_local, mesh, sp_pl, run_check=False)
     PP_single = PP.redistribute(placements=batch_sharded)
-    R2_local = cholesky_upper(PP_single.to_local().contiguous())
+    R2_local = cholesky_upper(PP_single.to_local().contiguous()).contiguous()
     R2 = DTensor.from_local(R2_local, mesh, PP_single.placements, run_check=False).redistribute(placements=full_rep)
     P_local = _right_solve(P_local, R2.to_local().contiguous())
     return DTensor.from_local(P_local.to(dtype).contiguous(), mesh, orig, run_check=False, shape=P.shape,
