@@ -1,6 +1,8 @@
 // Python bindings of the dion_b200 CUDA extension (module dion_b200._C).
 #include <torch/extension.h>
 
+#include <tuple>
+
 #include "host_utils.h"
 
 namespace bdion {
@@ -8,6 +10,20 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10::op
           double beta, const c10::optional<at::Tensor>& scale, int64_t alpha_pow, int64_t beta_pow, bool sym,
           bool param_mode, double gamma, double delta, int64_t bn_pref, const c10::optional<at::Tensor>& D_ptrs,
           int64_t ldd_ptrs, int64_t out_dtype_ptrs);
+void gemm_ex(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10::optional<at::Tensor>& C,
+             double alpha, double beta, const c10::optional<at::Tensor>& scale, int64_t alpha_pow, int64_t beta_pow,
+             bool sym, bool param_mode, double gamma, double delta, int64_t bn_pref,
+             const c10::optional<at::Tensor>& D_ptrs, int64_t ldd_ptrs, int64_t out_dtype_ptrs, int64_t nrep,
+             int64_t rows_per_ptr);
+std::tuple<int64_t, at::Tensor> symm_create(int64_t bytes);
+int64_t symm_open(const at::Tensor& handle);
+void symm_close(int64_t peer_ptr);
+void symm_free(int64_t ptr);
+at::Tensor symm_view(int64_t ptr, int64_t numel, int64_t dtype);
+void symm_barrier(const at::Tensor& peer_flags, int64_t my_flags, int64_t rank, int64_t world);
+void symm_reduce_slots(const at::Tensor& src, at::Tensor& dst, int64_t nslots);
+void symm_push(const at::Tensor& src, const at::Tensor& dsts);
+int64_t symm_flag_bytes();
 void newton_schulz(at::Tensor& U, const at::Tensor& scale, const std::vector<double>& coeffs, at::Tensor& out,
                    bool clobber_input);
 void muon_momentum(const std::vector<at::Tensor>& M, const std::vector<at::Tensor>& G,
@@ -34,6 +50,9 @@ void dion_momentum_add(const std::vector<at::Tensor>& M, const std::vector<at::T
 void dion_fixup(at::Tensor& P, at::Tensor& R, const at::Tensor& Q0, const at::Tensor& nz);
 void col_sumsq(const at::Tensor& R, at::Tensor& out);
 void col_normalize(const at::Tensor& R, const at::Tensor& sumsq, double eps, at::Tensor& Q);
+void cholesky_lower(at::Tensor& A, at::Tensor& info);
+void tri_inv_lower(const at::Tensor& S, at::Tensor& Z, bool upper);
+void qr_r(at::Tensor& A, at::Tensor& R);
 }  // namespace bdion
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -43,6 +62,20 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("scale") = py::none(), py::arg("alpha_pow") = 0, py::arg("beta_pow") = 0, py::arg("sym") = false,
         py::arg("param_mode") = false, py::arg("gamma") = 1.0, py::arg("delta") = 1.0, py::arg("bn") = 0,
         py::arg("D_ptrs") = py::none(), py::arg("ldd_ptrs") = 0, py::arg("out_dtype_ptrs") = 0);
+  m.def("gemm_ex", &bdion::gemm_ex, "gemm with replicated / row-split pointer-array outputs", py::arg("A"),
+        py::arg("B"), py::arg("D"), py::arg("C"), py::arg("alpha"), py::arg("beta"), py::arg("scale"),
+        py::arg("alpha_pow"), py::arg("beta_pow"), py::arg("sym"), py::arg("param_mode"), py::arg("gamma"),
+        py::arg("delta"), py::arg("bn"), py::arg("D_ptrs"), py::arg("ldd_ptrs"), py::arg("out_dtype_ptrs"),
+        py::arg("nrep"), py::arg("rows_per_ptr"));
+  m.def("symm_create", &bdion::symm_create);
+  m.def("symm_open", &bdion::symm_open);
+  m.def("symm_close", &bdion::symm_close);
+  m.def("symm_free", &bdion::symm_free);
+  m.def("symm_view", &bdion::symm_view);
+  m.def("symm_barrier", &bdion::symm_barrier);
+  m.def("symm_reduce_slots", &bdion::symm_reduce_slots);
+  m.def("symm_push", &bdion::symm_push);
+  m.def("symm_flag_bytes", &bdion::symm_flag_bytes);
   m.def("newton_schulz", &bdion::newton_schulz, "batched quintic Newton-Schulz", py::arg("U"), py::arg("scale"),
         py::arg("coeffs"), py::arg("out"), py::arg("clobber_input") = false);
   m.def("muon_momentum", &bdion::muon_momentum);
@@ -60,6 +93,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dion_fixup", &bdion::dion_fixup);
   m.def("col_sumsq", &bdion::col_sumsq);
   m.def("col_normalize", &bdion::col_normalize);
+  m.def("cholesky_lower", &bdion::cholesky_lower);
+  m.def("tri_inv_lower", &bdion::tri_inv_lower);
+  m.def("qr_r", &bdion::qr_r);
   m.def("status_read", &bdion::status_read);
   m.def("status_clear", &bdion::status_clear);
   m.def("set_wait_limit_ns", &bdion::set_wait_limit_ns);

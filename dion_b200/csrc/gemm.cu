@@ -72,10 +72,13 @@ int gemm_sm_count() {
 // given (int64 device tensor of batch addresses), per-batch outputs with row
 // stride ldd_ptrs.
 // param_mode: D = gamma*D + delta*(alpha*A@B + beta*C) in place.
-void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10::optional<at::Tensor>& C, double alpha,
-          double beta, const c10::optional<at::Tensor>& scale, int64_t alpha_pow, int64_t beta_pow, bool sym,
-          bool param_mode, double gamma, double delta, int64_t bn_pref, const c10::optional<at::Tensor>& D_ptrs,
-          int64_t ldd_ptrs, int64_t out_dtype_ptrs) {
+// nrep / rows_per_ptr: see the pointer-array note in gemm_tc.cuh (D_ptrs
+// then holds batch * ceil(M / rows_per_ptr) * nrep addresses).
+void gemm_ex(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10::optional<at::Tensor>& C,
+             double alpha, double beta, const c10::optional<at::Tensor>& scale, int64_t alpha_pow, int64_t beta_pow,
+             bool sym, bool param_mode, double gamma, double delta, int64_t bn_pref,
+             const c10::optional<at::Tensor>& D_ptrs, int64_t ldd_ptrs, int64_t out_dtype_ptrs, int64_t nrep,
+             int64_t rows_per_ptr) {
   TORCH_CHECK(A.is_cuda() && B.is_cuda(), "dion_b200 gemm: CUDA tensors expected");
   TORCH_CHECK(A.dim() == 3 && B.dim() == 3, "dion_b200 gemm: 3-D [batch, rows, cols] views expected");
   const bool fp32_in = A.scalar_type() == at::kFloat;
@@ -89,9 +92,15 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10::op
     TORCH_CHECK(D.is_cuda() && D.dim() == 3 && D.size(0) == batch && D.size(1) == M && D.size(2) == N &&
                     D.stride(2) == 1,
                 "dion_b200 gemm: D must be [batch, M, N] with unit column stride");
+  }
+  TORCH_CHECK(nrep >= 1 && rows_per_ptr >= 0, "dion_b200 gemm: bad nrep / rows_per_ptr");
+  const int64_t splits = (use_ptrs && rows_per_ptr > 0) ? (M + rows_per_ptr - 1) / rows_per_ptr : 1;
+  if (use_ptrs) {
+    TORCH_CHECK(D_ptrs->scalar_type() == at::kLong && D_ptrs->numel() >= batch * splits * nrep && D_ptrs->is_cuda(),
+                "dion_b200 gemm: D_ptrs must be an int64 CUDA tensor of batch*splits*nrep addresses");
+    TORCH_CHECK(!param_mode || nrep == 1, "dion_b200 gemm: param mode writes one destination");
   } else {
-    TORCH_CHECK(D_ptrs->scalar_type() == at::kLong && D_ptrs->numel() >= batch && D_ptrs->is_cuda(),
-                "dion_b200 gemm: D_ptrs must be an int64 CUDA tensor of batch addresses");
+    TORCH_CHECK(nrep == 1 && rows_per_ptr == 0, "dion_b200 gemm: nrep / rows_per_ptr need D_ptrs");
   }
   c10::cuda::CUDAGuard guard(A.device());
 
@@ -127,6 +136,9 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10::op
     args.strideD = D.stride(0);
     out_t = D.scalar_type();
   }
+  args.nrep = (int)nrep;
+  args.rows_per_ptr = use_ptrs ? (int)rows_per_ptr : 0;
+  args.splits = (int)splits;
   args.C = nullptr;
   if (C.has_value() && C->defined()) {
     TORCH_CHECK(C->dim() == 3 && C->size(0) == batch && C->size(1) == M && C->size(2) == N && C->stride(2) == 1,
@@ -186,6 +198,14 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10::op
     gemm_dispatch_tf32(a_mn, b_mn, bn, ma, mb, args, s, out_t, param_mode);
   else
     gemm_dispatch_bf16(a_mn, b_mn, bn, ma, mb, args, s, out_t, param_mode);
+}
+
+void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10::optional<at::Tensor>& C, double alpha,
+          double beta, const c10::optional<at::Tensor>& scale, int64_t alpha_pow, int64_t beta_pow, bool sym,
+          bool param_mode, double gamma, double delta, int64_t bn_pref, const c10::optional<at::Tensor>& D_ptrs,
+          int64_t ldd_ptrs, int64_t out_dtype_ptrs) {
+  gemm_ex(A, B, D, C, alpha, beta, scale, alpha_pow, beta_pow, sym, param_mode, gamma, delta, bn_pref, D_ptrs,
+          ldd_ptrs, out_dtype_ptrs, 1, 0);
 }
 
 }  // namespace bdion

@@ -24,6 +24,13 @@
 //   PARAM   : D = gamma*D + delta*(alpha_b*acc + beta_b*C)  (in-place weight
 //             update fused into the last Newton-Schulz GEMM)
 //
+// Pointer-array outputs (D_ptrs): destination d of row `row` of batch b is
+// D_ptrs[(b*splits + row/rows_per_ptr)*nrep + rep], rep < nrep, at local row
+// row % rows_per_ptr. The addresses may be another GPU's memory (peer
+// mapping): the epilogue then stores the tile over NVLink while the tensor
+// cores work on the next tile, which is how GEMM -> reduce-scatter,
+// GEMM -> all-gather (nrep = world) and NS -> scatter are fused.
+//
 // alpha_b = alpha * scale[b]^alpha_pow, beta_b = beta * scale[b]^beta_pow when
 // a per-batch scale vector is given (used to fold the Frobenius
 // normalisation of Newton-Schulz into the first iteration).
@@ -36,7 +43,10 @@ namespace bdion {
 struct GemmArgs {
   int M, N, K, batch;
   void* D;
-  void* const* D_ptrs;  // optional per-batch output pointers (device array)
+  void* const* D_ptrs;  // optional output pointers (device array), see below
+  int nrep;             // D_ptrs: copies of every output element (>= 1)
+  int rows_per_ptr;     // D_ptrs: rows per destination (0: all M rows)
+  int splits;           // D_ptrs: destinations per batch along M
   int64_t ldd, strideD;
   const void* C;  // may be null
   int64_t ldc, strideC;
@@ -306,8 +316,18 @@ __global__ void __launch_bounds__(192, 1)
       }
       const int row = tm * kBM + q * 32 + lane;
       const bool row_ok = row < args.M;
-      OutT* Db = args.D_ptrs ? reinterpret_cast<OutT*>(args.D_ptrs[b])
-                             : reinterpret_cast<OutT*>(args.D) + (int64_t)b * args.strideD;
+      int lrow = row;
+      void* const* dps = nullptr;
+      OutT* Db = reinterpret_cast<OutT*>(args.D) + (int64_t)b * args.strideD;
+      if (args.D_ptrs != nullptr && row_ok) {
+        int split = 0;
+        if (args.rows_per_ptr > 0) {
+          split = row / args.rows_per_ptr;
+          lrow = row - split * args.rows_per_ptr;
+        }
+        dps = args.D_ptrs + ((int64_t)b * args.splits + split) * args.nrep;
+        Db = reinterpret_cast<OutT*>(dps[0]);
+      }
       const CT* Cb = args.C ? reinterpret_cast<const CT*>(args.C) + (int64_t)b * args.strideC : nullptr;
 
 #pragma unroll 1
@@ -336,7 +356,7 @@ __global__ void __launch_bounds__(192, 1)
               if (col0 + i < args.N) v[i] += beta * to_f<CT>(crow[i]);
           }
         }
-        OutT* drow = Db + (int64_t)row * args.ldd + col0;
+        OutT* drow = Db + (int64_t)lrow * args.ldd + col0;
         if (PARAM) {
           if (full) {
 #pragma unroll
@@ -352,12 +372,15 @@ __global__ void __launch_bounds__(192, 1)
               if (col0 + i < args.N) drow[i] = from_f<OutT>(args.gamma * to_f<OutT>(drow[i]) + args.delta * v[i]);
           }
         } else if (!args.sym) {
-          if (full) {
+          for (int rep = 0; rep < args.nrep; ++rep) {
+            if (rep > 0) drow = reinterpret_cast<OutT*>(dps[rep]) + (int64_t)lrow * args.ldd + col0;
+            if (full) {
 #pragma unroll
-            for (int i = 0; i < 32; i += 8) store8(drow + i, v + i);
-          } else {
-            for (int i = 0; i < 32; ++i)
-              if (col0 + i < args.N) drow[i] = from_f<OutT>(v[i]);
+              for (int i = 0; i < 32; i += 8) store8(drow + i, v + i);
+            } else {
+              for (int i = 0; i < 32; ++i)
+                if (col0 + i < args.N) drow[i] = from_f<OutT>(v[i]);
+            }
           }
         } else {
           // symmetric: write (row, j) for j >= row and mirror (j, row) for j > row

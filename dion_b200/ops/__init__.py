@@ -18,6 +18,7 @@ from ._ext import ext, has_ext, check_status, clear_status, StatusError  # noqa:
 __all__ = [
     "matmul",
     "matmul_update_",
+    "matmul_to_ptrs",
     "newton_schulz",
     "muon_momentum_",
     "scaled_update_",
@@ -186,6 +187,33 @@ def matmul_update_(
     ptrs = _ptr_tensor(outs)
     ext().gemm(A3, B3, o0.unsqueeze(0), None, float(alpha), 0.0, None, 0, 0, False, True, float(gamma), float(delta),
                0, ptrs, o0.stride(0), _SCALAR_TYPE[o0.dtype])
+
+
+def matmul_to_ptrs(
+    A: Tensor,
+    B: Tensor,
+    ptrs: Tensor,
+    ldd: int,
+    out_dtype: torch.dtype,
+    *,
+    nrep: int = 1,
+    rows_per_ptr: int = 0,
+    alpha: float = 1.0,
+) -> None:
+    """``alpha * A[b] @ B[b]`` stored through a device pointer array.
+
+    Row ``i`` of batch ``b`` goes to ``ptrs[(b*splits + i//rows_per_ptr)*nrep + rep]``
+    (local row ``i % rows_per_ptr``, row stride ``ldd`` elements) for every
+    ``rep < nrep``; ``splits = ceil(M / rows_per_ptr)`` (1 when 0). The
+    addresses may be peer-GPU memory: the GEMM epilogue then writes each tile
+    over NVLink as soon as it leaves the tensor cores.
+    """
+    A3, B3 = _as3d(A), _as3d(B)
+    assert A.is_cuda and ptrs.is_cuda and ptrs.dtype == torch.int64
+    A3, B3 = _tma_operands(A3, B3)
+    dummy = torch.empty((1, 1, 1), device=A.device, dtype=out_dtype)
+    ext().gemm_ex(A3, B3, dummy, None, float(alpha), 0.0, None, 0, 0, False, False, 1.0, 1.0, 0, ptrs, int(ldd),
+                  _SCALAR_TYPE[out_dtype], int(nrep), int(rows_per_ptr))
 
 
 def _ns_reference(U: Tensor, coeffs: Sequence[Tuple[float, float, float]], eps: float) -> Tensor:

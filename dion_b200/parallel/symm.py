@@ -1,0 +1,138 @@
+"""Symmetric peer memory for in-kernel collectives over NVLink / NVSwitch.
+
+``SymmetricHeap(group, nbytes)`` gives every rank of a single-node process
+group one device region of the same size and maps every peer's region into
+this process (CUDA IPC, see csrc/symm.cu). Kernels then address any rank's
+copy of an offset directly:
+
+  * ``heap.view(offset, shape, dtype)``  local tensor view
+  * ``heap.addr(rank, offset)``          device address on ``rank``'s GPU
+  * ``heap.barrier()``                   device-side epoch barrier (bounded
+                                         wait; a timeout sets the status word)
+
+The reduce-scatter / all-gather of Dion's power iteration and the all-to-all
+of Muon are built from these: a producing GEMM's epilogue stores its tiles
+into the owner rank's region, a barrier orders those stores, and the consumer
+reads its own region locally. The collectives these replace are the
+``reduce_scatter_tensor`` / ``all_gather_into_tensor`` / ``all_to_all`` calls
+of ada_dion/optim/adadion_v2.py:927-949,1053-1071 and DION/muon.py:464-491.
+
+The path is used only when every rank of the job is on one node (the IPC
+mapping needs that) and can be switched off with ``DION_B200_P2P=0``.
+"""
+from __future__ import annotations
+
+import os
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+from torch import Tensor
+
+from .. import ops
+
+__all__ = ["SymmetricHeap", "p2p_enabled", "heap_for"]
+
+_ALIGN = 256
+_SCALAR_TYPE = {torch.float32: 6, torch.bfloat16: 15, torch.int64: 4, torch.uint8: 0}
+
+
+def p2p_enabled(group, device: torch.device) -> bool:
+    """Same answer on every rank: CUDA, extension built, >1 ranks, one node."""
+    if os.environ.get("DION_B200_P2P", "1") == "0":
+        return False
+    if device.type != "cuda" or not ops.has_ext() or not dist.is_initialized():
+        return False
+    if dist.get_backend(group) != "nccl":
+        return False
+    W = dist.get_world_size(group)
+    if W <= 1:
+        return False
+    local = int(os.environ.get("LOCAL_WORLD_SIZE", "0") or 0)
+    return local >= dist.get_world_size() and torch.cuda.device_count() >= W
+
+
+def _round(n: int, a: int = _ALIGN) -> int:
+    return (n + a - 1) // a * a
+
+
+class SymmetricHeap:
+    def __init__(self, group, nbytes: int, device: Optional[torch.device] = None):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        E = ops.ext()
+        self._flag_off = 0
+        self.data_off = _round(E.symm_flag_bytes())
+        self.nbytes = _round(nbytes)
+        ptr, handle = E.symm_create(self.data_off + self.nbytes)
+        hd = handle.to(self.device)
+        allh = torch.empty(self.world * hd.numel(), dtype=torch.uint8, device=self.device)
+        dist.all_gather_into_tensor(allh, hd, group=group)
+        allh = allh.cpu().view(self.world, -1)
+        self.bases: List[int] = []
+        for j in range(self.world):
+            self.bases.append(ptr if j == self.rank else E.symm_open(allh[j].contiguous()))
+        self._own = ptr
+        self._flags = torch.tensor(self.bases, dtype=torch.int64).to(self.device)
+        self._closed = False
+
+    # ------------------------------------------------------------ addressing
+    def addr(self, rank: int, offset: int) -> int:
+        return self.bases[rank] + self.data_off + int(offset)
+
+    def view(self, offset: int, shape: Sequence[int], dtype: torch.dtype) -> Tensor:
+        n = 1
+        for s in shape:
+            n *= int(s)
+        esz = torch.empty((), dtype=dtype).element_size()
+        assert offset % 16 == 0 and offset + n * esz <= self.nbytes, "symmetric heap view out of range"
+        return ops.ext().symm_view(self.addr(self.rank, offset), n, _SCALAR_TYPE[dtype]).view(*shape)
+
+    def ptr_tensor(self, addrs: Sequence[int]) -> Tensor:
+        return torch.tensor(list(addrs), dtype=torch.int64).to(self.device, non_blocking=True)
+
+    # ------------------------------------------------------------ collectives
+    def barrier(self) -> None:
+        ops.ext().symm_barrier(self._flags, self.bases[self.rank] + self._flag_off, self.rank, self.world)
+
+    def reduce_slots(self, src: Tensor, dst: Tensor, nslots: int) -> None:
+        ops.ext().symm_reduce_slots(src, dst, nslots)
+
+    def push(self, src: Tensor, dst_addrs: Tensor) -> None:
+        ops.ext().symm_push(src, dst_addrs)
+
+    def close(self) -> None:
+        if self._closed:
+            return
+        self._closed = True
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        E = ops.ext()
+        for j, b in enumerate(self.bases):
+            if j != self.rank:
+                E.symm_close(b)
+        E.symm_free(self._own)
+
+
+_HEAPS: Dict[Tuple[int, str], SymmetricHeap] = {}
+
+
+def heap_for(group, nbytes: int, tag: str, device: torch.device) -> SymmetricHeap:
+    """A cached heap of at least ``nbytes`` for (group, tag); regrown (collectively) when too small."""
+    key = (id(group), tag)
+    h = _HEAPS.get(key)
+    if h is None or h.nbytes < nbytes:
+        if h is not None:
+            h.close()
+        h = SymmetricHeap(group, nbytes, device)
+        _HEAPS[key] = h
+    return h
+
+
+def release_all() -> None:
+    """Unmap and free every cached heap (collective over each heap's group)."""
+    for h in list(_HEAPS.values()):
+        h.close()
+    _HEAPS.clear()
