@@ -24,6 +24,8 @@ void symm_barrier(const at::Tensor& peer_flags, int64_t my_flags, int64_t rank, 
 void symm_reduce_slots(const at::Tensor& src, at::Tensor& dst, int64_t nslots);
 void symm_push(const at::Tensor& src, const at::Tensor& dsts);
 int64_t symm_flag_bytes();
+void newton_schulz_ex(at::Tensor& U, const at::Tensor& scale, const std::vector<double>& coeffs, at::Tensor& out,
+                      bool clobber_input, const c10::optional<at::Tensor>& out_ptrs, int64_t rows_per_ptr);
 void newton_schulz(at::Tensor& U, const at::Tensor& scale, const std::vector<double>& coeffs, at::Tensor& out,
                    bool clobber_input);
 void muon_momentum(const std::vector<at::Tensor>& M, const std::vector<at::Tensor>& G,
@@ -78,6 +80,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_flag_bytes", &bdion::symm_flag_bytes);
   m.def("newton_schulz", &bdion::newton_schulz, "batched quintic Newton-Schulz", py::arg("U"), py::arg("scale"),
         py::arg("coeffs"), py::arg("out"), py::arg("clobber_input") = false);
+  m.def("newton_schulz_ex", &bdion::newton_schulz_ex, "Newton-Schulz whose last GEMM scatters rows",
+        py::arg("U"), py::arg("scale"), py::arg("coeffs"), py::arg("out"), py::arg("clobber_input"),
+        py::arg("out_ptrs"), py::arg("rows_per_ptr"));
   m.def("muon_momentum", &bdion::muon_momentum);
   m.def("multi_sumsq", &bdion::multi_sumsq);
   m.def("scaled_update", &bdion::scaled_update);

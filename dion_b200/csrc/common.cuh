@@ -82,5 +82,10 @@ __device__ __forceinline__ void store8(float* p, const float* v) {
   *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
   *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
 }
+// One 16-byte store: 8 bf16 or 4 fp32 elements.
+__device__ __forceinline__ void store8or4(__nv_bfloat16* p, const float* v) { store8(p, v); }
+__device__ __forceinline__ void store8or4(float* p, const float* v) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+}
 
 }  // namespace bdion

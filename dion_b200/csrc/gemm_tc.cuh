@@ -90,7 +90,9 @@ struct GemmCfg {
   static constexpr int kBBytes = BN * 128;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = 2 * BN;
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  // epilogue staging: one 32 x 33 fp32 transpose tile per epilogue warp
+  static constexpr int kStagingBytes = 4 * 32 * 33 * 4;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/ + kStagingBytes;
 };
 
 __device__ __forceinline__ int sym_row_start(int tm, int BN) { return (tm * kBM) / BN; }
@@ -146,6 +148,7 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* drain_bar = bars + 2 * S + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
   volatile int* s_abort = reinterpret_cast<volatile int*>(bars + 2 * S + 6);
+  float* staging = reinterpret_cast<float*>(smem + S * Cfg::kStageBytes + 256);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -330,17 +333,69 @@ __global__ void __launch_bounds__(192, 1)
       }
       const CT* Cb = args.C ? reinterpret_cast<const CT*>(args.C) + (int64_t)b * args.strideC : nullptr;
 
+      float* stg = staging + q * (32 * 33);
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN + c * 32, r);
         tmem_wait_ld();
         const int col0 = tn * BN + c * 32;
-        if (!row_ok || col0 >= args.N) continue;
+        if (col0 >= args.N) continue;  // warp-uniform
         float v[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = alpha * __uint_as_float(r[i]);
         const bool full = col0 + 32 <= args.N;
+        if (!PARAM && !args.sym && full) {
+          // Coalesced store: stage the warp's 32x32 block in shared memory, then
+          // each store instruction writes whole 128-byte (fp32) / 64-byte (bf16)
+          // row segments, which matters most when the rows live on a peer GPU.
+          if (row_ok && Cb != nullptr && beta != 0.f) {
+            const CT* crow = Cb + (int64_t)row * args.ldc + col0;
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              float cv[8];
+              load8(crow + i, cv);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) v[i + j] += beta * cv[j];
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < 32; ++i) stg[lane * 33 + i] = v[i];
+          __syncwarp();
+          constexpr int kVec = 16 / sizeof(OutT);     // elements per 16-byte store
+          constexpr int kLanesPerRow = 32 / kVec;     // 8 (fp32) or 4 (bf16)
+          constexpr int kRowsPerPass = 32 / kLanesPerRow;
+          const int sub = lane % kLanesPerRow;
+#pragma unroll
+          for (int pass = 0; pass < 32 / kRowsPerPass; ++pass) {
+            const int rr = pass * kRowsPerPass + lane / kLanesPerRow;
+            const int grow = tm * kBM + q * 32 + rr;
+            if (grow < args.M) {
+              float vals[kVec];
+#pragma unroll
+              for (int j = 0; j < kVec; ++j) vals[j] = stg[rr * 33 + sub * kVec + j];
+              int lr = grow;
+              void* const* rp = nullptr;
+              OutT* base = reinterpret_cast<OutT*>(args.D) + (int64_t)b * args.strideD;
+              if (args.D_ptrs != nullptr) {
+                int split = 0;
+                if (args.rows_per_ptr > 0) {
+                  split = grow / args.rows_per_ptr;
+                  lr = grow - split * args.rows_per_ptr;
+                }
+                rp = args.D_ptrs + ((int64_t)b * args.splits + split) * args.nrep;
+                base = reinterpret_cast<OutT*>(rp[0]);
+              }
+              for (int rep = 0; rep < args.nrep; ++rep) {
+                if (rep > 0) base = reinterpret_cast<OutT*>(rp[rep]);
+                store8or4(base + (int64_t)lr * args.ldd + col0 + sub * kVec, vals);
+              }
+            }
+          }
+          __syncwarp();
+          continue;
+        }
+        if (!row_ok) continue;
         if (Cb != nullptr && beta != 0.f) {
           const CT* crow = Cb + (int64_t)row * args.ldc + col0;
           if (full) {

@@ -142,13 +142,13 @@ class HybridOptimizersContainer(Optimizer):
         if name == "Muon":
             Muon = optim.Muon
             return Muon(groups, distributed_mesh=shard_mesh, lr=cfg.lr, mu=cfg.mu, weight_decay=cfg.weight_decay,
-                        nesterov=cfg.nesterov, adjust_lr=cfg.adjust_lr, ns_coeffs=cfg.ns_coeffs)
+                        nesterov=cfg.nesterov, adjust_lr=cfg.adjust_lr, ns_coeffs=cfg.ns_coeffs, tp_mesh=tp_mesh)
         if name == "Dion":
             return optim.Dion(groups, replicate_mesh=replicate_mesh, outer_shard_mesh=shard_mesh, inner_shard_mesh=tp_mesh,
                         lr=cfg.lr, mu=cfg.mu, rank_fraction=cfg.rank_fraction, weight_decay=cfg.weight_decay)
         if name == "Dion2":
             return optim.Dion2(groups, distributed_mesh=shard_mesh, lr=cfg.lr, fraction=cfg.fraction,
-                         ef_decay=cfg.ef_decay, weight_decay=cfg.weight_decay)
+                         ef_decay=cfg.ef_decay, weight_decay=cfg.weight_decay, tp_mesh=tp_mesh)
         if name == "AdaDionV2":
             return optim.AdaDionV2(groups, replicate_mesh=replicate_mesh, outer_shard_mesh=shard_mesh,
                              inner_shard_mesh=tp_mesh, lr=cfg.lr, mu=cfg.mu, weight_decay=cfg.weight_decay,

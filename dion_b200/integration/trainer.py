@@ -15,7 +15,7 @@ import math
 import os
 import time
 from dataclasses import dataclass, field
-from typing import Dict, Iterator, List, Optional, Tuple
+from typing import Any, Dict, Iterator, List, Optional, Tuple
 
 import torch
 import torch.distributed as dist
@@ -23,6 +23,7 @@ import torch.nn as nn
 
 from ..models.llama3 import Llama3Config, Transformer, llama3_config
 from ..parallel.fsdp import apply_fsdp
+from ..parallel.tp import apply_tp
 from ..parallel.mesh import ParallelDims, build_mesh, init_distributed
 from .hybrid_optimizer import HybridOptimizersContainer
 
@@ -82,6 +83,33 @@ class SyntheticTokens:
             yield self.next()
 
 
+def clip_grad_norm_multi_mesh_(params: List[torch.nn.Parameter], max_norm: float) -> torch.Tensor:
+    """Global-norm clipping when gradients live on different meshes (FSDP-only
+    and FSDP x TP DTensors in one model): norms are taken per (mesh,
+    placements) group, made replicated, and combined on the host side of the
+    autograd graph; the clip coefficient scales every local shard."""
+    from torch.distributed.tensor import DTensor
+
+    groups: Dict[Any, List[torch.Tensor]] = {}
+    for p in params:
+        g = p.grad
+        if g is None:
+            continue
+        key = (id(g.device_mesh), tuple(g.placements)) if isinstance(g, DTensor) else None
+        groups.setdefault(key, []).append(g)
+    sq = []
+    for gs in groups.values():
+        n = torch.nn.utils.get_total_norm(gs, 2.0, foreach=True)
+        if isinstance(n, DTensor):
+            n = n.full_tensor()
+        sq.append(n.float().square())
+    total = torch.stack(sq).sum().sqrt()
+    coef = (max_norm / (total + 1e-6)).clamp(max=1.0)
+    for gs in groups.values():
+        torch._foreach_mul_([g.to_local() if isinstance(g, DTensor) else g for g in gs], coef)
+    return total
+
+
 class Trainer:
     def __init__(self, cfg: TrainerConfig, device: Optional[torch.device] = None):
         self.cfg = cfg
@@ -107,16 +135,25 @@ class Trainer:
             model = Transformer(mcfg)
         gen = torch.Generator(device=device).manual_seed(cfg.seed)
         model.init_weights(cfg.init_mode, generator=gen)
+        tp_mesh = None
+        if cfg.tp > 1:
+            if self.mesh is None or "tp" not in self.mesh.mesh_dim_names:
+                raise ValueError("tensor parallelism needs use_fsdp=True (the mesh is built there)")
+            tp_mesh = self.mesh["tp"]
+            apply_tp(model, tp_mesh)
         if cfg.use_fsdp:
             apply_fsdp(model, self.dp_mesh)
         self.model = model
+        self.tp_mesh = tp_mesh
         self.optimizers = HybridOptimizersContainer(
-            cfg.optimizer, model_parts=[model], shard_mesh=shard_mesh, replicate_mesh=replicate_mesh
+            cfg.optimizer, model_parts=[model], shard_mesh=shard_mesh, replicate_mesh=replicate_mesh, tp_mesh=tp_mesh
         )
         self._base_lrs = [[g["lr"] for g in o.param_groups] for o in self.optimizers]
         self.step_idx = 0
-        self.data = SyntheticTokens(mcfg.vocab_size, cfg.seq_len, cfg.local_batch_size, cfg.seed, self.rank,
-                                    self.world // max(1, cfg.tp))
+        # TP is the innermost mesh dim: the ranks of one TP group share a batch
+        tp = max(1, cfg.tp)
+        self.data = SyntheticTokens(mcfg.vocab_size, cfg.seq_len, cfg.local_batch_size, cfg.seed, self.rank // tp,
+                                    self.world // tp)
 
     @property
     def last_grad_norm(self) -> float:
@@ -146,7 +183,11 @@ class Trainer:
         self._set_lr()
         loss = self.forward_backward(tokens, labels)
         if self.cfg.max_norm and self.cfg.max_norm > 0:
-            self._grad_norm = torch.nn.utils.clip_grad_norm_(self.model.parameters(), self.cfg.max_norm, foreach=True)
+            if self.tp_mesh is not None:
+                self._grad_norm = clip_grad_norm_multi_mesh_(list(self.model.parameters()), self.cfg.max_norm)
+            else:
+                self._grad_norm = torch.nn.utils.clip_grad_norm_(self.model.parameters(), self.cfg.max_norm,
+                                                                 foreach=True)
         self.optimizers.step()
         self.optimizers.zero_grad(set_to_none=True)
         self.step_idx += 1

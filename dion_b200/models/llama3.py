@@ -110,9 +110,10 @@ class Attention(nn.Module):
 
     def forward(self, x: torch.Tensor, rope: torch.Tensor) -> torch.Tensor:
         bs, seqlen, _ = x.shape
-        q = self.wq(x).view(bs, seqlen, self.n_heads, self.head_dim)
-        k = self.wk(x).view(bs, seqlen, self.n_kv_heads, self.head_dim)
-        v = self.wv(x).view(bs, seqlen, self.n_kv_heads, self.head_dim)
+        # -1 heads: under tensor parallelism each rank holds n_heads / tp of them
+        q = self.wq(x).view(bs, seqlen, -1, self.head_dim)
+        k = self.wk(x).view(bs, seqlen, -1, self.head_dim)
+        v = self.wv(x).view(bs, seqlen, -1, self.head_dim)
         q, k = L.apply_rope(q, k, rope)
         o = L.causal_attention(q, k, v)  # [bs, seq, heads, hd]
         return self.wo(o.reshape(bs, seqlen, -1))

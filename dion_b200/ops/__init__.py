@@ -240,12 +240,19 @@ def newton_schulz(
     scale: Optional[Tensor] = None,
     out: Optional[Tensor] = None,
     clobber_input: bool = False,
+    out_ptrs: Optional[Tensor] = None,
+    rows_per_ptr: int = 0,
 ) -> Tensor:
     """Orthogonalise each matrix of ``U`` (``[batch, m, n]`` or ``[m, n]``).
 
     ``scale`` (fp32, one value per matrix) is ``1/(||U_b||_F + eps)``; it is
     computed here when not given (the Muon momentum kernel produces it for
     free). Returns bf16.
+
+    With ``out_ptrs`` (int64 device array, ``batch * m/rows_per_ptr``
+    addresses) the result is not written to ``out``: the last GEMM stores rows
+    ``[j*rows_per_ptr, (j+1)*rows_per_ptr)`` of matrix b at ``out_ptrs[b*splits + j]``
+    (row stride n). Used to scatter row shards straight to their owner GPUs.
     """
     squeeze = U.dim() == 2
     U3 = _as3d(U)
@@ -259,6 +266,16 @@ def newton_schulz(
         U3 = U3.to(torch.bfloat16).contiguous()
         clobber_input = True
     m, n = U3.shape[-2:]
+    if out_ptrs is not None:
+        assert m % 8 == 0 and n % 8 == 0 and rows_per_ptr > 0, "row-scatter Newton-Schulz needs 8-aligned shapes"
+        if scale is None:
+            ss = multi_sumsq(list(U3.unbind(0)))
+            scale = 1.0 / (ss.sqrt() + eps)
+        out3 = _as3d(out) if out is not None else torch.empty_like(U3)
+        flat = [float(x) for abc in coeffs for x in abc]
+        ext().newton_schulz_ex(U3, scale.float().contiguous(), flat, out3, bool(clobber_input), out_ptrs,
+                               int(rows_per_ptr))
+        return out3
     if (m % 8) or (n % 8):
         # pad both dims with zeros: orthogonalisation of [[X, 0], [0, 0]] keeps X's block
         pm, pn = (-m) % 8, (-n) % 8

@@ -170,6 +170,7 @@ class Dion(Optimizer):
         )
         self._mixed_precision_config = mixed_precision_config or DionMixedPrecisionConfig()
         self._arenas: Dict[Tuple, Dict[str, Any]] = {}
+        self._p2p_ptrs: Dict[Tuple, Any] = {}
         self._q_init_calls = 0
 
     # ------------------------------------------------------------------ step
@@ -561,16 +562,21 @@ class Dion(Optimizer):
         nz = torch.zeros(sets * W, device=Mb.device, dtype=torch.float32)
         nz[torch.tensor(order, device=Mb.device)] = nz_p
         t = cfg.is_transposed
-        P_part = self._power_p(Mb, Qb, t)  # partial sums over this rank's shard
-        pd, r = P_part.shape[1:]
-        mine = torch.empty((sets, pd, r), device=Mb.device, dtype=torch.float32)
-        dist.reduce_scatter_tensor(mine, P_part, op=dist.ReduceOp.SUM, group=pg)
-        if compressed:
-            mine = self._all_reduce_replicate([mine])[0]
         me = mesh.get_local_rank()
-        mine = self._orth(mine, group, None if ranks is None else ranks[me * sets:(me + 1) * sets])
-        P_all = torch.empty((sets * W, pd, r), device=Mb.device, dtype=torch.float32)
-        dist.all_gather_into_tensor(P_all, mine.contiguous(), group=pg)
+        my_ranks = None if ranks is None else ranks[me * sets:(me + 1) * sets]
+        heap = self._p2p_heap(pg, Mb, Qb, t, sets, W)
+        if heap is not None:
+            P_all = self._p2p_power_orth(heap, group, Mb, Qb, t, sets, W, me, my_ranks, compressed)
+        else:
+            P_part = self._power_p(Mb, Qb, t)  # partial sums over this rank's shard
+            pd, r = P_part.shape[1:]
+            mine = torch.empty((sets, pd, r), device=Mb.device, dtype=torch.float32)
+            dist.reduce_scatter_tensor(mine, P_part, op=dist.ReduceOp.SUM, group=pg)
+            if compressed:
+                mine = self._all_reduce_replicate([mine])[0]
+            mine = self._orth(mine, group, my_ranks)
+            P_all = torch.empty((sets * W, pd, r), device=Mb.device, dtype=torch.float32)
+            dist.all_gather_into_tensor(P_all, mine.contiguous(), group=pg)
         R = self._power_r(Mb, P_all, t)
         if compressed:
             R = self._all_reduce_replicate([R])[0]
@@ -579,6 +585,63 @@ class Dion(Optimizer):
         dist.all_reduce(sumsq, op=dist.ReduceOp.SUM, group=pg)
         self._update(group, params, order, Mb, Qb, P_all, R, nz, t, sumsq)
         self._after_update(group, params, order, sumsq, ranks)
+
+    # ---- in-kernel collectives over symmetric peer memory
+    def _p2p_heap(self, pg, Mb: Tensor, Qb: Tensor, transposed: bool, sets: int, W: int):
+        """The group's symmetric heap when the fused NVLink path applies (the
+        decision depends only on shapes and the job layout, so every rank of
+        ``pg`` takes the same branch)."""
+        from ..parallel.symm import heap_for, p2p_enabled
+
+        if not p2p_enabled(pg, Mb.device):
+            return None
+        pd = Mb.size(2) if transposed else Mb.size(1)
+        r = Qb.size(-1)
+        if r % 4:
+            return None
+        slot = pd * r * 4
+        return heap_for(pg, 2 * W * sets * slot, "dion", Mb.device)
+
+    def _p2p_power_orth(self, heap, group: dict, Mb: Tensor, Qb: Tensor, transposed: bool, sets: int, W: int,
+                        me: int, my_ranks, compressed: bool) -> Tensor:
+        """P = M Q reduce-scattered, orthogonalised and all-gathered without NCCL.
+
+        Heap layout (fp32): recv [W (source), sets, pd, r] then P_all [W*sets, pd, r].
+          1. the P GEMM's epilogue stores batch k = j*sets + s straight into rank
+             j's recv[me, s] (NVLink stores overlapping the next tiles' MMAs);
+          2. device barrier; 3. this rank sums its W recv slots (fixed order);
+          4. the orthogonaliser's last GEMM stores each result into P_all[me*sets + s]
+             of every rank (nrep = W); 5. device barrier.
+        Replaces ada_dion/optim/adadion_v2.py:1051-1071 (reduce-scatter, orthogonalize, all-gather).
+        """
+        dt = self._op_dtype(Mb.dtype)
+        A = Mb.transpose(1, 2) if transposed else Mb
+        pd, r = A.size(1), Qb.size(-1)
+        slot = pd * r * 4
+        recv_off, pall_off = 0, W * sets * slot
+        key = ("p2p", heap.uid, sets, W, pd, r)
+        cached = self._p2p_ptrs.get(key)
+        if cached is None:
+            rs = [heap.addr(k // sets, recv_off + (me * sets + k % sets) * slot) for k in range(W * sets)]
+            ag = [heap.addr(j, pall_off + (me * sets + s) * slot) for s in range(sets) for j in range(W)]
+            cached = (heap.ptr_tensor(rs), heap.ptr_tensor(ag))
+            self._p2p_ptrs[key] = cached
+        rs_ptrs, ag_ptrs = cached
+        ops.matmul_to_ptrs(A.to(dt), Qb.to(dt), rs_ptrs, r, torch.float32)
+        heap.barrier()
+        recv = heap.view(recv_off, (W, sets, pd, r), torch.float32)
+        mine = torch.empty((sets, pd, r), device=Mb.device, dtype=torch.float32)
+        heap.reduce_slots(recv, mine, W)
+        if compressed:
+            mine = self._all_reduce_replicate([mine])[0]
+        if my_ranks is None and type(self)._orth is Dion._orth:
+            orthogonalize(mine, float(group["oversample"]), out_ptrs=ag_ptrs, nrep=W)
+        else:
+            out = self._orth(mine, group, my_ranks).float().contiguous()
+            for s in range(sets):
+                heap.push(out[s], ag_ptrs[s * W:(s + 1) * W])
+        heap.barrier()
+        return heap.view(pall_off, (W * sets, pd, r), torch.float32)
 
     # ---- FSDP x TP (inner-sharded) parameters
     def _dion_fsdp_tp(self, group: dict, params: List[Tensor], cfg: DionParamConfig) -> None:

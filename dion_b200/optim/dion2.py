@@ -56,6 +56,7 @@ class Dion2(Optimizer):
         adjust_lr: Optional[str] = "spectral_norm",
         ns_coeffs=None,
         seed: int = 0,
+        tp_mesh: Optional[DeviceMesh] = None,
     ):
         if lr < 0.0:
             raise ValueError(f"Invalid learning rate: {lr}")
@@ -82,6 +83,10 @@ class Dion2(Optimizer):
         else:
             self._rank, self._world, self._pg = 0, 1, None
         self._coeffs = _resolve_coeffs(ns_coeffs)
+        # tensor-parallel sub-mesh (FSDP x TP): the selected rows of a matrix are
+        # assembled over both meshes before Newton-Schulz
+        self._tp_pg = tp_mesh.get_group() if isinstance(tp_mesh, DeviceMesh) and tp_mesh.size() > 1 else None
+        self._tp = tp_mesh.size() if self._tp_pg is not None else 1
         self._gen: Optional[torch.Generator] = None
         self._seed = seed
 
@@ -117,8 +122,27 @@ class Dion2(Optimizer):
         return loss
 
     # ------------------------------------------------------------------ selection
-    def _select(self, Mb: Tensor, k: int, method: str) -> Tensor:
-        """Row indices [n, k] (sorted) of each matrix of the batch Mb [n, rows, cols]."""
+    def _tp_dim(self, p: Tensor) -> Optional[int]:
+        if self._tp_pg is None or not isinstance(p, DTensor):
+            return None
+        names = p.device_mesh.mesh_dim_names or ()
+        if "tp" not in names:
+            return None
+        pl = p.placements[names.index("tp")]
+        return pl.dim if pl.is_shard() else None
+
+    def _dp_dim(self, p: Tensor) -> Optional[int]:
+        """Tensor dim sharded over the FSDP (data-parallel shard) mesh."""
+        names = p.device_mesh.mesh_dim_names or ()
+        for i, pl in enumerate(p.placements):
+            if pl.is_shard() and p.device_mesh.size(i) > 1 and (not names or names[i] != "tp"):
+                return pl.dim
+        return None
+
+    def _select(self, Mb: Tensor, k: int, method: str, col_groups=()) -> Tensor:
+        """Row indices [n, k] (sorted) of each matrix of the batch Mb [n, rows, cols].
+        ``col_groups``: process groups the columns are split over; the row
+        scores are summed over them so all those ranks pick the same rows."""
         n, rows = Mb.shape[:2]
         if k >= rows:
             return torch.arange(rows, device=Mb.device).expand(n, rows)
@@ -127,7 +151,10 @@ class Dion2(Optimizer):
                 self._gen = torch.Generator(device=Mb.device).manual_seed(self._seed)
             idx = torch.rand((n, rows), device=Mb.device, generator=self._gen).topk(k, dim=1).indices
         else:
-            idx = Mb.abs().sum(dim=2, dtype=torch.float32).topk(k, dim=1).indices
+            score = Mb.abs().sum(dim=2, dtype=torch.float32)
+            for pg in col_groups:
+                dist.all_reduce(score, group=pg)
+            idx = score.topk(k, dim=1).indices
         return idx.sort(dim=1).values
 
     # ------------------------------------------------------------------ update
@@ -151,11 +178,16 @@ class Dion2(Optimizer):
             Mb = torch.stack(M)
         rows = Mb.shape[1]
         k = max(1, int(math.ceil(float(g["fraction"]) * rows)))
-        idx = self._select(Mb, k, g["selection_method"])                    # [n, k]
+        tp_dim = self._tp_dim(p0)
+        dp_dim = self._dp_dim(p0) if sharded else None
+        col_groups = [pg for pg, d in ((self._tp_pg, tp_dim), (self._pg, dp_dim)) if d == 1 and pg is not None]
+        idx = self._select(Mb, k, g["selection_method"], col_groups)       # [n, k]
         gather_idx = idx.unsqueeze(-1).expand(-1, -1, Mb.shape[2])
         sel = Mb.gather(1, gather_idx).to(torch.bfloat16)                   # [n, k, cols]
-        if sharded and self._world > 1:
-            U = self._orthogonalize_sharded(sel, eps)
+        if tp_dim is not None and self._world == 1:
+            U = self._ns_tp_gathered(sel, tp_dim, eps)
+        elif sharded and self._world > 1 and dp_dim is not None:
+            U = self._orthogonalize_sharded(sel, eps, tp_dim, dp_dim)
         elif self._pg is not None and self._world > 1:
             U = self._orthogonalize_replicated(sel, eps)
         else:
@@ -182,9 +214,26 @@ class Dion2(Optimizer):
         dist.all_gather_into_tensor(allp.view(W * sets, k, c), out.contiguous(), group=self._pg)
         return allp.transpose(0, 1).reshape(sets * W, k, c)[:n]
 
-    def _orthogonalize_sharded(self, sel: Tensor, eps: float) -> Tensor:
-        """Rows of every shard go to the matrix owner (one all-to-all), the owner
-        orthogonalises the stacked W*k rows, the rows come back."""
+    def _ns_tp_gathered(self, full: Tensor, tp_dim: int, eps: float) -> Tensor:
+        """Newton-Schulz of the matrices assembled over the TP mesh: rows are
+        stacked (column-parallel weights, tp_dim 0) or columns concatenated
+        (row-parallel, tp_dim 1); each rank keeps its block of the result."""
+        T = self._tp
+        parts = torch.empty((T,) + tuple(full.shape), device=full.device, dtype=full.dtype)
+        dist.all_gather_into_tensor(parts.view(T, -1), full.contiguous().view(1, -1), group=self._tp_pg)
+        whole = torch.cat(list(parts.unbind(0)), dim=1 + tp_dim).contiguous()
+        O = ops.newton_schulz(whole, self._coeffs, eps, clobber_input=True)
+        me = dist.get_rank(self._tp_pg)
+        w = full.shape[1 + tp_dim]
+        return O.narrow(1 + tp_dim, me * w, w).contiguous()
+
+    def _orthogonalize_sharded(self, sel: Tensor, eps: float, tp_dim: Optional[int] = None,
+                               dp_dim: int = 0) -> Tensor:
+        """The selected block of every shard goes to the matrix owner (one
+        all-to-all); the owner stacks the W blocks along the FSDP-sharded dim
+        (rows: W*k selected rows; columns: the same k rows, all columns),
+        assembles over TP as well when the matrix is also TP-sharded,
+        orthogonalises, and the blocks come back."""
         W, r = self._world, self._rank
         n, k, c = sel.shape
         sets = (n + W - 1) // W
@@ -193,9 +242,18 @@ class Dion2(Optimizer):
             send[i % W, i // W] = sel[i]
         recv = torch.empty_like(send)
         dist.all_to_all_single(recv.view(W, -1), send.view(W, -1), group=self._pg)
-        full = recv.permute(1, 0, 2, 3).reshape(sets, W * k, c).contiguous()
-        out = ops.newton_schulz(full, self._coeffs, eps, clobber_input=True)
-        back = out.view(sets, W, k, c).permute(1, 0, 2, 3).contiguous()
+        if dp_dim == 0:
+            full = recv.permute(1, 0, 2, 3).reshape(sets, W * k, c).contiguous()
+        else:
+            full = recv.permute(1, 2, 0, 3).reshape(sets, k, W * c).contiguous()
+        if tp_dim is not None:
+            out = self._ns_tp_gathered(full, tp_dim, eps)
+        else:
+            out = ops.newton_schulz(full, self._coeffs, eps, clobber_input=True)
+        if dp_dim == 0:
+            back = out.view(sets, W, k, c).permute(1, 0, 2, 3).contiguous()
+        else:
+            back = out.view(sets, k, W, c).permute(2, 0, 1, 3).contiguous()
         ret = torch.empty_like(back)
         dist.all_to_all_single(ret.view(W, -1), back.view(W, -1), group=self._pg)
         return torch.stack([ret[i % W, i // W] for i in range(n)])

@@ -91,13 +91,28 @@ def _apply_inv_lower_t(P: Tensor, Z: Tensor) -> Tensor:
     return P @ Z.mT
 
 
-def orthogonalize(P: Tensor, oversample: float = 1.25, generator: Optional[torch.Generator] = None) -> Tensor:
+def orthogonalize(P: Tensor, oversample: float = 1.25, generator: Optional[torch.Generator] = None,
+                  out_ptrs: Optional[Tensor] = None, nrep: int = 1) -> Optional[Tensor]:
+    """Orthonormal-column basis of every P[i] (see module doc).
+
+    With ``out_ptrs`` (CUDA, fp32, int64 device array of ``b * nrep``
+    addresses, entry ``i*nrep + j``) the result is not returned: the last
+    GEMM's epilogue stores matrix i to all ``nrep`` addresses, which may be
+    peer GPUs' memory (the all-gather of the orthonormal P fused into the
+    GEMM that produces it).
+    """
     assert P.ndim == 3, "Expected a batch of matrices"
     dtype = P.dtype
     Pf = P.float().contiguous()
     b, d, r = Pf.shape
+    assert out_ptrs is None or P.is_cuda, "out_ptrs needs CUDA tensors"
     if d <= r:
         Q, _ = torch.linalg.qr(Pf)
+        if out_ptrs is not None:
+            Qc = Q.float().contiguous()
+            for i in range(b):
+                ops.ext().symm_push(Qc[i], out_ptrs[i * nrep:(i + 1) * nrep])
+            return None
         return Q.to(dtype)
     k = sketch_size(r, oversample)
     S = torch.randn((b, k, d), device=P.device, dtype=torch.float32, generator=generator)
@@ -109,7 +124,11 @@ def orthogonalize(P: Tensor, oversample: float = 1.25, generator: Optional[torch
         Pf = _apply_inv_lower_t(Pf, tri_inv_lower(R1, upper=True))
         PP = ops.matmul(Pf.transpose(1, 2), Pf, symmetric=True)
         L2 = cholesky_lower(PP)
-        Pf = _apply_inv_lower_t(Pf, tri_inv_lower(L2))
+        Z2 = tri_inv_lower(L2)
+        if out_ptrs is not None:
+            ops.matmul_to_ptrs(Pf, Z2.transpose(1, 2), out_ptrs, r, torch.float32, nrep=nrep)
+            return None
+        Pf = _apply_inv_lower_t(Pf, Z2)
         return Pf.to(dtype)
     R1 = qr_r(SP)
     Pf = torch.linalg.solve_triangular(R1, Pf, upper=True, left=False)
@@ -155,13 +174,18 @@ def distributed_orthogonalize(P: DTensor, oversample: float = 1.25, shard_mesh_d
     SP = DTensor.from_local(SP_local, mesh, sp_pl, run_check=False)
     SP_single = SP.redistribute(placements=batch_sharded)
     R_local = qr_r(SP_single.to_local().float().contiguous())
-    R = DTensor.from_local(R_local, mesh, SP_single.placements, run_check=False).redistribute(placements=full_rep)
+    bsz = P.shape[0]
+    rr_shape, rr_stride = torch.Size((bsz, r, r)), (r * r, r, 1)
+    # explicit global shape: with fewer matrices than ranks some local batches are empty
+    R = DTensor.from_local(R_local, mesh, SP_single.placements, run_check=False, shape=rr_shape,
+                           stride=rr_stride).redistribute(placements=full_rep)
     P_local = _right_solve(P_local, R.to_local().contiguous())
     PP_local = ops.matmul(P_local.transpose(1, 2), P_local, symmetric=True) if P_local.is_cuda else P_local.mT @ P_local
     PP = DTensor.from_local(PP_local, mesh, sp_pl, run_check=False)
     PP_single = PP.redistribute(placements=batch_sharded)
     R2_local = cholesky_upper(PP_single.to_local().contiguous()).contiguous()
-    R2 = DTensor.from_local(R2_local, mesh, PP_single.placements, run_check=False).redistribute(placements=full_rep)
+    R2 = DTensor.from_local(R2_local, mesh, PP_single.placements, run_check=False, shape=rr_shape,
+                            stride=rr_stride).redistribute(placements=full_rep)
     P_local = _right_solve(P_local, R2.to_local().contiguous())
     return DTensor.from_local(P_local.to(dtype).contiguous(), mesh, orig, run_check=False, shape=P.shape,
                               stride=P.stride())

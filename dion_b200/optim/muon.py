@@ -105,6 +105,7 @@ class Muon(Optimizer):
         ns_coeffs=None,
         fsdp_mesh_dim: Optional[int] = None,
         world_mesh: Optional[DeviceMesh] = None,
+        tp_mesh: Optional[DeviceMesh] = None,
     ):
         if lr < 0.0:
             raise ValueError(f"Invalid learning rate: {lr}")
@@ -151,9 +152,14 @@ class Muon(Optimizer):
             raise TypeError(f"Invalid distributed_mesh type: {type(distributed_mesh)}")
         self._distributed_mesh = distributed_mesh
         self._ns_func = newton_schulz_func
+        self._p2p_cache: Dict[Tuple, Any] = {}
         self._coeffs = _resolve_coeffs(ns_coeffs)
         self.fsdp_mesh_dim = fsdp_mesh_dim
         self._world_mesh = world_mesh
+        # tensor-parallel sub-mesh: TP blocks are gathered at the matrix owner so
+        # Newton-Schulz sees the whole matrix (not its TP-local block)
+        self._tp_pg = tp_mesh.get_group() if isinstance(tp_mesh, DeviceMesh) and tp_mesh.size() > 1 else None
+        self._tp = tp_mesh.size() if self._tp_pg is not None else 1
 
     # ------------------------------------------------------------------ state
     def _state(self, p: Tensor, algo: str) -> Dict[str, Any]:
@@ -223,10 +229,14 @@ class Muon(Optimizer):
         if not isinstance(self._distributed_mesh, DeviceMesh):
             raise RuntimeError("Must create optimizer with DeviceMesh if using DTensor parameters.")
         shards = [(i, pl) for i, pl in enumerate(p.placements) if pl.is_shard() and p.device_mesh.size(i) > 1]
+        names = p.device_mesh.mesh_dim_names or ()
+        if "tp" in names:
+            shards = [(i, pl) for i, pl in shards if names[i] != "tp"]
         if not shards:
             return None
         if len(shards) > 1:
-            mesh_dim = self.fsdp_mesh_dim if self.fsdp_mesh_dim is not None else 0
+            mesh_dim = self.fsdp_mesh_dim if self.fsdp_mesh_dim is not None else (
+                names.index("dp_shard") if "dp_shard" in names else 0)
             match = [s for s in shards if s[0] == mesh_dim]
             if not match:
                 raise RuntimeError(f"Expected mesh dim {mesh_dim} to be the FSDP shard dim, got {shards}")
@@ -293,17 +303,22 @@ class Muon(Optimizer):
         X = to_local(params)
         G = to_local([p.grad for p in params])
         M = to_local([s["momentum"] for s in states])
-        full_shape = tuple(params[0].shape)
-        if len(full_shape) != 2:
+        if params[0].ndim != 2:
             raise NotImplementedError("FSDP Muon supports 2-D matrices")
-        if full_shape[shard_dim] % W:
+        if params[0].shape[shard_dim] % W:
             raise ValueError(
-                f"Shard dimension {shard_dim} size {full_shape[shard_dim]} is not divisible by world size {W}."
+                f"Shard dimension {shard_dim} size {params[0].shape[shard_dim]} is not divisible by world size {W}."
             )
         local_shape = tuple(X[0].shape)
+        # the matrix assembled over the FSDP mesh (TP-local when TP also shards it)
+        full_shape = tuple(s * W if d == shard_dim else s for d, s in enumerate(local_shape))
+        tp_dim = self._tp_dim(params[0])
         n = len(X)
         sets = (n + W - 1) // W
         dev = X[0].device
+        if tp_dim is None and shard_dim == 0 and self._ns_func is None and self._p2p_ok(full_shape, W, dev):
+            self._muon_fsdp_p2p(X, G, M, full_shape, local_shape, n, sets, mu, nesterov, eps, decay, adj_lr)
+            return
         # send[j, s] = my shard of matrix s*W + j (goes to rank j)
         send = torch.zeros((W, sets) + local_shape, device=dev, dtype=torch.bfloat16)
         Uv = [send[i % W, i // W].view(-1) for i in range(n)]
@@ -312,7 +327,10 @@ class Muon(Optimizer):
         dist.all_to_all_single(recv.view(W, -1), send.view(W, -1), group=self._pg)
         # recv[j, s] = shard j of matrix s*W + r  -> full matrices [sets, m, k]
         full = recv.movedim(0, 1 + shard_dim).reshape((sets,) + full_shape).contiguous()
-        O = self._ns(full, None, eps)
+        if tp_dim is not None:
+            O = self._ns_tp_gathered(full, tp_dim, eps)
+        else:
+            O = self._ns(full, None, eps)
         # split along shard_dim into W shards -> [W, sets, *local_shape]
         chunks = O.view(
             (sets,) + full_shape[:shard_dim] + (W, full_shape[shard_dim] // W) + full_shape[shard_dim + 1 :]
@@ -320,5 +338,77 @@ class Muon(Optimizer):
         ret = torch.empty_like(chunks)
         dist.all_to_all_single(ret.view(W, -1), chunks.view(W, -1), group=self._pg)
         # ret[j, s] = my shard of matrix s*W + j
+        upd = [ret[i % W, i // W] for i in range(n)]
+        ops.scaled_update_(X, upd, decay, [adj_lr] * n)
+
+    def _tp_dim(self, p: Tensor) -> Optional[int]:
+        """Tensor dim sharded over the TP mesh, if any."""
+        if self._tp_pg is None or not isinstance(p, DTensor):
+            return None
+        names = p.device_mesh.mesh_dim_names or ()
+        if "tp" not in names:
+            return None
+        pl = p.placements[names.index("tp")]
+        return pl.dim if pl.is_shard() else None
+
+    def _ns_tp_gathered(self, full: Tensor, tp_dim: int, eps: float) -> Tensor:
+        """All-gather the TP blocks of each owned matrix, orthogonalise the whole
+        matrix (every TP rank of the owner computes the same result), keep this
+        rank's block."""
+        T = self._tp
+        parts = torch.empty((T,) + tuple(full.shape), device=full.device, dtype=full.dtype)
+        dist.all_gather_into_tensor(parts.view(T, -1), full.reshape(1, -1), group=self._tp_pg)
+        whole = torch.cat(list(parts.unbind(0)), dim=1 + tp_dim).contiguous()
+        O = self._ns(whole, None, eps)
+        me = dist.get_rank(self._tp_pg)
+        return O.narrow(1 + tp_dim, me * full.shape[1 + tp_dim], full.shape[1 + tp_dim]).contiguous()
+
+    # ---- in-kernel all-to-all over symmetric peer memory
+    def _p2p_ok(self, full_shape, W: int, dev: torch.device) -> bool:
+        from ..parallel.symm import p2p_enabled
+
+        m, k = full_shape
+        return p2p_enabled(self._pg, dev) and m % 8 == 0 and k % 8 == 0 and (m // W) % 8 == 0
+
+    def _muon_fsdp_p2p(self, X, G, M, full_shape, local_shape, n, sets, mu, nesterov, eps, decay, adj_lr) -> None:
+        """Row-sharded FSDP Muon without NCCL (DION/muon.py:448-491 does two all_to_all calls).
+
+        Heap layout (bf16): gather [sets, m, k] (matrices this rank owns) then
+        ret [W (owner), sets, m/W, k] (this rank's row shards coming back).
+          1. the momentum kernel writes U for matrix i = s*W + j straight into
+             rows [me*m/W, (me+1)*m/W) of rank j's gather[s] (P2P stores);
+          2. device barrier;
+          3. Newton-Schulz on the full matrices; the last GEMM's epilogue
+             stores row shard j of matrix s into rank j's ret[me, s];
+          4. device barrier; 5. scaled weight update from ret.
+        """
+        from ..parallel.symm import heap_for
+
+        W, me = self._world, self._rank
+        m, k = full_shape
+        ms = m // W
+        mat = m * k * 2
+        gather_off, ret_off = 0, sets * mat
+        heap = heap_for(self._pg, 2 * sets * mat, "muon", X[0].device)
+        key = (heap.uid, sets, m, k)
+        cached = self._p2p_cache.get(key)
+        if cached is None:
+            # peer rows written only by this extension's kernels (the momentum kernel)
+            dst_views = [ops.ext().symm_view(heap.addr(i % W, gather_off + (i // W) * mat + me * ms * k * 2),
+                                             ms * k, 15) for i in range(n)]
+            ptrs = heap.ptr_tensor([heap.addr(j, ret_off + ((me * sets + s_) * ms * k) * 2)
+                                    for s_ in range(sets) for j in range(W)])
+            cached = (dst_views, ptrs)
+            self._p2p_cache[key] = cached
+        dst_views, ptrs = cached
+        full = heap.view(gather_off, (sets, m, k), torch.bfloat16)
+        for i in range(n + (-n) % W):
+            if i >= n and i % W == me:  # this rank owns an absent matrix of the last set
+                full[i // W].zero_()
+        ops.muon_momentum_([t.view(-1) for t in M], [g.reshape(-1) for g in G], dst_views, mu, nesterov, eps)
+        heap.barrier()
+        ops.newton_schulz(full, self._coeffs, eps, clobber_input=False, out_ptrs=ptrs, rows_per_ptr=ms)
+        heap.barrier()
+        ret = heap.view(ret_off, (W, sets, ms, k), torch.bfloat16)
         upd = [ret[i % W, i // W] for i in range(n)]
         ops.scaled_update_(X, upd, decay, [adj_lr] * n)

@@ -32,7 +32,22 @@ def apply_fsdp(
     layers = list(model.layers.values()) if isinstance(model.layers, nn.ModuleDict) else list(model.layers)
     for i, block in enumerate(layers):
         # the last block is resharded by the root right after backward anyway
-        fully_shard(block, mesh=mesh, mp_policy=mp,
+        fully_shard(block, mesh=mesh, mp_policy=mp, shard_placement_fn=_fsdp_placement,
                     reshard_after_forward=reshard_after_forward and i < len(layers) - 1)
-    fully_shard(model, mesh=mesh, mp_policy=mp, reshard_after_forward=reshard_after_forward)
+    fully_shard(model, mesh=mesh, mp_policy=mp, reshard_after_forward=reshard_after_forward,
+                shard_placement_fn=_fsdp_placement)
     return model
+
+
+def _fsdp_placement(param: nn.Parameter):
+    """FSDP shards dim 0, except for weights tensor parallelism already splits
+    along dim 0 (column-parallel): those are sharded along dim 1 so each
+    matrix has one mesh per dimension (no strided sharding), which is the
+    layout Dion's FSDP x TP update expects (ada_dion/optim/adadion_v2.py:572-575
+    rejects the strided form)."""
+    from torch.distributed.tensor import DTensor, Shard
+
+    if isinstance(param, DTensor) and param.ndim == 2:
+        if any(pl.is_shard() and pl.dim == 0 for pl in param.placements):
+            return Shard(1)
+    return Shard(0)

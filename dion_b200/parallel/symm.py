@@ -22,6 +22,7 @@ mapping needs that) and can be switched off with ``DION_B200_P2P=0``.
 """
 from __future__ import annotations
 
+import itertools
 import os
 from typing import Dict, List, Optional, Sequence, Tuple
 
@@ -34,6 +35,7 @@ from .. import ops
 __all__ = ["SymmetricHeap", "p2p_enabled", "heap_for"]
 
 _ALIGN = 256
+_UID = itertools.count()
 _SCALAR_TYPE = {torch.float32: 6, torch.bfloat16: 15, torch.int64: 4, torch.uint8: 0}
 
 
@@ -77,6 +79,7 @@ class SymmetricHeap:
         self._own = ptr
         self._flags = torch.tensor(self.bases, dtype=torch.int64).to(self.device)
         self._closed = False
+        self.uid = next(_UID)  # never reused, unlike id()
 
     # ------------------------------------------------------------ addressing
     def addr(self, rank: int, offset: int) -> int:

@@ -64,3 +64,48 @@ def test_trace_parser(tmp_path):
     assert r["nccl_allgather_count"] == 1 and abs(r["nccl_allgather_ms"] - 0.1) < 1e-9
     assert abs(r["nccl_reducescatter_ms"] - 0.25) < 1e-9 and abs(r["nccl_total_ms"] - 0.4) < 1e-9
     assert r["dion_b200_kernels_count"] == 1 and abs(r["library_kernels_ms"] - 0.3) < 1e-9
+
+
+def test_plots_write_svg(tmp_path):
+    from dion_b200.benchmarks import plots
+
+    runs = {"dion": {"tokens": [0, 1, 2], "val_loss": [3.0, 2.5, 2.2], "step": [1, 2, 3],
+                     "tokens_per_sec": [10.0, 11.0, 12.0], "num_gpus": [1, 2, 4], "fwd_ms": 5.0, "bwd_ms": 9.0,
+                     "opt_ms": 2.0, "nccl_ms": 1.0, "allreduce_bytes": 2**20, "allgather_bytes": 0,
+                     "reducescatter_bytes": 2**21, "allreduce_ms": 0.1, "allgather_ms": 0.2,
+                     "reducescatter_ms": 0.3, "comm_compute_ratio": [0.1, 0.2, 0.3]},
+            "muon": {"tokens": [0, 1, 2], "val_loss": [3.0, 2.6, 2.4], "step": [1, 2, 3],
+                     "tokens_per_sec": [9.0, 9.5, 9.0], "num_gpus": [1, 2, 4], "fwd_ms": 5.0, "bwd_ms": 9.0,
+                     "opt_ms": 3.0, "nccl_ms": 2.0, "allreduce_bytes": 0, "allgather_bytes": 2**20,
+                     "reducescatter_bytes": 2**20, "allreduce_ms": 0.0, "allgather_ms": 0.3,
+                     "reducescatter_ms": 0.3, "comm_compute_ratio": [0.2, 0.3, 0.5]}}
+    runs["dion"]["tokens_per_sec"] = [10.0, 19.0, 37.0]
+    runs["muon"]["tokens_per_sec"] = [9.0, 17.0, 30.0]
+    dd = {"step": [1, 2, 3], "rank_mean": [64, 64, 60], "residual_norm_mean": [1.0, 0.9, 0.8]}
+    d2 = {"step": [1, 2], "alpha": [0.25], "sparsity": [0.75, 0.75], "selected_frac_mean": [0.25, 0.25]}
+    ad = {"step": [1, 2], "rank_mean": [32, 40], "aerr_mean": [0.1, 0.08]}
+    out = plots.save_all_plots(str(tmp_path), runs=runs, dion_data=dd, dion2_data=d2, adadion_data=ad)
+    assert len(out) == 10
+    for p in out:
+        s = open(p).read()
+        assert s.startswith("<svg") and s.rstrip().endswith("</svg>")
+
+
+def test_logparse(tmp_path):
+    from dion_b200.benchmarks import logparse
+
+    log = tmp_path / "llama3_160m_dion.log"
+    lines = ["Optimizer: Dion"]
+    for s in (10, 20, 20, 30):
+        lines.append(f"[titan] 2026-01-01 00:00:{s:02d},000 - INFO - step: {s:5d}  loss: {5 - s / 10:8.4f}  "
+                     f"grad_norm:  1.2500  memory: 12.50GiB  tps: 1,234  tflops: 56.78  mfu: 12.34%")
+    log.write_text("\n".join(lines))
+    d = logparse.parse_log(str(log))
+    assert d["optimizer"] == "dion" and d["step"] == [10, 20, 30]
+    assert d["tps"] == [1234.0] * 3 and d["mfu"][0] == 12.34 and d["time_s"] == [0.0, 10.0, 20.0]
+    ours = tmp_path / "muon_run.log"
+    ours.write_text("step:    10  loss:   7.1234  grad_norm:  0.5000  memory:  3.00GiB  tps: 98,765  "
+                    "tflops: 400.50  mfu: 20.00%\n")
+    out = logparse.generate_plots([str(log), str(ours)], str(tmp_path / "plots"), tokens_per_step=4096)
+    assert any(p.endswith(".svg") for p in out)
+    assert "| muon_run | muon | 10 | 7.1234 | 98,765 |" in open(out[-1]).read()
