@@ -23,6 +23,7 @@ __all__ = [
     "ModelConfig",
     "TrainingConfig",
     "LRSchedulerConfig",
+    "ActivationCheckpointConfig",
     "ParallelismConfig",
     "CheckpointConfig",
     "MetricsConfig",
@@ -50,6 +51,12 @@ class TrainingConfig:
     dtype: str = "bfloat16"
     max_norm: float = 1.0
     seed: int = 0
+
+
+@dataclass
+class ActivationCheckpointConfig:
+    mode: str = "none"  # none | full | selective
+    selective_ac_option: str = "op"  # "op" or an integer N (every N-th block)
 
 
 @dataclass
@@ -109,6 +116,7 @@ class JobConfig:
     optimizer: HybridOptimizersContainer.Config = field(default_factory=HybridOptimizersContainer.Config)
     lr_scheduler: LRSchedulerConfig = field(default_factory=LRSchedulerConfig)
     training: TrainingConfig = field(default_factory=TrainingConfig)
+    activation_checkpoint: ActivationCheckpointConfig = field(default_factory=ActivationCheckpointConfig)
     parallelism: ParallelismConfig = field(default_factory=ParallelismConfig)
     checkpoint: CheckpointConfig = field(default_factory=CheckpointConfig)
     metrics: MetricsConfig = field(default_factory=MetricsConfig)

@@ -192,10 +192,20 @@ def llama3_1b_muon() -> JobConfig:
     return cfg
 
 
+def _8b(opt: Opt) -> JobConfig:
+    # 32K tokens per GPU: keep GEMM / attention outputs, recompute the
+    # elementwise work (~90 GB of activations fits next to the sharded state
+    # in 180 GB of HBM, so full recomputation is not needed)
+    cfg = _base("8B", opt, steps=10000, lbs=4, seq=8192)
+    cfg.activation_checkpoint.mode = "selective"
+    cfg.activation_checkpoint.selective_ac_option = "op"
+    return cfg
+
+
 @register
 def llama3_8b_dion() -> JobConfig:
     """8B decoder, seq 8192, 4 sequences per GPU, Dion rank 1/4 + AdamW, FSDP2."""
-    return _base("8B", _dion(), steps=10000, lbs=4, seq=8192)
+    return _8b(_dion())
 
 
 @register
@@ -205,4 +215,14 @@ def llama3_8b_adadion_v2() -> JobConfig:
     opt.rank_fraction_max = 0.25
     opt.init_rank_fraction = 0.25
     opt.rank_min = 4096 // 16
-    return _base("8B", opt, steps=10000, lbs=4, seq=8192)
+    return _8b(opt)
+
+
+@register
+def llama3_8b_dion2_fsdp_tp() -> JobConfig:
+    """8B decoder on a 2-D mesh: FSDP 4 x TP 2, Dion2 (fraction 1/4), seq 8192, 4 sequences per data-parallel rank."""
+    opt = _dion2()
+    cfg = _8b(opt)
+    cfg.parallelism.data_parallel_shard_degree = 4
+    cfg.parallelism.tensor_parallel_degree = 2
+    return cfg

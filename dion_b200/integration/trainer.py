@@ -47,6 +47,8 @@ class TrainerConfig:
     dp_shard: int = -1
     tp: int = 1
     use_fsdp: bool = True
+    ac_mode: str = "none"  # none | full | selective
+    ac_option: str = "op"
     optimizer: HybridOptimizersContainer.Config = field(default_factory=HybridOptimizersContainer.Config)
     log_freq: int = 10
 
@@ -135,6 +137,7 @@ class Trainer:
             model = Transformer(mcfg)
         gen = torch.Generator(device=device).manual_seed(cfg.seed)
         model.init_weights(cfg.init_mode, generator=gen)
+        model.set_activation_checkpointing(cfg.ac_mode, cfg.ac_option)
         tp_mesh = None
         if cfg.tp > 1:
             if self.mesh is None or "tp" not in self.mesh.mesh_dim_names:

@@ -130,19 +130,50 @@ class FeedForward(nn.Module):
         return self.w2(L.swiglu(self.w1(x), self.w3(x)))
 
 
+# ops whose outputs selective activation checkpointing keeps (everything else
+# -- norms, rotary, SwiGLU, residual adds -- is recomputed in the backward)
+_SAC_SAVE = None
+
+
+def _sac_context():
+    global _SAC_SAVE
+    from torch.utils.checkpoint import CheckpointPolicy, create_selective_checkpoint_contexts
+
+    if _SAC_SAVE is None:
+        aten = torch.ops.aten
+        names = ("mm", "addmm", "bmm", "_scaled_dot_product_flash_attention", "_scaled_dot_product_cudnn_attention",
+                 "_scaled_dot_product_efficient_attention")
+        _SAC_SAVE = {getattr(aten, n).default for n in names if hasattr(aten, n)}
+
+    def policy(ctx, op, *args, **kwargs):
+        return CheckpointPolicy.MUST_SAVE if op in _SAC_SAVE else CheckpointPolicy.PREFER_RECOMPUTE
+
+    return create_selective_checkpoint_contexts(policy)
+
+
 class TransformerBlock(nn.Module):
     def __init__(self, layer_id: int, cfg: Llama3Config):
         super().__init__()
         self.layer_id = layer_id
+        self.ac_mode = "none"  # "none" | "full" | "op" (see Transformer.set_activation_checkpointing)
         self.attention = Attention(cfg)
         self.feed_forward = FeedForward(cfg.dim, cfg.hidden_dim())
         self.attention_norm = L.RMSNorm(cfg.dim, cfg.norm_eps)
         self.ffn_norm = L.RMSNorm(cfg.dim, cfg.norm_eps)
         self.weight_init_std = 0.02 / (2 * (layer_id + 1)) ** 0.5 if cfg.depth_init else 0.02 / (2 * cfg.n_layers) ** 0.5
 
-    def forward(self, x: torch.Tensor, rope: torch.Tensor) -> torch.Tensor:
+    def _block(self, x: torch.Tensor, rope: torch.Tensor) -> torch.Tensor:
         h = x + self.attention(self.attention_norm(x), rope)
         return h + self.feed_forward(self.ffn_norm(h))
+
+    def forward(self, x: torch.Tensor, rope: torch.Tensor) -> torch.Tensor:
+        if self.ac_mode == "none" or not torch.is_grad_enabled():
+            return self._block(x, rope)
+        from torch.utils.checkpoint import checkpoint
+
+        if self.ac_mode == "op":
+            return checkpoint(self._block, x, rope, use_reentrant=False, context_fn=_sac_context)
+        return checkpoint(self._block, x, rope, use_reentrant=False)
 
 
 class Transformer(nn.Module):
@@ -154,6 +185,29 @@ class Transformer(nn.Module):
         self.norm = L.RMSNorm(cfg.dim, cfg.norm_eps)
         self.output = nn.Linear(cfg.dim, cfg.vocab_size, bias=False)
         self.register_buffer("rope_cache", L.rope_table(cfg.head_dim, cfg.max_seq_len, cfg.rope_theta), persistent=False)
+
+    def set_activation_checkpointing(self, mode: str = "none", option: str = "1") -> None:
+        """Activation checkpointing per transformer block (torchtitan's
+        ``activation_checkpoint.mode`` / ``selective_ac_option``):
+        ``full``: every block keeps only its input and recomputes the rest;
+        ``selective`` with option ``op``: every block keeps its GEMM and
+        attention outputs and recomputes the elementwise work;
+        ``selective`` with an integer N: every N-th block is fully checkpointed.
+        Checkpointing runs inside each block's forward, so parameter names
+        (and checkpoints / optimizer groups) do not change."""
+        blocks = list(self.layers.values())
+        for i, b in enumerate(blocks):
+            if mode == "none":
+                b.ac_mode = "none"
+            elif mode == "full":
+                b.ac_mode = "full"
+            elif mode == "selective" and option == "op":
+                b.ac_mode = "op"
+            elif mode == "selective":
+                every = int(option)
+                b.ac_mode = "full" if every > 0 and i % every == 0 else "none"
+            else:
+                raise ValueError(f"unknown activation checkpointing mode {mode!r}")
 
     @torch.no_grad()
     def init_weights(self, mode: str = "normal", std: float = 0.02, generator: Optional[torch.Generator] = None):

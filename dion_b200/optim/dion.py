@@ -46,6 +46,7 @@ from torch.optim.optimizer import Optimizer, ParamsT
 
 from .. import ops
 from ._utils import group_by_signature, scalar_update, to_local
+from ..utils.trace import phase
 from .linalg import orthogonalize
 
 try:
@@ -426,12 +427,16 @@ class Dion(Optimizer):
     def _dion_group(self, group: dict, params: List[Tensor]) -> None:
         for same in group_by_signature(params).values():
             cfg = self._get_dion_param_config(same[0])
+            shape = "x".join(str(d) for d in same[0].shape)
             if cfg.inner_shard_mesh_dim is not None:
-                self._dion_fsdp_tp(group, same, cfg)
+                with phase(f"dion/fsdp_tp/{shape}"):
+                    self._dion_fsdp_tp(group, same, cfg)
             elif cfg.outer_shard_mesh_dim is not None and self._outer_shard_mesh.size() > 1:
-                self._dion_sharded(group, same, cfg)
+                with phase(f"dion/sharded/{shape}"):
+                    self._dion_sharded(group, same, cfg)
             else:
-                self._dion_replicated(group, same, cfg)
+                with phase(f"dion/replicated/{shape}"):
+                    self._dion_replicated(group, same, cfg)
 
     # hooks overridden by the adaptive-rank subclass
     def _active_q(self, params, order, Qb):

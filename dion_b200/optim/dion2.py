@@ -35,6 +35,7 @@ from torch.distributed.tensor import DTensor
 from torch.optim.optimizer import Optimizer, ParamsT
 
 from .. import ops
+from ..utils.trace import phase
 from ._utils import group_by_signature, scalar_update, to_local
 from .muon import _ADJUST, _resolve_coeffs
 
@@ -113,7 +114,8 @@ class Dion2(Optimizer):
                 continue
             if algo in ("dion2", "dion", "muon"):
                 for same in group_by_signature(params).values():
-                    self._dion2_group(g, same)
+                    with phase("dion2/" + "x".join(str(d) for d in same[0].shape)):
+                        self._dion2_group(g, same)
             elif algo in ("adamw", "lion"):
                 scalar_update(algo, params, [p.grad for p in params], [self._state(p, algo) for p in params], g)
             else:

@@ -33,6 +33,7 @@ from torch.distributed.tensor import DTensor
 from torch.optim.optimizer import Optimizer, ParamsT
 
 from .. import ops
+from ..utils.trace import phase
 from ._utils import group_by_signature, scalar_update, to_local
 
 __all__ = ["Muon", "adjust_lr_spectral_norm", "adjust_lr_rms_norm", "adjust_lr_keller_muon"]
@@ -216,12 +217,16 @@ class Muon(Optimizer):
             adj_lr = adjust(lr, p0.shape)
             states = [self._state(p, "muon") for p in same]
             shard_dim = self._shard_dim(p0)
+            shape = "x".join(str(d) for d in p0.shape)
             if shard_dim is not None and self._world > 1:
-                self._muon_fsdp(same, states, shard_dim, mu, nesterov, eps, decay, adj_lr, group)
+                with phase(f"muon/fsdp/{shape}"):
+                    self._muon_fsdp(same, states, shard_dim, mu, nesterov, eps, decay, adj_lr, group)
             elif self._world > 1 and self._pg is not None:
-                self._muon_ddp(same, states, mu, nesterov, eps, decay, adj_lr, group)
+                with phase(f"muon/ddp/{shape}"):
+                    self._muon_ddp(same, states, mu, nesterov, eps, decay, adj_lr, group)
             else:
-                self._muon_local(same, states, mu, nesterov, eps, decay, adj_lr, group)
+                with phase(f"muon/local/{shape}"):
+                    self._muon_local(same, states, mu, nesterov, eps, decay, adj_lr, group)
 
     def _shard_dim(self, p: Tensor) -> Optional[int]:
         if not isinstance(p, DTensor):

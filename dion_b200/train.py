@@ -49,6 +49,8 @@ def trainer_config_from_job(job: JobConfig) -> TrainerConfig:
         tp=par.tensor_parallel_degree,
         optimizer=job.optimizer,
         log_freq=job.metrics.log_freq,
+        ac_mode=job.activation_checkpoint.mode,
+        ac_option=job.activation_checkpoint.selective_ac_option,
     )
 
 

@@ -109,3 +109,27 @@ def test_logparse(tmp_path):
     out = logparse.generate_plots([str(log), str(ours)], str(tmp_path / "plots"), tokens_per_step=4096)
     assert any(p.endswith(".svg") for p in out)
     assert "| muon_run | muon | 10 | 7.1234 | 98,765 |" in open(out[-1]).read()
+
+
+def test_optimizer_phases_show_in_profiler_trace(tmp_path):
+    """Optimizer phases are record_function events when a profiler runs, and
+    the trace parser reads the exported Chrome trace."""
+    import torch
+    from dion_b200.optim import Dion, Muon
+
+    ps = [torch.nn.Parameter(torch.randn(16, 8)) for _ in range(2)]
+    opts = [Muon(ps, lr=0.01), Dion([torch.nn.Parameter(torch.randn(16, 8))], lr=0.01)]
+    for o in opts:
+        for g in o.param_groups:
+            for p in g["params"]:
+                p.grad = torch.randn_like(p)
+    with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CPU]) as prof:
+        for o in opts:
+            o.step()
+    names = {e.name for e in prof.events()}
+    assert any(n.startswith("muon/local/") for n in names)
+    assert any(n.startswith("dion/replicated/") for n in names)
+    path = tmp_path / "trace.json"
+    prof.export_chrome_trace(str(path))
+    r = tiers.parse_profiler_trace(str(path))
+    assert r["nccl_total_ms"] == 0.0

@@ -140,3 +140,37 @@ def test_dcp_checkpoint_roundtrip(tmp_path):
     losses = train.main(args + ["--training.steps", "4", "--metrics.log_freq", "1"])
     assert len(losses) == 2
     assert (ck / "step-4").exists()
+
+
+@pytest.mark.parametrize("mode,option", [("full", "1"), ("selective", "op"), ("selective", "2")])
+def test_activation_checkpointing_matches(mode, option):
+    """Checkpointed blocks give the same loss and gradients as plain ones."""
+    from dion_b200.models.llama3 import Transformer, llama3_config
+
+    torch.manual_seed(0)
+    cfg = llama3_config("tiny", n_layers=3, vocab_size=256, max_seq_len=32)
+    a = Transformer(cfg)
+    a.init_weights("normal", generator=torch.Generator().manual_seed(1))
+    b = Transformer(cfg)
+    b.load_state_dict(a.state_dict())
+    b.set_activation_checkpointing(mode, option)
+    tok = torch.randint(0, 256, (2, 16))
+    lab = torch.randint(0, 256, (2, 16))
+    la = a(tok, labels=lab)
+    la.backward()
+    lb = b(tok, labels=lab)
+    lb.backward()
+    assert torch.allclose(la, lb, atol=1e-6)
+    for (n, pa), (_, pb) in zip(a.named_parameters(), b.named_parameters()):
+        assert torch.allclose(pa.grad, pb.grad, atol=1e-5, rtol=1e-4), n
+    assert [n for n, _ in a.named_parameters()] == [n for n, _ in b.named_parameters()]
+
+
+def test_registry_8b_configs_use_selective_ac():
+    from dion_b200.integration.config_registry import get_config
+
+    for name in ("llama3_8b_dion", "llama3_8b_adadion_v2", "llama3_8b_dion2_fsdp_tp"):
+        c = get_config(name)
+        assert c.activation_checkpoint.mode == "selective" and c.training.seq_len == 8192
+    c = get_config("llama3_8b_dion2_fsdp_tp")
+    assert c.parallelism.tensor_parallel_degree == 2 and c.parallelism.data_parallel_shard_degree == 4
