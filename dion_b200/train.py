@@ -54,13 +54,30 @@ def trainer_config_from_job(job: JobConfig) -> TrainerConfig:
     )
 
 
+def _load_config(module: Optional[str], name: str) -> JobConfig:
+    """Config ``name`` from this package's registry, or from ``module``'s
+    function of that name (so experiment modules can add configs)."""
+    if module in (None, "", "dion_b200.integration.config_registry", "ada_dion.integration.config_registry"):
+        return get_config(name)
+    import importlib
+
+    mod = importlib.import_module(module)
+    fn = getattr(mod, name, None)
+    if fn is None:
+        raise SystemExit(f"config {name!r} not found in module {module!r}")
+    return fn()
+
+
 def main(argv: Optional[List[str]] = None) -> List[float]:
     argv = list(sys.argv[1:] if argv is None else argv)
     p = argparse.ArgumentParser(add_help=True)
     p.add_argument("--config", required=True)
+    p.add_argument("--module", default=None,
+                   help="module whose config functions to use (torchtitan-style --module); "
+                        "default: dion_b200.integration.config_registry")
     p.add_argument("--job.config_file", dest="unused", default=None)
     known, rest = p.parse_known_args(argv)
-    job = get_config(known.config)
+    job = _load_config(known.module, known.config)
     leftover = apply_overrides(job, rest)
     if leftover:
         raise SystemExit(f"unrecognised arguments: {leftover}")

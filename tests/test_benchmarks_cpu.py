@@ -133,3 +133,15 @@ def test_optimizer_phases_show_in_profiler_trace(tmp_path):
     prof.export_chrome_trace(str(path))
     r = tiers.parse_profiler_trace(str(path))
     assert r["nccl_total_ms"] == 0.0
+
+
+def test_cifar10_benchmark_runs(tmp_path):
+    from dion_b200.benchmarks import cifar10
+
+    logs = cifar10.main(["--epochs", "1", "--batch-size", "32", "--train-size", "256", "--optimizers",
+                         "muon,dion_r03", "--log-freq", "2", "--outdir", str(tmp_path), "--data-dir",
+                         str(tmp_path / "none")])
+    assert set(logs) == {"muon", "dion_r03"}
+    for l in logs.values():
+        assert l["eval/val_acc"] and all(v == v for v in l["train_loss"])
+    assert (tmp_path / "results.json").exists() and (tmp_path / "cifar10.svg").exists()

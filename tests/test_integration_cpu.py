@@ -174,3 +174,28 @@ def test_registry_8b_configs_use_selective_ac():
         assert c.activation_checkpoint.mode == "selective" and c.training.seq_len == 8192
     c = get_config("llama3_8b_dion2_fsdp_tp")
     assert c.parallelism.tensor_parallel_degree == 2 and c.parallelism.data_parallel_shard_degree == 4
+
+
+def test_launch_scripts_are_valid_bash():
+    import glob
+    import subprocess
+
+    root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "dion_b200", "launch")
+    files = glob.glob(os.path.join(root, "*.sh")) + glob.glob(os.path.join(root, "slurm", "*"))
+    assert len(files) >= 8
+    for f in files:
+        r = subprocess.run(["bash", "-n", f], capture_output=True, text=True)
+        assert r.returncode == 0, (f, r.stderr)
+        text = open(f).read()
+        assert "torchtitan" not in text
+    single = open(os.path.join(root, "run_single_node.sh")).read()
+    assert "-m dion_b200.train" in single and "--parallelism.data_parallel_shard_degree" in single
+
+
+def test_train_module_flag():
+    from dion_b200.train import _load_config
+
+    a = _load_config(None, "llama3_debug_dion")
+    b = _load_config("ada_dion.integration.config_registry", "llama3_debug_dion")
+    c = _load_config("dion_b200.integration.config_registry", "llama3_debug_dion")
+    assert a.optimizer.name == b.optimizer.name == c.optimizer.name == "Dion"
