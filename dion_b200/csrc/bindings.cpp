@@ -52,6 +52,7 @@ void dion_momentum_add(const std::vector<at::Tensor>& M, const std::vector<at::T
 void dion_fixup(at::Tensor& P, at::Tensor& R, const at::Tensor& Q0, const at::Tensor& nz);
 void col_sumsq(const at::Tensor& R, at::Tensor& out);
 void col_normalize(const at::Tensor& R, const at::Tensor& sumsq, double eps, at::Tensor& Q);
+void effective_rank(const at::Tensor& sumsq, const at::Tensor& slots, const at::Tensor& ranks, at::Tensor& out);
 void cholesky_lower(at::Tensor& A, at::Tensor& info);
 void tri_inv_lower(const at::Tensor& S, at::Tensor& Z, bool upper);
 void qr_r(at::Tensor& A, at::Tensor& R);
@@ -98,6 +99,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dion_fixup", &bdion::dion_fixup);
   m.def("col_sumsq", &bdion::col_sumsq);
   m.def("col_normalize", &bdion::col_normalize);
+  m.def("effective_rank", &bdion::effective_rank);
   m.def("cholesky_lower", &bdion::cholesky_lower);
   m.def("tri_inv_lower", &bdion::tri_inv_lower);
   m.def("qr_r", &bdion::qr_r);

@@ -213,4 +213,64 @@ void col_normalize(const at::Tensor& R, const at::Tensor& sumsq, double eps, at:
   note_launch();
 }
 
+// ---------------------------------------------------------------------------
+// Adaptive-rank statistic (AdaDionV2): entropy effective rank of the column
+// norms of R over each matrix's active columns,
+//   s_i = sqrt(max(sumsq_i, 0)) + 1e-12 (i < r_b),  p_i = s_i / (sum s + 1e-12),
+//   erank_b = exp(-sum_i p_i log(p_i + 1e-12)).
+// One block per matrix; the result stays on the device (the host reads all
+// matrices of a shape group with one copy).
+namespace {
+__device__ __forceinline__ float block_sum256(float v, float* red) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x / 32, l = threadIdx.x % 32;
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = (threadIdx.x < blockDim.x / 32) ? red[threadIdx.x] : 0.f;
+  if (w == 0)
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+  __syncthreads();
+  if (threadIdx.x == 0) red[0] = t;
+  __syncthreads();
+  t = red[0];
+  __syncthreads();
+  return t;
+}
+
+__global__ void erank_kernel(const float* __restrict__ sumsq, int width, const int64_t* __restrict__ slots,
+                             const int* __restrict__ ranks, float* __restrict__ out) {
+  __shared__ float red[32];
+  const int m = blockIdx.x;
+  const float* row = sumsq + slots[m] * (int64_t)width;
+  const int r = min(ranks[m], width);
+  float s = 0.f;
+  for (int i = threadIdx.x; i < r; i += blockDim.x) s += sqrtf(fmaxf(row[i], 0.f)) + 1e-12f;
+  const float total = block_sum256(s, red) + 1e-12f;
+  float h = 0.f;
+  for (int i = threadIdx.x; i < r; i += blockDim.x) {
+    const float pr = (sqrtf(fmaxf(row[i], 0.f)) + 1e-12f) / total;
+    h -= pr * logf(pr + 1e-12f);
+  }
+  h = block_sum256(h, red);
+  if (threadIdx.x == 0) out[m] = expf(h);
+}
+}  // namespace
+
+// sumsq [b, width] fp32; slots [n] int64 (rows of sumsq); ranks [n] int32; out [n] fp32
+void effective_rank(const at::Tensor& sumsq, const at::Tensor& slots, const at::Tensor& ranks, at::Tensor& out) {
+  TORCH_CHECK(sumsq.dim() == 2 && sumsq.is_contiguous() && sumsq.scalar_type() == at::kFloat,
+              "dion_b200 effective_rank: sumsq must be a contiguous [b, width] fp32 tensor");
+  TORCH_CHECK(slots.scalar_type() == at::kLong && ranks.scalar_type() == at::kInt && out.scalar_type() == at::kFloat,
+              "dion_b200 effective_rank: slots int64, ranks int32, out fp32");
+  const int64_t n = slots.numel();
+  TORCH_CHECK(ranks.numel() == n && out.numel() == n, "dion_b200 effective_rank: sizes");
+  if (n == 0) return;
+  c10::cuda::CUDAGuard guard(sumsq.device());
+  erank_kernel<<<(unsigned)n, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      sumsq.data_ptr<float>(), (int)sumsq.size(1), slots.data_ptr<int64_t>(), ranks.data_ptr<int>(),
+      out.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  note_launch();
+}
+
 }  // namespace bdion

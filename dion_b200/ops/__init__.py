@@ -445,6 +445,22 @@ def col_sumsq(R: Tensor) -> Tensor:
     return out
 
 
+def effective_rank(sumsq: Tensor, slots: Tensor, ranks: Tensor) -> Tensor:
+    """Entropy effective rank of each selected row of ``sumsq`` ([b, width]
+    column sums of squares) over its first ``ranks[i]`` columns -> [n] fp32."""
+    if not sumsq.is_cuda:
+        rows = sumsq.index_select(0, slots.long()).clamp_min(0).sqrt()
+        width = rows.size(1)
+        active = torch.arange(width, device=rows.device).unsqueeze(0) < ranks.long().unsqueeze(1)
+        sig = torch.where(active, rows + 1e-12, torch.zeros_like(rows))
+        prob = sig / (sig.sum(dim=1, keepdim=True) + 1e-12)
+        ent = -(torch.where(active, prob * torch.log(prob + 1e-12), torch.zeros_like(prob))).sum(dim=1)
+        return torch.exp(ent)
+    out = torch.empty(slots.numel(), device=sumsq.device, dtype=torch.float32)
+    ext().effective_rank(sumsq.float().contiguous(), slots.long().contiguous(), ranks.int().contiguous(), out)
+    return out
+
+
 def col_normalize(R: Tensor, sumsq: Tensor, eps: float, out: Tensor) -> Tensor:
     """``out = R / (sqrt(sumsq) + eps)`` column-wise, written in ``out``'s dtype."""
     if not R.is_cuda:

@@ -31,6 +31,7 @@ from torch import Tensor
 from torch.distributed import ProcessGroup
 from torch.distributed.device_mesh import DeviceMesh
 
+from .. import ops
 from ._utils import to_local
 from .dion import Dion, DionMixedPrecisionConfig
 from .linalg import orthogonalize
@@ -166,15 +167,13 @@ class AdaDionV2(Dion):
         if ranks is None:
             return
         c = self._ada_config
-        slots = torch.tensor([order[i] for i in range(len(params))], device=sumsq.device)
-        rs = torch.tensor([ranks[order[i]] for i in range(len(params))], device=sumsq.device)
-        width = sumsq.shape[-1]
-        sig = sumsq.index_select(0, slots).clamp_min(0).sqrt()
-        active = torch.arange(width, device=sumsq.device).unsqueeze(0) < rs.unsqueeze(1)
-        sig = torch.where(active, sig + 1e-12, torch.zeros_like(sig))
-        prob = sig / (sig.sum(dim=1, keepdim=True) + 1e-12)
-        ent = -(torch.where(active, prob * torch.log(prob + 1e-12), torch.zeros_like(prob))).sum(dim=1)
-        eranks = torch.exp(ent).cpu().tolist()  # one device->host copy per shape group
+        slots = torch.tensor([order[i] for i in range(len(params))], dtype=torch.int64).to(sumsq.device,
+                                                                                            non_blocking=True)
+        rs = torch.tensor([ranks[order[i]] for i in range(len(params))], dtype=torch.int32).to(sumsq.device,
+                                                                                               non_blocking=True)
+        # entropy effective rank of the active column norms (one kernel), one
+        # device->host copy per shape group for the host-side rank schedule
+        eranks = ops.effective_rank(sumsq, slots, rs).cpu().tolist()
         for p, er in zip(params, eranks):
             st = self.state[p]
             r, r_cap = st["r"], st["r_cap"]

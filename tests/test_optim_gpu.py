@@ -53,3 +53,18 @@ def test_dion_cuda_vs_oracle(shape, dtype):
         else:
             # bf16 weights: the step is below bf16 resolution of X, compare at that resolution
             torch.testing.assert_close(p.detach().cpu().double(), Xr, rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.gpu
+def test_effective_rank_kernel_matches_torch():
+    from dion_b200 import ops
+
+    torch.manual_seed(0)
+    sumsq = torch.rand(12, 96, device="cuda") ** 3
+    sumsq[3, 5] = -1e-9  # rounding can leave tiny negatives: clamped
+    slots = torch.tensor([0, 3, 7, 11, 5], device="cuda")
+    ranks = torch.tensor([96, 40, 1, 64, 17], device="cuda", dtype=torch.int32)
+    got = ops.effective_rank(sumsq, slots, ranks)
+    ref = ops.effective_rank(sumsq.cpu().double(), slots.cpu(), ranks.cpu())
+    torch.testing.assert_close(got.cpu().double(), ref, rtol=1e-4, atol=1e-4)
+    assert abs(float(got[2]) - 1.0) < 1e-4  # one active column: effective rank 1
