@@ -81,6 +81,7 @@ __global__ void fixup_kernel(float* P, int64_t pn, float* R, const QT* Q0, int64
 
 // column sum of squares: R [b, rows, r] row-major -> partial [b, chunks, r]
 constexpr int kRowsPerChunk = 256;
+constexpr int kRowsPerChunk4 = 32;  // vector kernel: more blocks in flight
 __global__ void col_sumsq_kernel(const float* R, int rows, int r, float* partial, int chunks) {
   const int b = blockIdx.z, ch = blockIdx.y;
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
@@ -93,6 +94,67 @@ __global__ void col_sumsq_kernel(const float* R, int rows, int r, float* partial
     s += v * v;
   }
   partial[((int64_t)b * chunks + ch) * r + c] = s;
+}
+
+// 4 columns per thread (float4), 8 rows of loads in flight
+__global__ void col_sumsq4_kernel(const float* R, int rows, int r, float* partial, int chunks) {
+  const int b = blockIdx.z, ch = blockIdx.y;
+  const int c4 = blockIdx.x * blockDim.x + threadIdx.x;
+  const int r4 = r / 4;
+  if (c4 >= r4) return;
+  const float4* Rb = reinterpret_cast<const float4*>(R + (int64_t)b * rows * r) + c4;
+  const int r0 = ch * kRowsPerChunk4, r1 = min(rows, r0 + kRowsPerChunk4);
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+  int i = r0;
+  for (; i + 8 <= r1; i += 8) {
+    float4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = Rb[(int64_t)(i + u) * r4];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      s.x += v[u].x * v[u].x;
+      s.y += v[u].y * v[u].y;
+      s.z += v[u].z * v[u].z;
+      s.w += v[u].w * v[u].w;
+    }
+  }
+  for (; i < r1; ++i) {
+    const float4 v = Rb[(int64_t)i * r4];
+    s.x += v.x * v.x;
+    s.y += v.y * v.y;
+    s.z += v.z * v.z;
+    s.w += v.w * v.w;
+  }
+  reinterpret_cast<float4*>(partial + ((int64_t)b * chunks + ch) * r)[c4] = s;
+}
+
+// Q = R / (sqrt(sumsq) + eps): each thread owns 4 columns (one reciprocal
+// each) and walks kNormRows rows; Q rows 16-byte (fp32) / 8-byte (bf16) aligned
+constexpr int kNormRows = 32;
+template <typename QT>
+__global__ void col_normalize4_kernel(const float* R, const float* sumsq, int rows, int r, float eps, QT* Q,
+                                      int64_t q_bstride, int64_t q_ld) {
+  const int b = blockIdx.z;
+  const int r4 = r / 4;
+  const int c4 = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c4 >= r4) return;
+  const float4 ss = reinterpret_cast<const float4*>(sumsq + (int64_t)b * r)[c4];
+  const float i0 = 1.f / (sqrtf(ss.x) + eps), i1 = 1.f / (sqrtf(ss.y) + eps), i2 = 1.f / (sqrtf(ss.z) + eps),
+              i3 = 1.f / (sqrtf(ss.w) + eps);
+  const float4* Rb = reinterpret_cast<const float4*>(R + (int64_t)b * rows * r) + c4;
+  QT* Qb = Q + (int64_t)b * q_bstride + 4 * c4;
+  const int row0 = blockIdx.y * kNormRows, row1 = min(rows, row0 + kNormRows);
+#pragma unroll 4
+  for (int row = row0; row < row1; ++row) {
+    const float4 v = Rb[(int64_t)row * r4];
+    QT* q = Qb + (int64_t)row * q_ld;
+    if constexpr (sizeof(QT) == 4) {
+      *reinterpret_cast<float4*>(q) = make_float4(v.x * i0, v.y * i1, v.z * i2, v.w * i3);
+    } else {
+      __nv_bfloat162 h[2] = {__floats2bfloat162_rn(v.x * i0, v.y * i1), __floats2bfloat162_rn(v.z * i2, v.w * i3)};
+      *reinterpret_cast<uint2*>(q) = *reinterpret_cast<uint2*>(h);
+    }
+  }
 }
 
 __global__ void col_sumsq_finalize(const float* partial, int chunks, int r, int batch, float* out) {
@@ -181,11 +243,18 @@ void col_sumsq(const at::Tensor& R, at::Tensor& out) {
   TORCH_CHECK(R.dim() == 3 && R.is_contiguous() && R.scalar_type() == at::kFloat, "dion_b200 col_sumsq: [b,rows,r] fp32");
   c10::cuda::CUDAGuard guard(R.device());
   const int b = (int)R.size(0), rows = (int)R.size(1), r = (int)R.size(2);
-  const int chunks = (rows + kRowsPerChunk - 1) / kRowsPerChunk;
+  const bool vec4 = r % 4 == 0;
+  const int rows_per_chunk = vec4 ? kRowsPerChunk4 : kRowsPerChunk;
+  const int chunks = (rows + rows_per_chunk - 1) / rows_per_chunk;
   auto part = at::empty({b, chunks, r}, R.options());
   auto s = at::cuda::getCurrentCUDAStream();
-  dim3 grid((r + 127) / 128, chunks, b);
-  col_sumsq_kernel<<<grid, 128, 0, s>>>(R.data_ptr<float>(), rows, r, part.data_ptr<float>(), chunks);
+  if (vec4) {
+    dim3 grid((r / 4 + 127) / 128, chunks, b);
+    col_sumsq4_kernel<<<grid, 128, 0, s>>>(R.data_ptr<float>(), rows, r, part.data_ptr<float>(), chunks);
+  } else {
+    dim3 grid((r + 127) / 128, chunks, b);
+    col_sumsq_kernel<<<grid, 128, 0, s>>>(R.data_ptr<float>(), rows, r, part.data_ptr<float>(), chunks);
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   note_launch();
   const int64_t tot = (int64_t)b * r;
@@ -203,12 +272,27 @@ void col_normalize(const at::Tensor& R, const at::Tensor& sumsq, double eps, at:
   c10::cuda::CUDAGuard guard(R.device());
   const int b = (int)R.size(0), rows = (int)R.size(1), r = (int)R.size(2);
   const int64_t total = (int64_t)rows * r;
-  dim3 grid((unsigned)std::min<int64_t>((total + 255) / 256, 2048), 1, b);
   auto s = at::cuda::getCurrentCUDAStream();
-  DISPATCH_FB(Q.scalar_type(), QT, {
-    col_normalize_kernel<QT><<<grid, 256, 0, s>>>(R.data_ptr<float>(), sumsq.data_ptr<float>(), rows, r, (float)eps,
-                                                  reinterpret_cast<QT*>(Q.data_ptr()), Q.stride(0), Q.stride(1));
-  });
+  const int qsz = (int)Q.element_size();
+  const bool vec = r % 4 == 0 && reinterpret_cast<uintptr_t>(Q.data_ptr()) % (4 * qsz) == 0 &&
+                   (Q.stride(1) * qsz) % (4 * qsz) == 0 && (Q.stride(0) * qsz) % (4 * qsz) == 0 &&
+                   reinterpret_cast<uintptr_t>(R.data_ptr()) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(sumsq.data_ptr()) % 16 == 0;
+  if (vec) {
+    dim3 grid((unsigned)((r / 4 + 127) / 128), (unsigned)((rows + kNormRows - 1) / kNormRows), (unsigned)b);
+    DISPATCH_FB(Q.scalar_type(), QT, {
+      col_normalize4_kernel<QT><<<grid, 128, 0, s>>>(R.data_ptr<float>(), sumsq.data_ptr<float>(), rows, r,
+                                                     (float)eps, reinterpret_cast<QT*>(Q.data_ptr()), Q.stride(0),
+                                                     Q.stride(1));
+    });
+  } else {
+    dim3 grid((unsigned)std::min<int64_t>((total + 255) / 256, 2048), 1, b);
+    DISPATCH_FB(Q.scalar_type(), QT, {
+      col_normalize_kernel<QT><<<grid, 256, 0, s>>>(R.data_ptr<float>(), sumsq.data_ptr<float>(), rows, r,
+                                                    (float)eps, reinterpret_cast<QT*>(Q.data_ptr()), Q.stride(0),
+                                                    Q.stride(1));
+    });
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   note_launch();
 }

@@ -1,9 +1,13 @@
 // Small dense factorizations for Dion's orthogonalisation (fp32, batched,
-// one CTA of 1024 threads per matrix, blocked by 32-column panels):
+// blocked by 32-column panels; each matrix is handled by a thread-block
+// cluster of up to 8 CTAs sized so the batch covers the SMs -- the panel
+// work is repeated in every CTA of the cluster, the trailing update is split
+// across them, and a hardware cluster barrier separates block steps):
 //
 //   cholesky_lower : A = L L^T in place (lower triangle of row-major A)
 //   tri_inv_lower  : Z = L^-1 for a lower-triangular L (or L = U^T for an
 //                    upper-triangular input), written as a full lower matrix
+//                    (recursive doubling over batched fp32 GEMMs, below)
 //   qr_r           : Householder QR of a tall A (m x n, m >= n), R only
 //
 // Dion needs P R^-1 with R from a QR (randomised sketch) and from a Cholesky
@@ -30,7 +34,7 @@ namespace {
 constexpr int NB = 32;
 constexpr int LD = NB + 1;  // padded smem row
 constexpr int CT = 1024;
-constexpr int QR_CT = 512;  // Householder kernel: two trailing columns per thread, more registers each
+constexpr int QR_CT = 256;  // Householder kernel: 32 accumulators per trailing column, no register spills
 
 __device__ __forceinline__ float block_sum_1024(float v, float* red) {
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffff, v, o);
@@ -47,9 +51,22 @@ __device__ __forceinline__ float block_sum_1024(float v, float* red) {
 }
 
 // ------------------------------------------------------------ Cholesky
+// Barrier over every thread of every CTA of this thread-block cluster, with
+// release/acquire ordering of global-memory accesses at cluster scope (a
+// hardware barrier: no memory polling).
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Cluster of `nclus` CTAs per matrix: every CTA factors the diagonal block
+// and solves the panel itself (cheap, and it keeps panel data local), the
+// trailing-triangle tiles are split over the CTAs, and a cluster barrier
+// orders each block step's updates before the next step reads them.
 __global__ void __launch_bounds__(CT, 1) cholesky_lower_kernel(float* __restrict__ A_all, int r, int64_t bstride,
-                                                               int* __restrict__ info) {
-  float* A = A_all + (int64_t)blockIdx.x * bstride;
+                                                               int* __restrict__ info, int nclus) {
+  const int crank = (int)(blockIdx.x % nclus);
+  const int mat = (int)(blockIdx.x / nclus);
+  float* A = A_all + (int64_t)mat * bstride;
   extern __shared__ float sm[];
   float* sD = sm;            // NB x LD   diagonal block
   float* sP = sm + NB * LD;  // (r) x LD  current panel below the diagonal block
@@ -85,10 +102,6 @@ __global__ void __launch_bounds__(CT, 1) cholesky_lower_kernel(float* __restrict
       }
     }
     __syncthreads();
-    for (int e = threadIdx.x; e < kb * kb; e += CT) {
-      const int i = e / kb, j = e % kb;
-      if (j <= i) A[(int64_t)(k0 + i) * r + k0 + j] = sD[i * LD + j];
-    }
     const int rows = r - k0 - kb;
     for (int ii = threadIdx.x; ii < rows; ii += CT) {  // panel: x L_kk^T = a, one row per thread
       const int64_t base = (int64_t)(k0 + kb + ii) * r + k0;
@@ -107,16 +120,13 @@ __global__ void __launch_bounds__(CT, 1) cholesky_lower_kernel(float* __restrict
       }
 #pragma unroll
       for (int j = 0; j < NB; ++j)
-        if (j < kb) {
-          A[base + j] = x[j];
-          sP[ii * LD + j] = x[j];
-        }
+        if (j < kb) sP[ii * LD + j] = x[j];
     }
     __syncthreads();
-    // trailing update of the lower triangle, 4x4 tiles per thread
+    // trailing update of the lower triangle, 4x4 tiles per thread, tiles split over the cluster
     const int nt = (rows + 3) / 4;
     const int ntiles = nt * (nt + 1) / 2;
-    for (int tt = threadIdx.x; tt < ntiles; tt += CT) {
+    for (int tt = crank * CT + threadIdx.x; tt < ntiles; tt += nclus * CT) {
       int ti = (int)((sqrtf(8.f * (float)tt + 1.f) - 1.f) * 0.5f);
       while ((ti + 1) * (ti + 2) / 2 <= tt) ++ti;
       while (ti * (ti + 1) / 2 > tt) --ti;
@@ -143,9 +153,22 @@ __global__ void __launch_bounds__(CT, 1) cholesky_lower_kernel(float* __restrict
           if (i < rows && j <= i) A[(int64_t)(k0 + kb + i) * r + k0 + kb + j] -= acc[u][v];
         }
     }
+    cluster_sync_all();
+    // the factored block column goes back to A only now: every CTA has read
+    // this step's inputs, and later steps never read these columns
+    if (crank == 0) {
+      for (int e = threadIdx.x; e < kb * kb; e += CT) {
+        const int i = e / kb, j = e % kb;
+        if (j <= i) A[(int64_t)(k0 + i) * r + k0 + j] = sD[i * LD + j];
+      }
+      for (int64_t e = threadIdx.x; e < (int64_t)rows * kb; e += CT) {
+        const int ii = (int)(e / kb), j = (int)(e % kb);
+        A[(int64_t)(k0 + kb + ii) * r + k0 + j] = sP[ii * LD + j];
+      }
+    }
     __syncthreads();
   }
-  if (threadIdx.x == 0 && info != nullptr) info[blockIdx.x] = bad;
+  if (threadIdx.x == 0 && crank == 0 && info != nullptr) info[mat] = bad;
 }
 
 // ------------------------------------------------------------ triangular inverse
@@ -155,114 +178,144 @@ __device__ __forceinline__ float tri_get(const float* S, int r, int i, int j, in
   return upper ? S[(int64_t)j * r + i] : S[(int64_t)i * r + j];
 }
 
-__global__ void __launch_bounds__(CT, 1) tri_inv_lower_kernel(const float* __restrict__ S_all, float* __restrict__ Z_all,
-                                                              int r, int64_t bstride, int upper) {
-  const float* S = S_all + (int64_t)blockIdx.x * bstride;
-  float* Z = Z_all + (int64_t)blockIdx.x * bstride;
-  extern __shared__ float sm[];
-  float* sInv = sm;              // NB x LD  inverse of the diagonal block
-  float* sDiag = sm + NB * LD;   // NB x LD  the diagonal block of L
-  float* sRow = sm + 2 * NB * LD;  // NB x (r+1) row block of L left of the diagonal
-  const int ldr = r + 1;
-  for (int64_t e = threadIdx.x; e < (int64_t)r * r; e += CT) {
-    const int i = (int)(e / r), j = (int)(e % r);
-    if (j > i) Z[e] = 0.f;
+// ------------------------------------------------------------ triangular inverse by recursive doubling
+// L^-1 for lower-triangular L, level by level: all 32x32 diagonal blocks are
+// inverted independently, then blocks of size s are paired into 2s:
+//     [L11  0 ]^-1   [ Z11          0  ]
+//     [L21 L22]    = [ -Z22 L21 Z11  Z22 ],   Z21 = -Z22 (L21 Z11)
+// which is two batched fp32 GEMMs per level (log2(r/32) levels), every
+// pair of every matrix in parallel across the GPU.
+
+// one warp per 32x32 diagonal block: lane c solves L_jj x = e_c (forward substitution)
+__global__ void tri_inv_diag_kernel(const float* __restrict__ S_all, float* __restrict__ Z_all, int r,
+                                    int64_t bstride, int upper) {
+  const int mat = blockIdx.y;
+  const int blk = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int c = threadIdx.x % 32;
+  const int nblk = (r + NB - 1) / NB;
+  if (blk >= nblk) return;
+  const float* S = S_all + (int64_t)mat * bstride;
+  float* Z = Z_all + (int64_t)mat * bstride;
+  const int i0 = blk * NB, kb = min(NB, r - i0);
+  __shared__ float sD[4][NB][LD];
+  float (*D)[LD] = sD[threadIdx.x / 32];
+  for (int i = 0; i < NB; ++i) D[i][c] = (i < kb && c <= i) ? tri_get(S, r, i0 + i, i0 + c, upper) : 0.f;
+  __syncwarp();
+  float x[NB];
+#pragma unroll
+  for (int i = 0; i < NB; ++i) {
+    float s2 = (i == c) ? 1.f : 0.f;
+#pragma unroll
+    for (int t = 0; t < NB; ++t)
+      if (t < i) s2 -= D[i][t] * x[t];
+    x[i] = (i < kb && c < kb && i >= c) ? s2 / D[i][i] : 0.f;
   }
-  __syncthreads();
-  for (int i0 = 0; i0 < r; i0 += NB) {
-    const int kb = min(NB, r - i0);
-    // diagonal block of L into smem (sDiag), then its inverse by warp 0:
-    // lane c solves L_ii x = e_c from shared memory
-    for (int e = threadIdx.x; e < NB * NB; e += CT) {
-      const int i = e / NB, t = e % NB;
-      sDiag[i * LD + t] = (i < kb && t <= i) ? tri_get(S, r, i0 + i, i0 + t, upper) : 0.f;
+  // row i0+i of Z: x[i] in column i0+c; zero the rest of the row band above the diagonal
+  if (c < kb) {
+#pragma unroll
+    for (int i = 0; i < NB; ++i)
+      if (i < kb) Z[(int64_t)(i0 + i) * r + i0 + c] = x[i];
+  }
+  for (int i = 0; i < kb; ++i)
+    for (int j = i0 + NB + c; j < r; j += 32) Z[(int64_t)(i0 + i) * r + j] = 0.f;
+}
+
+// C[z] = alpha * A[z] @ B[z] (M x K @ K x N), fp32 FMA, 64x64 tiles, 4x4 per thread.
+// Operand z = (matrix b, pair p): base + b*bstride + p*pstride + off, element
+// (i, j) at i*rs + j*cs (any strides: covers transposed views).
+struct Opnd {
+  const float* base;
+  int64_t bstride, pstride, off, rs, cs;
+  __device__ __forceinline__ const float* at(int b, int p) const { return base + b * bstride + p * pstride + off; }
+};
+
+__global__ void __launch_bounds__(256) sgemm_pairs_kernel(Opnd A, Opnd B, float* Cbase, int64_t c_bstride,
+                                                          int64_t c_pstride, int64_t c_off, int64_t c_rs, int M,
+                                                          int N, int K, int pairs, float alpha) {
+  const int z = blockIdx.z;
+  const int b = z / pairs, p = z % pairs;
+  const float* Ap = A.at(b, p);
+  const float* Bp = B.at(b, p);
+  float* Cp = Cbase + b * c_bstride + p * c_pstride + c_off;
+  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  __shared__ float As[16][64 + 4];
+  __shared__ float Bs[16][64 + 4];
+  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < K; k0 += 16) {
+    for (int e = threadIdx.x; e < 16 * 64; e += 256) {
+      const int kk = e / 64, mm = e % 64;
+      const int gi = m0 + mm, gk = k0 + kk;
+      As[kk][mm] = (gi < M && gk < K) ? Ap[gi * A.rs + gk * A.cs] : 0.f;
+      const int gn = n0 + mm;
+      Bs[kk][mm] = (gk < K && gn < N) ? Bp[gk * B.rs + gn * B.cs] : 0.f;
     }
     __syncthreads();
-    if (threadIdx.x < 32) {
-      const int c = threadIdx.x;
-      float x[NB];
 #pragma unroll
-      for (int i = 0; i < NB; ++i) {
-        float s = (i == c) ? 1.f : 0.f;
+    for (int kk = 0; kk < 16; ++kk) {
+      float a[4], bb[4];
 #pragma unroll
-        for (int t = 0; t < NB; ++t)
-          if (t < i) s -= sDiag[i * LD + t] * x[t];
-        x[i] = (i < kb && c < kb && i >= c) ? s / sDiag[i * LD + i] : 0.f;
+      for (int u = 0; u < 4; ++u) {
+        a[u] = As[kk][ty * 4 + u];
+        bb[u] = Bs[kk][tx * 4 + u];
       }
 #pragma unroll
-      for (int i = 0; i < NB; ++i) sInv[i * LD + c] = x[i];
-    }
-    // the row block of L left of the diagonal
-    for (int e = threadIdx.x; e < kb * i0; e += CT) {
-      const int a = e / i0, t = e % i0;
-      sRow[a * ldr + t] = tri_get(S, r, i0 + a, t, upper);
-    }
-    __syncthreads();
-    for (int e = threadIdx.x; e < kb * kb; e += CT) {
-      const int a = e / kb, b = e % kb;
-      if (b <= a) Z[(int64_t)(i0 + a) * r + i0 + b] = sInv[a * LD + b];
-    }
-    // off-diagonal: Z[i-block, c] = -Zii * (L[i-block, 0:i0] Z[0:i0, c]) for c < i0
-    for (int c = threadIdx.x; c < i0; c += CT) {
-      float s[NB];
+      for (int u = 0; u < 4; ++u)
 #pragma unroll
-      for (int a = 0; a < NB; ++a) s[a] = 0.f;
-      int t = c;
-      for (; t + 8 <= i0; t += 8) {  // 8 independent loads in flight
-        float z[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) z[u] = Z[(int64_t)(t + u) * r + c];
-#pragma unroll
-        for (int u = 0; u < 8; ++u)
-#pragma unroll
-          for (int a = 0; a < NB; ++a) s[a] += sRow[a * ldr + t + u] * z[u];
-      }
-      for (; t < i0; ++t) {
-        const float z = Z[(int64_t)t * r + c];
-#pragma unroll
-        for (int a = 0; a < NB; ++a) s[a] += sRow[a * ldr + t] * z;
-      }
-#pragma unroll
-      for (int a = 0; a < NB; ++a) {
-        if (a < kb) {
-          float o = 0.f;
-#pragma unroll
-          for (int b = 0; b < NB; ++b)
-            if (b <= a) o += sInv[a * LD + b] * s[b];
-          Z[(int64_t)(i0 + a) * r + c] = -o;
-        }
-      }
+        for (int v = 0; v < 4; ++v) acc[u][v] += a[u] * bb[v];
     }
     __syncthreads();
   }
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      const int gi = m0 + ty * 4 + u, gj = n0 + tx * 4 + v;
+      if (gi < M && gj < N) Cp[gi * c_rs + gj] = alpha * acc[u][v];
+    }
 }
 
 // ------------------------------------------------------------ Householder QR (R only)
+// One thread-block cluster of `nclus` CTAs per matrix (cluster dims set at
+// launch). Every CTA factors the current 32-column panel itself (read from
+// global memory, so no panel data crosses CTAs) and applies the block
+// reflector to the trailing column blocks it owns (block jb belongs to CTA
+// jb % nclus); a cluster barrier (release/acquire) after each panel makes
+// the owners' updated columns visible before the next panel is read. With
+// nclus = 1 this is the single-CTA algorithm.
+constexpr int QLD = NB + 4;  // panel row stride: 16-byte rows for vector reads of V
+
 __global__ void __launch_bounds__(QR_CT, 1) qr_r_kernel(float* __restrict__ A_all, int m, int n, int64_t bstride,
-                                                     float* __restrict__ R_all, int64_t rstride) {
-  float* A = A_all + (int64_t)blockIdx.x * bstride;
-  float* R = R_all + (int64_t)blockIdx.x * rstride;
-  extern __shared__ float sm[];
-  float* sV = sm;                 // rows x LD : the panel, then its Householder vectors
-  float* sT = sV + (int64_t)m * LD;  // NB x LD : WY block reflector T
-  float* red = sT + NB * LD;      // 40 floats for reductions
-  float* sTau = red + 40;         // NB
-  float* sBeta = sTau + NB;       // NB
-  for (int64_t e = threadIdx.x; e < (int64_t)n * n; e += QR_CT) R[e] = 0.f;
+                                                     float* __restrict__ R_all, int64_t rstride, int nclus) {
+  const int crank = (int)(blockIdx.x % nclus);
+  const int mat = (int)(blockIdx.x / nclus);
+  float* A = A_all + (int64_t)mat * bstride;
+  float* R = R_all + (int64_t)mat * rstride;
+  extern __shared__ __align__(16) float sm[];
+  float* sV = sm;                     // rows x QLD : the panel, then its Householder vectors
+  float* sT = sV + (int64_t)m * QLD;  // NB x LD : WY block reflector T
+  float* red = sT + NB * LD;          // 40 floats for reductions
+  float* sTau = red + 40;             // NB
+  float* sBeta = sTau + NB;           // NB
+  // strictly-lower part of R is zero; everything else is written by the panel
+  // loop (no overlap, so no ordering with the other CTAs is needed)
+  for (int64_t e = (int64_t)crank * QR_CT + threadIdx.x; e < (int64_t)n * n; e += (int64_t)nclus * QR_CT)
+    if (e % n < e / n) R[e] = 0.f;
+  const int nblk = (n + NB - 1) / NB;
   for (int k0 = 0; k0 < n; k0 += NB) {
     const int kb = min(NB, n - k0);
     const int rows = m - k0;
     for (int64_t e = threadIdx.x; e < (int64_t)rows * NB; e += QR_CT) {
       const int i = (int)(e / NB), j = (int)(e % NB);
-      sV[i * LD + j] = j < kb ? A[(int64_t)(k0 + i) * n + k0 + j] : 0.f;
+      sV[i * QLD + j] = j < kb ? A[(int64_t)(k0 + i) * n + k0 + j] : 0.f;
     }
     __syncthreads();
     // unblocked Householder on the panel
     for (int j = 0; j < kb; ++j) {
       float ss = 0.f;
-      for (int i = j + 1 + threadIdx.x; i < rows; i += QR_CT) ss += sV[i * LD + j] * sV[i * LD + j];
+      for (int i = j + 1 + threadIdx.x; i < rows; i += QR_CT) ss += sV[i * QLD + j] * sV[i * QLD + j];
       const float sigma = block_sum_1024(ss, red);
-      const float x0 = sV[j * LD + j];
+      const float x0 = sV[j * QLD + j];
       float beta, tau, scale;
       if (sigma == 0.f) {
         beta = x0;
@@ -274,30 +327,32 @@ __global__ void __launch_bounds__(QR_CT, 1) qr_r_kernel(float* __restrict__ A_al
         tau = (beta - x0) / beta;
         scale = 1.f / (x0 - beta);
       }
-      for (int i = j + 1 + threadIdx.x; i < rows; i += QR_CT) sV[i * LD + j] *= scale;
+      for (int i = j + 1 + threadIdx.x; i < rows; i += QR_CT) sV[i * QLD + j] *= scale;
       __syncthreads();
       if (threadIdx.x == 0) {
         sTau[j] = tau;
         sBeta[j] = beta;
-        sV[j * LD + j] = 1.f;
+        sV[j * QLD + j] = 1.f;
       }
       __syncthreads();
       // apply (I - tau v v^T) to panel columns j+1..kb-1: one warp per column
       const int w = threadIdx.x / 32, l = threadIdx.x % 32;
       for (int c = j + 1 + w; c < kb; c += QR_CT / 32) {
         float d = 0.f;
-        for (int i = j + l; i < rows; i += 32) d += sV[i * LD + j] * sV[i * LD + c];
+        for (int i = j + l; i < rows; i += 32) d += sV[i * QLD + j] * sV[i * QLD + c];
         for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffff, d, o);
         const float f = tau * d;
-        for (int i = j + l; i < rows; i += 32) sV[i * LD + c] -= f * sV[i * LD + j];
+        for (int i = j + l; i < rows; i += 32) sV[i * QLD + c] -= f * sV[i * QLD + j];
       }
       __syncthreads();
     }
-    // R block of this panel (upper part of the factored panel; diagonal = beta)
-    for (int e = threadIdx.x; e < kb * kb; e += QR_CT) {
-      const int i = e / kb, j = e % kb;
-      if (j > i) R[(int64_t)(k0 + i) * n + k0 + j] = sV[i * LD + j];
-      if (j == i) R[(int64_t)(k0 + i) * n + k0 + j] = sBeta[i];
+    // R block of this panel (upper part of the factored panel; diagonal = beta): panel owner only
+    if ((k0 / NB) % nclus == crank) {
+      for (int e = threadIdx.x; e < kb * kb; e += QR_CT) {
+        const int i = e / kb, j = e % kb;
+        if (j > i) R[(int64_t)(k0 + i) * n + k0 + j] = sV[i * QLD + j];
+        if (j == i) R[(int64_t)(k0 + i) * n + k0 + j] = sBeta[i];
+      }
     }
     // T of the compact WY form: H_0 ... H_{kb-1} = I - V T V^T
     {
@@ -307,8 +362,8 @@ __global__ void __launch_bounds__(QR_CT, 1) qr_r_kernel(float* __restrict__ A_al
         if (a < b) {
           float d = 0.f;
           for (int i = b + l; i < rows; i += 32) {
-            const float va = (i == a) ? 1.f : (i > a ? sV[i * LD + a] : 0.f);
-            d += va * sV[i * LD + b];
+            const float va = (i == a) ? 1.f : (i > a ? sV[i * QLD + a] : 0.f);
+            d += va * sV[i * QLD + b];
           }
           for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffff, d, o);
           if (l == 0) sT[a * LD + b] = d;
@@ -320,9 +375,9 @@ __global__ void __launch_bounds__(QR_CT, 1) qr_r_kernel(float* __restrict__ A_al
         for (int j = 0; j < kb; ++j) {
           for (int a = 0; a < j; ++a) tmp[a] = sT[a * LD + j];
           for (int a = 0; a < j; ++a) {
-            float s = 0.f;
-            for (int b = a; b < j; ++b) s += sT[a * LD + b] * tmp[b];
-            sT[a * LD + j] = -sTau[j] * s;
+            float s2 = 0.f;
+            for (int b = a; b < j; ++b) s2 += sT[a * LD + b] * tmp[b];
+            sT[a * LD + j] = -sTau[j] * s2;
           }
           sT[j * LD + j] = sTau[j];
           for (int a = j + 1; a < NB; ++a) sT[a * LD + j] = 0.f;
@@ -330,10 +385,13 @@ __global__ void __launch_bounds__(QR_CT, 1) qr_r_kernel(float* __restrict__ A_al
       }
       __syncthreads();
     }
-    // trailing columns: C -= V (T^T (V^T C)), one column per thread
-    const int nc = n - k0 - kb;
-    for (int c = threadIdx.x; c < nc; c += QR_CT) {
-      const int col = k0 + kb + c;
+    // trailing columns this CTA owns: C -= V (T^T (V^T C)), one column per thread
+    const int jb0 = k0 / NB + 1;
+    const int jfirst = jb0 + ((crank - jb0 % nclus) % nclus + nclus) % nclus;
+    const int owned = jfirst < nblk ? (nblk - 1 - jfirst) / nclus + 1 : 0;
+    for (int t = threadIdx.x; t < owned * NB; t += QR_CT) {
+      const int col = (jfirst + (t / NB) * nclus) * NB + t % NB;
+      if (col >= n) continue;
       float wv[NB];
 #pragma unroll
       for (int a = 0; a < NB; ++a) wv[a] = 0.f;
@@ -344,25 +402,33 @@ __global__ void __launch_bounds__(QR_CT, 1) qr_r_kernel(float* __restrict__ A_al
         const float cv = Ac[(int64_t)i * n];
 #pragma unroll
         for (int a = 0; a < NB; ++a) {
-          const float va = (i == a) ? 1.f : (i > a ? sV[i * LD + a] : 0.f);
+          const float va = (i == a) ? 1.f : (i > a ? sV[i * QLD + a] : 0.f);
           wv[a] += va * cv;
         }
       }
-      // dense rows: 8 independent loads in flight per step
+      // dense rows: 8 independent loads in flight, V rows read as float4 broadcasts
       int i = ktri;
       for (; i + 8 <= rows; i += 8) {
         float cv[8];
 #pragma unroll
         for (int u = 0; u < 8; ++u) cv[u] = Ac[(int64_t)(i + u) * n];
 #pragma unroll
-        for (int u = 0; u < 8; ++u)
+        for (int u = 0; u < 8; ++u) {
+          const float4* vr = reinterpret_cast<const float4*>(sV + (i + u) * QLD);
 #pragma unroll
-          for (int a = 0; a < NB; ++a) wv[a] += sV[(i + u) * LD + a] * cv[u];
+          for (int a4 = 0; a4 < NB / 4; ++a4) {
+            const float4 v4 = vr[a4];
+            wv[4 * a4 + 0] += v4.x * cv[u];
+            wv[4 * a4 + 1] += v4.y * cv[u];
+            wv[4 * a4 + 2] += v4.z * cv[u];
+            wv[4 * a4 + 3] += v4.w * cv[u];
+          }
+        }
       }
       for (; i < rows; ++i) {
         const float cv = Ac[(int64_t)i * n];
 #pragma unroll
-        for (int a = 0; a < NB; ++a) wv[a] += sV[i * LD + a] * cv;
+        for (int a = 0; a < NB; ++a) wv[a] += sV[i * QLD + a] * cv;
       }
       // wv <- T^T wv in place (row a only needs entries b <= a, so go downwards)
 #pragma unroll
@@ -378,7 +444,7 @@ __global__ void __launch_bounds__(QR_CT, 1) qr_r_kernel(float* __restrict__ A_al
         float sacc = 0.f;
 #pragma unroll
         for (int a = 0; a < NB; ++a) {
-          const float va = (i2 == a) ? 1.f : (i2 > a ? sV[i2 * LD + a] : 0.f);
+          const float va = (i2 == a) ? 1.f : (i2 > a ? sV[i2 * QLD + a] : 0.f);
           sacc += va * wv[a];
         }
         const float nv = Ac[(int64_t)i2 * n] - sacc;
@@ -392,9 +458,13 @@ __global__ void __launch_bounds__(QR_CT, 1) qr_r_kernel(float* __restrict__ A_al
         for (int u = 0; u < 8; ++u) cv[u] = Ac[(int64_t)(i + u) * n];
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
+          const float4* vr = reinterpret_cast<const float4*>(sV + (i + u) * QLD);
           float sacc = 0.f;
 #pragma unroll
-          for (int a = 0; a < NB; ++a) sacc += sV[(i + u) * LD + a] * wv[a];
+          for (int a4 = 0; a4 < NB / 4; ++a4) {
+            const float4 v4 = vr[a4];
+            sacc += v4.x * wv[4 * a4] + v4.y * wv[4 * a4 + 1] + v4.z * wv[4 * a4 + 2] + v4.w * wv[4 * a4 + 3];
+          }
           sv8[u] = sacc;
         }
 #pragma unroll
@@ -403,15 +473,47 @@ __global__ void __launch_bounds__(QR_CT, 1) qr_r_kernel(float* __restrict__ A_al
       for (; i < rows; ++i) {
         float sacc = 0.f;
 #pragma unroll
-        for (int a = 0; a < NB; ++a) sacc += sV[i * LD + a] * wv[a];
+        for (int a = 0; a < NB; ++a) sacc += sV[i * QLD + a] * wv[a];
         Ac[(int64_t)i * n] -= sacc;
       }
     }
-    __syncthreads();
+    // owners' updated columns -> visible to every CTA of the cluster before the next panel
+    cluster_sync_all();
   }
 }
 
 }  // namespace
+
+// CTAs per matrix for the clustered kernels: enough to cover the SMs, at
+// most 8 (the portable cluster size), 1 when the batch alone fills the GPU.
+int cluster_size_for(int batch) {
+  int sms = 0, dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int nclus = 1;
+  while (nclus < 8 && batch * nclus * 2 <= sms) nclus *= 2;
+  return nclus;
+}
+
+template <typename Kern, typename... Args>
+void launch_clustered(Kern kern, int batch, int threads, size_t smem, Args... args) {
+  const int nclus = cluster_size_for(batch);
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(batch * nclus));
+  cfg.blockDim = dim3((unsigned)threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = at::cuda::getCurrentCUDAStream();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)nclus;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, args..., nclus));
+  note_launch();
+}
 
 // A: [b, r, r] fp32 contiguous, overwritten with L in its lower triangle.
 void cholesky_lower(at::Tensor& A, at::Tensor& info) {
@@ -421,11 +523,8 @@ void cholesky_lower(at::Tensor& A, at::Tensor& info) {
   const size_t smem = (size_t)(NB * LD + (size_t)r * LD) * sizeof(float);
   TORCH_CHECK(smem <= 227 * 1024, "dion_b200 cholesky: r too large for the single-CTA kernel");
   c10::cuda::CUDAGuard guard(A.device());
-  cudaFuncSetAttribute(cholesky_lower_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  cholesky_lower_kernel<<<b, CT, smem, at::cuda::getCurrentCUDAStream()>>>(A.data_ptr<float>(), r, (int64_t)r * r,
-                                                                            info.data_ptr<int>());
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
-  note_launch();
+  launch_clustered(cholesky_lower_kernel, b, CT, smem, A.data_ptr<float>(), r, (int64_t)r * r,
+                   info.data_ptr<int>());
 }
 
 // S: [b, r, r] fp32 (lower, or upper if `upper`); Z: [b, r, r] = inv(L) lower.
@@ -433,29 +532,72 @@ void tri_inv_lower(const at::Tensor& S, at::Tensor& Z, bool upper) {
   TORCH_CHECK(S.dim() == 3 && S.is_contiguous() && Z.is_contiguous() && S.scalar_type() == at::kFloat,
               "dion_b200 tri_inv: contiguous [b, r, r] fp32");
   const int b = (int)S.size(0), r = (int)S.size(1);
-  const size_t smem = (size_t)(2 * NB * LD + (size_t)NB * (r + 1)) * sizeof(float);
-  TORCH_CHECK(smem <= 227 * 1024, "dion_b200 tri_inv: r too large");
   c10::cuda::CUDAGuard guard(S.device());
-  cudaFuncSetAttribute(tri_inv_lower_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  tri_inv_lower_kernel<<<b, CT, smem, at::cuda::getCurrentCUDAStream()>>>(S.data_ptr<float>(), Z.data_ptr<float>(),
-                                                                           r, (int64_t)r * r, upper ? 1 : 0);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const int nblk = (r + NB - 1) / NB;
+  const int64_t bs = (int64_t)r * r;
+  tri_inv_diag_kernel<<<dim3((unsigned)((nblk + 3) / 4), (unsigned)b), 128, 0, stream>>>(
+      S.data_ptr<float>(), Z.data_ptr<float>(), r, bs, upper ? 1 : 0);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   note_launch();
+  // scratch for T = L21 Z11 of every pair of every matrix at the current level
+  // (per level: pairs x s2 x s <= r x r per matrix)
+  at::Tensor T = at::empty({(int64_t)b * r * r}, S.options());
+  const float* Sp = S.data_ptr<float>();
+  float* Zp = Z.data_ptr<float>();
+  for (int s = NB; s < r; s *= 2) {
+    const int pairs = (r - s + 2 * s - 1) / (2 * s);  // pairs whose L22 block exists (may be partial)
+    // partial last pair: L22 rows [2ks+s, min(r, 2ks+2s)); sizes differ only for the last pair,
+    // so launch full pairs and the ragged last pair separately
+    const int full = (r / (2 * s));
+    for (int part = 0; part < 2; ++part) {
+      const int np = part == 0 ? full : pairs - full;
+      if (np <= 0) continue;
+      const int p0 = part == 0 ? 0 : full;
+      const int s2 = part == 0 ? s : r - (p0 * 2 * s + s);  // rows of L22 / Z22
+      const int64_t pstr = (int64_t)2 * s * r + 2 * s;       // next pair: 2s rows and 2s columns on
+      const int64_t o0 = (int64_t)p0 * pstr;
+      // L21 (s2 x s): rows 2ks+s.., columns 2ks..; for an upper input L = S^T
+      Opnd L21{Sp, bs, pstr, 0, 0, 0};
+      if (!upper) {
+        L21.off = o0 + (int64_t)s * r;
+        L21.rs = r;
+        L21.cs = 1;
+      } else {
+        L21.off = o0 + s;
+        L21.rs = 1;
+        L21.cs = r;
+      }
+      Opnd Z11{Zp, bs, pstr, o0, r, 1};
+      float* Tp = T.data_ptr<float>();
+      const int64_t t_pstr = (int64_t)s2 * s;
+      dim3 g1((unsigned)((s + 63) / 64), (unsigned)((s2 + 63) / 64), (unsigned)(b * np));
+      sgemm_pairs_kernel<<<g1, 256, 0, stream>>>(L21, Z11, Tp, (int64_t)np * t_pstr, t_pstr, 0, s, s2, s, s, np,
+                                                 1.f);
+      C10_CUDA_KERNEL_LAUNCH_CHECK();
+      note_launch();
+      Opnd Z22{Zp, bs, pstr, o0 + (int64_t)s * r + s, r, 1};
+      Opnd Tm{Tp, (int64_t)np * t_pstr, t_pstr, 0, s, 1};
+      sgemm_pairs_kernel<<<g1, 256, 0, stream>>>(Z22, Tm, Zp, bs, pstr, o0 + (int64_t)s * r, r, s2, s, s2, np,
+                                                 -1.f);
+      C10_CUDA_KERNEL_LAUNCH_CHECK();
+      note_launch();
+    }
+  }
 }
 
 // A: [b, m, n] fp32 contiguous (m >= n), overwritten; R: [b, n, n] upper.
+// Cluster size: enough CTAs per matrix to cover the SMs (at most 8, the
+// portable cluster size), 1 when the batch alone fills the GPU.
 void qr_r(at::Tensor& A, at::Tensor& R) {
   TORCH_CHECK(A.dim() == 3 && A.is_contiguous() && A.scalar_type() == at::kFloat && A.size(1) >= A.size(2),
               "dion_b200 qr_r: contiguous [b, m, n] fp32 with m >= n");
   const int b = (int)A.size(0), m = (int)A.size(1), n = (int)A.size(2);
-  const size_t smem = ((size_t)m * LD + NB * LD + 40 + 2 * NB) * sizeof(float);
-  TORCH_CHECK(smem <= 227 * 1024, "dion_b200 qr_r: m too large for the single-CTA kernel");
+  const size_t smem = ((size_t)m * QLD + NB * LD + 40 + 2 * NB) * sizeof(float);
+  TORCH_CHECK(smem <= 227 * 1024, "dion_b200 qr_r: m too large for the panel kernel");
   c10::cuda::CUDAGuard guard(A.device());
-  cudaFuncSetAttribute(qr_r_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  qr_r_kernel<<<b, QR_CT, smem, at::cuda::getCurrentCUDAStream()>>>(A.data_ptr<float>(), m, n, (int64_t)m * n,
-                                                                  R.data_ptr<float>(), (int64_t)n * n);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
-  note_launch();
+  launch_clustered(qr_r_kernel, b, QR_CT, smem, A.data_ptr<float>(), m, n, (int64_t)m * n, R.data_ptr<float>(),
+                   (int64_t)n * n);
 }
 
 }  // namespace bdion

@@ -52,6 +52,38 @@ __global__ void rms_fwd_kernel(const __nv_bfloat16* __restrict__ x, const WT* __
   }
 }
 
+// Same, for D = NC*256: the row stays in registers between the sum of
+// squares and the scaling, so x is read from memory once.
+template <typename WT, int NC>
+__global__ void rms_fwd_reg_kernel(const __nv_bfloat16* __restrict__ x, const WT* __restrict__ w,
+                                   __nv_bfloat16* __restrict__ y, float* __restrict__ rstd, int R, float eps) {
+  constexpr int D = NC * 256;
+  const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (row >= R) return;
+  const __nv_bfloat16* xr = x + (int64_t)row * D;
+  float v[NC][8];
+#pragma unroll
+  for (int k = 0; k < NC; ++k) load8(xr + k * 256 + lane * 8, v[k]);
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < NC; ++k)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += v[k][i] * v[k][i];
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / D + eps);
+  if (lane == 0) rstd[row] = r;
+  __nv_bfloat16* yr = y + (int64_t)row * D;
+#pragma unroll
+  for (int k = 0; k < NC; ++k) {
+    float wv[8];
+    load8(w + k * 256 + lane * 8, wv);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[k][i] = v[k][i] * r * wv[i];
+    store8(yr + k * 256 + lane * 8, v[k]);
+  }
+}
+
 // gx = r*w*gy - x * r^3/D * sum(gy*w*x); partial gw[blk, :] += gy*x*r over this block's rows
 template <typename WT>
 __global__ void rms_bwd_kernel(const __nv_bfloat16* __restrict__ gy, const __nv_bfloat16* __restrict__ x,
@@ -348,7 +380,29 @@ void rms_norm_fwd(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, at::T
   const int grid = (R + rows_per_blk - 1) / rows_per_blk;
   auto xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
   auto yp = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
-  if (w.scalar_type() == at::kFloat)
+  const int nc = D % 256 == 0 ? D / 256 : 0;
+  if (nc == 1 || nc == 2 || nc == 3 || nc == 4 || nc == 8 || nc == 16) {
+    auto launch = [&](auto tag_w, auto ncc) {
+      using WT = decltype(tag_w);
+      constexpr int NC = decltype(ncc)::value;
+      rms_fwd_reg_kernel<WT, NC><<<grid, 128, 0, s>>>(xp, reinterpret_cast<const WT*>(w.data_ptr()), yp,
+                                                       rstd.data_ptr<float>(), R, (float)eps);
+    };
+    auto by_nc = [&](auto tag_w) {
+      switch (nc) {
+        case 1: launch(tag_w, std::integral_constant<int, 1>{}); break;
+        case 2: launch(tag_w, std::integral_constant<int, 2>{}); break;
+        case 3: launch(tag_w, std::integral_constant<int, 3>{}); break;
+        case 4: launch(tag_w, std::integral_constant<int, 4>{}); break;
+        case 8: launch(tag_w, std::integral_constant<int, 8>{}); break;
+        default: launch(tag_w, std::integral_constant<int, 16>{}); break;
+      }
+    };
+    if (w.scalar_type() == at::kFloat)
+      by_nc(float{});
+    else
+      by_nc(__nv_bfloat16{});
+  } else if (w.scalar_type() == at::kFloat)
     rms_fwd_kernel<float><<<grid, 128, 0, s>>>(xp, w.data_ptr<float>(), yp, rstd.data_ptr<float>(), R, D, (float)eps);
   else
     rms_fwd_kernel<__nv_bfloat16><<<grid, 128, 0, s>>>(

@@ -72,6 +72,8 @@ class ParallelismConfig:
     data_parallel_shard_degree: int = -1
     tensor_parallel_degree: int = 1
     pipeline_parallel_degree: int = 1
+    pipeline_parallel_microbatches: int = 0
+    pipeline_parallel_schedule: str = "1F1B"
 
 
 @dataclass

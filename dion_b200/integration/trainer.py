@@ -46,6 +46,9 @@ class TrainerConfig:
     dp_replicate: int = 1
     dp_shard: int = -1
     tp: int = 1
+    pp: int = 1
+    pp_microbatches: int = 0  # 0: 2 x pp
+    pp_schedule: str = "1F1B"  # 1F1B | GPipe
     use_fsdp: bool = True
     ac_mode: str = "none"  # none | full | selective
     ac_option: str = "op"
@@ -85,11 +88,13 @@ class SyntheticTokens:
             yield self.next()
 
 
-def clip_grad_norm_multi_mesh_(params: List[torch.nn.Parameter], max_norm: float) -> torch.Tensor:
+def clip_grad_norm_multi_mesh_(params: List[torch.nn.Parameter], max_norm: float,
+                               stage_group=None) -> torch.Tensor:
     """Global-norm clipping when gradients live on different meshes (FSDP-only
     and FSDP x TP DTensors in one model): norms are taken per (mesh,
-    placements) group, made replicated, and combined on the host side of the
-    autograd graph; the clip coefficient scales every local shard."""
+    placements) group, made replicated, and combined; the clip coefficient
+    scales every local shard. ``stage_group``: the pipeline group, whose
+    stages hold disjoint parameters (their squared norms are summed)."""
     from torch.distributed.tensor import DTensor
 
     groups: Dict[Any, List[torch.Tensor]] = {}
@@ -105,7 +110,10 @@ def clip_grad_norm_multi_mesh_(params: List[torch.nn.Parameter], max_norm: float
         if isinstance(n, DTensor):
             n = n.full_tensor()
         sq.append(n.float().square())
-    total = torch.stack(sq).sum().sqrt()
+    total_sq = torch.stack(sq).sum() if sq else torch.zeros((), device=params[0].device)
+    if stage_group is not None:
+        dist.all_reduce(total_sq, group=stage_group)
+    total = total_sq.sqrt()
     coef = (max_norm / (total + 1e-6)).clamp(max=1.0)
     for gs in groups.values():
         torch._foreach_mul_([g.to_local() if isinstance(g, DTensor) else g for g in gs], coef)
@@ -121,12 +129,14 @@ class Trainer:
         self.device = device
         self.mesh = None
         shard_mesh = replicate_mesh = None
-        dims = ParallelDims(cfg.dp_replicate, cfg.dp_shard, cfg.tp)
-        if cfg.use_fsdp:
+        dims = ParallelDims(cfg.dp_replicate, cfg.dp_shard, cfg.tp, cfg.pp)
+        self.dp_mesh = None
+        if cfg.use_fsdp or cfg.pp > 1:
             self.mesh = build_mesh(dims, device.type)
             names = self.mesh.mesh_dim_names
             dp_names = tuple(n for n in ("dp_replicate", "dp_shard") if n in names)
-            self.dp_mesh = self.mesh[dp_names] if len(dp_names) > 1 else self.mesh[dp_names[0]]
+            if dp_names:
+                self.dp_mesh = self.mesh[dp_names] if len(dp_names) > 1 else self.mesh[dp_names[0]]
             shard_mesh = self.mesh["dp_shard"] if "dp_shard" in names else None
             replicate_mesh = self.mesh["dp_replicate"] if "dp_replicate" in names else None
         mcfg: Llama3Config = llama3_config(cfg.model, **cfg.model_overrides)
@@ -138,14 +148,27 @@ class Trainer:
         gen = torch.Generator(device=device).manual_seed(cfg.seed)
         model.init_weights(cfg.init_mode, generator=gen)
         model.set_activation_checkpointing(cfg.ac_mode, cfg.ac_option)
+        self.pp_runner = None
+        self.pp_group = None
+        if cfg.pp > 1:
+            from ..parallel.pp import PipelineRunner, build_pipeline_stage
+
+            pp_mesh = self.mesh["pp"]
+            model = build_pipeline_stage(model, pp_mesh)
+            self.pp_group = pp_mesh.get_group()
         tp_mesh = None
         if cfg.tp > 1:
             if self.mesh is None or "tp" not in self.mesh.mesh_dim_names:
                 raise ValueError("tensor parallelism needs use_fsdp=True (the mesh is built there)")
             tp_mesh = self.mesh["tp"]
             apply_tp(model, tp_mesh)
-        if cfg.use_fsdp:
-            apply_fsdp(model, self.dp_mesh)
+        if cfg.use_fsdp and self.dp_mesh is not None:
+            # pipeline stages keep their parameters gathered across micro-batches
+            # (and the last stage's LM head stays gathered for the loss)
+            apply_fsdp(model, self.dp_mesh, reshard_after_forward=cfg.pp == 1)
+        if cfg.pp > 1:
+            self.pp_runner = PipelineRunner(model, self.mesh["pp"], device, cfg.pp_microbatches or 2 * cfg.pp,
+                                            cfg.pp_schedule)
         self.model = model
         self.tp_mesh = tp_mesh
         self.optimizers = HybridOptimizersContainer(
@@ -153,10 +176,12 @@ class Trainer:
         )
         self._base_lrs = [[g["lr"] for g in o.param_groups] for o in self.optimizers]
         self.step_idx = 0
-        # TP is the innermost mesh dim: the ranks of one TP group share a batch
-        tp = max(1, cfg.tp)
-        self.data = SyntheticTokens(mcfg.vocab_size, cfg.seq_len, cfg.local_batch_size, cfg.seed, self.rank // tp,
-                                    self.world // tp)
+        # mesh order (pp, dp_replicate, dp_shard, tp): the ranks of one TP group
+        # and of one pipeline share a batch
+        tp, pp = max(1, cfg.tp), max(1, cfg.pp)
+        per_stage = self.world // pp
+        self.data = SyntheticTokens(mcfg.vocab_size, cfg.seq_len, cfg.local_batch_size, cfg.seed,
+                                    (self.rank % per_stage) // tp, per_stage // tp)
 
     @property
     def last_grad_norm(self) -> float:
@@ -184,10 +209,14 @@ class Trainer:
         tokens = tokens.to(self.device, non_blocking=True)
         labels = labels.to(self.device, non_blocking=True)
         self._set_lr()
-        loss = self.forward_backward(tokens, labels)
+        if self.pp_runner is not None:
+            loss = self.pp_runner.step(tokens, labels)
+        else:
+            loss = self.forward_backward(tokens, labels)
         if self.cfg.max_norm and self.cfg.max_norm > 0:
-            if self.tp_mesh is not None:
-                self._grad_norm = clip_grad_norm_multi_mesh_(list(self.model.parameters()), self.cfg.max_norm)
+            if self.tp_mesh is not None or self.pp_group is not None:
+                self._grad_norm = clip_grad_norm_multi_mesh_(list(self.model.parameters()), self.cfg.max_norm,
+                                                             self.pp_group)
             else:
                 self._grad_norm = torch.nn.utils.clip_grad_norm_(self.model.parameters(), self.cfg.max_norm,
                                                                  foreach=True)

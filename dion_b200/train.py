@@ -47,6 +47,9 @@ def trainer_config_from_job(job: JobConfig) -> TrainerConfig:
         dp_replicate=par.data_parallel_replicate_degree,
         dp_shard=par.data_parallel_shard_degree,
         tp=par.tensor_parallel_degree,
+        pp=par.pipeline_parallel_degree,
+        pp_microbatches=par.pipeline_parallel_microbatches,
+        pp_schedule=par.pipeline_parallel_schedule,
         optimizer=job.optimizer,
         log_freq=job.metrics.log_freq,
         ac_mode=job.activation_checkpoint.mode,

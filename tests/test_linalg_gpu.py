@@ -37,7 +37,7 @@ def test_cholesky_not_pd_flags():
     assert torch.isnan(A).any()
 
 
-@pytest.mark.parametrize("r", [32, 77, 512, 1024])
+@pytest.mark.parametrize("r", [32, 77, 96, 600, 1024])
 @pytest.mark.parametrize("upper", [False, True])
 def test_tri_inv(r, upper):
     g = torch.Generator(device="cuda").manual_seed(1)

@@ -68,3 +68,24 @@ def test_effective_rank_kernel_matches_torch():
     ref = ops.effective_rank(sumsq.cpu().double(), slots.cpu(), ranks.cpu())
     torch.testing.assert_close(got.cpu().double(), ref, rtol=1e-4, atol=1e-4)
     assert abs(float(got[2]) - 1.0) < 1e-4  # one active column: effective rank 1
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("r", [64, 30])
+@pytest.mark.parametrize("qdtype", [torch.float32, torch.bfloat16])
+def test_column_norm_kernels(r, qdtype):
+    """col_sumsq / col_normalize (vector path when r % 4 == 0, scalar otherwise;
+    output into a strided view of a wider buffer) against torch fp32."""
+    from dion_b200 import ops
+
+    torch.manual_seed(0)
+    R = torch.randn(3, 1000, r, device="cuda")
+    s = ops.col_sumsq(R)
+    torch.testing.assert_close(s, R.square().sum(dim=1), rtol=1e-5, atol=1e-4)
+    wide = torch.zeros(3, 1000, r + 8, device="cuda", dtype=qdtype)
+    Q = wide[:, :, :r]
+    ops.col_normalize(R, s, 1e-8, Q)
+    ref = R / (s.sqrt().unsqueeze(1) + 1e-8)
+    tol = 1e-5 if qdtype == torch.float32 else 1e-2
+    torch.testing.assert_close(Q.float(), ref, rtol=tol, atol=tol)
+    assert float(wide[:, :, r:].abs().max()) == 0.0
