@@ -60,11 +60,12 @@ def main(argv=None):
         # reduce-scatter: slice j -> rank j's slot [rank]
         rs_dst = [heap.ptr_tensor([heap.addr(j, rank * chunk * 4)]) for j in range(W)]
         # all-gather: my chunk -> every rank's out_ag[rank]
-        ag_dst = heap.ptr_tensor([heap.addr(j, n * 4 + rank * chunk * 4) for j in range(W)])
+        order = [(rank + 1 + i) % W for i in range(W)]  # one source per destination at a time
+        ag_dst = heap.ptr_tensor([heap.addr(j, n * 4 + rank * chunk * 4) for j in order])
         xs = x.view(W, chunk)
 
         def p2p_rs():
-            for j in range(W):
+            for j in order:
                 E.symm_push(xs[j], rs_dst[j])
             heap.barrier()
             E.symm_reduce_slots(recv, mine, W)
@@ -74,7 +75,7 @@ def main(argv=None):
             heap.barrier()
 
         def p2p_a2a():
-            for j in range(W):
+            for j in order:
                 E.symm_push(xs[j], rs_dst[j])
             heap.barrier()
 

@@ -37,13 +37,21 @@ def bench_gemm(small: bool):
         A = torch.randn(n, n, device="cuda", dtype=dt)
         B = torch.randn(n, n, device="cuda", dtype=dt)
         C = torch.empty(n, n, device="cuda", dtype=torch.bfloat16 if dt == torch.bfloat16 else torch.float32)
-        ms = _time(lambda: ops.matmul(A, B, out=C))
+        E = ops.ext()
+        mode = E.gemm_pair_mode()
+        E.set_gemm_pair_mode(0)
+        ms_single = _time(lambda: ops.matmul(A, B, out=C))
+        E.set_gemm_pair_mode(1)
+        ms_pair = _time(lambda: ops.matmul(A, B, out=C))
+        E.set_gemm_pair_mode(mode)
+        ms = min(ms_single, ms_pair)
         torch.backends.cuda.matmul.allow_tf32 = True
         ref = _time(lambda: torch.matmul(A, B, out=C))
         torch.backends.cuda.matmul.allow_tf32 = False
         fl = 2 * n**3
         out.append({"case": f"gemm_{'bf16' if dt == torch.bfloat16 else 'tf32'}_{n}^3", "ms": ms, "ref_ms": ref,
-                    "tflops": fl / ms / 1e9, "ref_tflops": fl / ref / 1e9})
+                    "tflops": fl / ms / 1e9, "ref_tflops": fl / ref / 1e9,
+                    "tflops_1cta": fl / ms_single / 1e9, "tflops_cta_pair": fl / ms_pair / 1e9})
     X = torch.randn(4096, 14336 if not small else 8192, device="cuda", dtype=torch.bfloat16)
     S = torch.empty(4096, 4096, device="cuda", dtype=torch.bfloat16)
     ms = _time(lambda: ops.matmul(X, X.t(), out=S, symmetric=True))
@@ -70,11 +78,18 @@ def bench_ns(small: bool):
     for b, m, n in cases:
         U = torch.randn(b, m, n, device="cuda", dtype=torch.bfloat16)
         co = ops.KELLER_NS_COEFFS
-        ms = _time(lambda: ops.newton_schulz(U, co), warmup=2, iters=5)
+        E = ops.ext()
+        mode = E.gemm_pair_mode()
+        times = {}
+        for pm in (0, 1):
+            E.set_gemm_pair_mode(pm)
+            times[pm] = _time(lambda: ops.newton_schulz(U, co), warmup=2, iters=5)
+        E.set_gemm_pair_mode(mode)
+        ms = min(times.values())
         ref = _time(lambda: _ns_torch(U, co), warmup=2, iters=5)
         fl = 5 * b * (4 * m * m * n + 2 * m**3)  # dense-equivalent FLOPs of the iteration
         out.append({"case": f"newton_schulz_{b}x{m}x{n}", "ms": ms, "ref_ms": ref, "tflops_equiv": fl / ms / 1e9,
-                    "ref_tflops": fl / ref / 1e9})
+                    "ref_tflops": fl / ref / 1e9, "ms_1cta": times[0], "ms_cta_pair": times[1]})
     return out
 
 

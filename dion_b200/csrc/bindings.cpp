@@ -14,7 +14,9 @@ void gemm_ex(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10:
              double alpha, double beta, const c10::optional<at::Tensor>& scale, int64_t alpha_pow, int64_t beta_pow,
              bool sym, bool param_mode, double gamma, double delta, int64_t bn_pref,
              const c10::optional<at::Tensor>& D_ptrs, int64_t ldd_ptrs, int64_t out_dtype_ptrs, int64_t nrep,
-             int64_t rows_per_ptr);
+             int64_t rows_per_ptr, int64_t rot_b, int64_t rot_rows);
+void set_gemm_pair_mode(int64_t mode);
+int gemm_pair_mode();
 std::tuple<int64_t, at::Tensor> symm_create(int64_t bytes);
 int64_t symm_open(const at::Tensor& handle);
 void symm_close(int64_t peer_ptr);
@@ -25,7 +27,8 @@ void symm_reduce_slots(const at::Tensor& src, at::Tensor& dst, int64_t nslots);
 void symm_push(const at::Tensor& src, const at::Tensor& dsts);
 int64_t symm_flag_bytes();
 void newton_schulz_ex(at::Tensor& U, const at::Tensor& scale, const std::vector<double>& coeffs, at::Tensor& out,
-                      bool clobber_input, const c10::optional<at::Tensor>& out_ptrs, int64_t rows_per_ptr);
+                      bool clobber_input, const c10::optional<at::Tensor>& out_ptrs, int64_t rows_per_ptr,
+                      int64_t rot_rows);
 void newton_schulz(at::Tensor& U, const at::Tensor& scale, const std::vector<double>& coeffs, at::Tensor& out,
                    bool clobber_input);
 void muon_momentum(const std::vector<at::Tensor>& M, const std::vector<at::Tensor>& G,
@@ -69,7 +72,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("B"), py::arg("D"), py::arg("C"), py::arg("alpha"), py::arg("beta"), py::arg("scale"),
         py::arg("alpha_pow"), py::arg("beta_pow"), py::arg("sym"), py::arg("param_mode"), py::arg("gamma"),
         py::arg("delta"), py::arg("bn"), py::arg("D_ptrs"), py::arg("ldd_ptrs"), py::arg("out_dtype_ptrs"),
-        py::arg("nrep"), py::arg("rows_per_ptr"));
+        py::arg("nrep"), py::arg("rows_per_ptr"), py::arg("rot_b") = 0, py::arg("rot_rows") = 0);
+  m.def("set_gemm_pair_mode", &bdion::set_gemm_pair_mode, "CTA-pair GEMM kernels on (1) / off (0)");
+  m.def("gemm_pair_mode", &bdion::gemm_pair_mode);
   m.def("symm_create", &bdion::symm_create);
   m.def("symm_open", &bdion::symm_open);
   m.def("symm_close", &bdion::symm_close);
@@ -83,7 +88,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("coeffs"), py::arg("out"), py::arg("clobber_input") = false);
   m.def("newton_schulz_ex", &bdion::newton_schulz_ex, "Newton-Schulz whose last GEMM scatters rows",
         py::arg("U"), py::arg("scale"), py::arg("coeffs"), py::arg("out"), py::arg("clobber_input"),
-        py::arg("out_ptrs"), py::arg("rows_per_ptr"));
+        py::arg("out_ptrs"), py::arg("rows_per_ptr"), py::arg("rot_rows") = 0);
   m.def("muon_momentum", &bdion::muon_momentum);
   m.def("multi_sumsq", &bdion::multi_sumsq);
   m.def("scaled_update", &bdion::scaled_update);

@@ -4,6 +4,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "gemm_launch.cuh"
@@ -56,6 +57,18 @@ CUtensorMap make_map(const void* base, bool fp32, int64_t cols, int64_t rows, in
 
 }  // namespace
 
+// CTA-pair (cta_group::2) kernels for problems with at least two 128-row
+// tiles: 0 = off, 1 = on. Initial value from DION_B200_GEMM_PAIR (default on; "0" selects the single-CTA kernels).
+static int g_pair_mode = -1;
+int gemm_pair_mode() {
+  if (g_pair_mode < 0) {
+    const char* e = std::getenv("DION_B200_GEMM_PAIR");
+    g_pair_mode = (e != nullptr && e[0] == '0') ? 0 : 1;
+  }
+  return g_pair_mode;
+}
+void set_gemm_pair_mode(int64_t mode) { g_pair_mode = mode ? 1 : 0; }
+
 int gemm_sm_count() {
   static int n = [] {
     int dev = 0, v = 0;
@@ -78,7 +91,7 @@ void gemm_ex(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10:
              double alpha, double beta, const c10::optional<at::Tensor>& scale, int64_t alpha_pow, int64_t beta_pow,
              bool sym, bool param_mode, double gamma, double delta, int64_t bn_pref,
              const c10::optional<at::Tensor>& D_ptrs, int64_t ldd_ptrs, int64_t out_dtype_ptrs, int64_t nrep,
-             int64_t rows_per_ptr) {
+             int64_t rows_per_ptr, int64_t rot_b, int64_t rot_rows) {
   TORCH_CHECK(A.is_cuda() && B.is_cuda(), "dion_b200 gemm: CUDA tensors expected");
   TORCH_CHECK(A.dim() == 3 && B.dim() == 3, "dion_b200 gemm: 3-D [batch, rows, cols] views expected");
   const bool fp32_in = A.scalar_type() == at::kFloat;
@@ -112,10 +125,14 @@ void gemm_ex(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10:
 
   const int row_elems = fp32_in ? 32 : 64;  // elements per 128-byte swizzle row
   int bn = (bn_pref == 128 || bn_pref == 256) ? (int)bn_pref : (N > 128 ? 256 : 128);
+  // CTA pairs: a 256 x bn tile per pair of SMs, each CTA loading bn/2 columns of B
+  const bool pair = gemm_pair_mode() && M > kBM;
+  const int bm = pair ? kBM2 : kBM;
   CUtensorMap ma = a_mn ? make_map(A.data_ptr(), fp32_in, M, K, batch, A.stride(2), A.stride(0), row_elems, true)
                         : make_map(A.data_ptr(), fp32_in, K, M, batch, A.stride(1), A.stride(0), kBM, false);
   CUtensorMap mb = b_mn ? make_map(B.data_ptr(), fp32_in, N, K, batch, B.stride(1), B.stride(0), row_elems, true)
-                        : make_map(B.data_ptr(), fp32_in, K, N, batch, B.stride(2), B.stride(0), bn, false);
+                        : make_map(B.data_ptr(), fp32_in, K, N, batch, B.stride(2), B.stride(0), pair ? bn / 2 : bn,
+                                   false);
 
   GemmArgs args{};
   args.M = (int)M;
@@ -136,6 +153,9 @@ void gemm_ex(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10:
     args.strideD = D.stride(0);
     out_t = D.scalar_type();
   }
+  TORCH_CHECK(rot_b >= 0 && rot_rows >= 0, "dion_b200 gemm: rotations must be non-negative");
+  args.rot_b = (int)(batch > 0 ? rot_b % batch : 0);
+  args.rot_rows = (int)rot_rows;
   args.nrep = (int)nrep;
   args.rows_per_ptr = use_ptrs ? (int)rows_per_ptr : 0;
   args.splits = (int)splits;
@@ -159,11 +179,11 @@ void gemm_ex(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10:
   args.gamma = (float)gamma;
   args.delta = (float)delta;
   args.sym = sym ? 1 : 0;
-  args.tiles_m = (int)((M + kBM - 1) / kBM);
+  args.tiles_m = (int)((M + bm - 1) / bm);
   args.tiles_n = (int)((N + bn - 1) / bn);
   if (sym) {
     int cnt = 0;
-    for (int tm = 0; tm < args.tiles_m; ++tm) cnt += args.tiles_n - (tm * kBM) / bn;
+    for (int tm = 0; tm < args.tiles_m; ++tm) cnt += args.tiles_n - (tm * bm) / bn;
     args.tiles_per_batch = cnt;
   } else {
     args.tiles_per_batch = args.tiles_m * args.tiles_n;
@@ -195,9 +215,9 @@ void gemm_ex(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10:
 
   cudaStream_t s = at::cuda::getCurrentCUDAStream();
   if (fp32_in)
-    gemm_dispatch_tf32(a_mn, b_mn, bn, ma, mb, args, s, out_t, param_mode);
+    gemm_dispatch_tf32(a_mn, b_mn, bn, pair, ma, mb, args, s, out_t, param_mode);
   else
-    gemm_dispatch_bf16(a_mn, b_mn, bn, ma, mb, args, s, out_t, param_mode);
+    gemm_dispatch_bf16(a_mn, b_mn, bn, pair, ma, mb, args, s, out_t, param_mode);
 }
 
 void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10::optional<at::Tensor>& C, double alpha,
@@ -205,7 +225,7 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10::op
           bool param_mode, double gamma, double delta, int64_t bn_pref, const c10::optional<at::Tensor>& D_ptrs,
           int64_t ldd_ptrs, int64_t out_dtype_ptrs) {
   gemm_ex(A, B, D, C, alpha, beta, scale, alpha_pow, beta_pow, sym, param_mode, gamma, delta, bn_pref, D_ptrs,
-          ldd_ptrs, out_dtype_ptrs, 1, 0);
+          ldd_ptrs, out_dtype_ptrs, 1, 0, 0, 0);
 }
 
 }  // namespace bdion

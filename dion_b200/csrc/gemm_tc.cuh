@@ -60,6 +60,11 @@ struct GemmArgs {
   int total_tiles;
   int* status;
   uint64_t limit_ns;
+  // tile-order rotation (non-symmetric GEMMs): batch b is processed as
+  // (b + rot_b) % batch and row tile tm as (tm + rot_rows / BM) % tiles_m, so
+  // that ranks storing to peer GPUs start on different destinations
+  int rot_b;
+  int rot_rows;
 };
 
 constexpr int kBM = 128;
@@ -96,6 +101,20 @@ struct GemmCfg {
 };
 
 __device__ __forceinline__ int sym_row_start(int tm, int BN) { return (tm * kBM) / BN; }
+
+template <int BN>
+__device__ __forceinline__ void decode_tile(const GemmArgs& a, int local, int& tm, int& tn);
+
+// tile t -> (batch, row tile, column tile) including the rotations
+template <int BN>
+__device__ __forceinline__ void map_tile(const GemmArgs& a, int t, int& b, int& tm, int& tn) {
+  b = t / a.tiles_per_batch;
+  decode_tile<BN>(a, t - b * a.tiles_per_batch, tm, tn);
+  if (!a.sym) {
+    if (a.rot_b) b = (b + a.rot_b) % a.batch;
+    if (a.rot_rows) tm = (tm + a.rot_rows / kBM) % a.tiles_m;
+  }
+}
 
 // Map a linear tile id inside one batch to (tm, tn).
 template <int BN>
@@ -190,9 +209,8 @@ __global__ void __launch_bounds__(192, 1)
       long issued = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < args.total_tiles && ok; t += gridDim.x) {
-        const int b = t / args.tiles_per_batch;
-        int tm, tn;
-        decode_tile<BN>(args, t - b * args.tiles_per_batch, tm, tn);
+        int b, tm, tn;
+        map_tile<BN>(args, t, b, tm, tn);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1, s_abort, limit)) {
             report_status(args.status, kStatusGemmProducerTimeout);
@@ -300,9 +318,8 @@ __global__ void __launch_bounds__(192, 1)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     int local_tile = 0;
     for (int t = blockIdx.x; t < args.total_tiles; t += gridDim.x, ++local_tile) {
-      const int b = t / args.tiles_per_batch;
-      int tm, tn;
-      decode_tile<BN>(args, t - b * args.tiles_per_batch, tm, tn);
+      int b, tm, tn;
+      map_tile<BN>(args, t, b, tm, tn);
       const int acc = local_tile & 1;
       const uint32_t acc_phase = (local_tile >> 1) & 1;
       if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, s_abort, limit)) {

@@ -199,6 +199,8 @@ def matmul_to_ptrs(
     nrep: int = 1,
     rows_per_ptr: int = 0,
     alpha: float = 1.0,
+    rot_b: int = 0,
+    rot_rows: int = 0,
 ) -> None:
     """``alpha * A[b] @ B[b]`` stored through a device pointer array.
 
@@ -206,14 +208,16 @@ def matmul_to_ptrs(
     (local row ``i % rows_per_ptr``, row stride ``ldd`` elements) for every
     ``rep < nrep``; ``splits = ceil(M / rows_per_ptr)`` (1 when 0). The
     addresses may be peer-GPU memory: the GEMM epilogue then writes each tile
-    over NVLink as soon as it leaves the tensor cores.
+    over NVLink as soon as it leaves the tensor cores. ``rot_b`` /
+    ``rot_rows`` rotate the tile order (batch, row tile) so that ranks writing
+    to peers concurrently start on different destinations.
     """
     A3, B3 = _as3d(A), _as3d(B)
     assert A.is_cuda and ptrs.is_cuda and ptrs.dtype == torch.int64
     A3, B3 = _tma_operands(A3, B3)
     dummy = torch.empty((1, 1, 1), device=A.device, dtype=out_dtype)
     ext().gemm_ex(A3, B3, dummy, None, float(alpha), 0.0, None, 0, 0, False, False, 1.0, 1.0, 0, ptrs, int(ldd),
-                  _SCALAR_TYPE[out_dtype], int(nrep), int(rows_per_ptr))
+                  _SCALAR_TYPE[out_dtype], int(nrep), int(rows_per_ptr), int(rot_b), int(rot_rows))
 
 
 def _ns_reference(U: Tensor, coeffs: Sequence[Tuple[float, float, float]], eps: float) -> Tensor:
@@ -242,6 +246,7 @@ def newton_schulz(
     clobber_input: bool = False,
     out_ptrs: Optional[Tensor] = None,
     rows_per_ptr: int = 0,
+    rot_rows: int = 0,
 ) -> Tensor:
     """Orthogonalise each matrix of ``U`` (``[batch, m, n]`` or ``[m, n]``).
 
@@ -274,7 +279,7 @@ def newton_schulz(
         out3 = _as3d(out) if out is not None else torch.empty_like(U3)
         flat = [float(x) for abc in coeffs for x in abc]
         ext().newton_schulz_ex(U3, scale.float().contiguous(), flat, out3, bool(clobber_input), out_ptrs,
-                               int(rows_per_ptr))
+                               int(rows_per_ptr), int(rot_rows))
         return out3
     if (m % 8) or (n % 8):
         # pad both dims with zeros: orthogonalisation of [[X, 0], [0, 0]] keeps X's block

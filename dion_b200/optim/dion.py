@@ -628,11 +628,13 @@ class Dion(Optimizer):
         cached = self._p2p_ptrs.get(key)
         if cached is None:
             rs = [heap.addr(k // sets, recv_off + (me * sets + k % sets) * slot) for k in range(W * sets)]
-            ag = [heap.addr(j, pall_off + (me * sets + s) * slot) for s in range(sets) for j in range(W)]
+            order = [(me + 1 + i) % W for i in range(W)]  # replicas to the next ranks first
+            ag = [heap.addr(j, pall_off + (me * sets + s) * slot) for s in range(sets) for j in order]
             cached = (heap.ptr_tensor(rs), heap.ptr_tensor(ag))
             self._p2p_ptrs[key] = cached
         rs_ptrs, ag_ptrs = cached
-        ops.matmul_to_ptrs(A.to(dt), Qb.to(dt), rs_ptrs, r, torch.float32)
+        # start with the matrices owned by the next rank: concurrent ranks store to different GPUs
+        ops.matmul_to_ptrs(A.to(dt), Qb.to(dt), rs_ptrs, r, torch.float32, rot_b=((me + 1) % W) * sets)
         heap.barrier()
         recv = heap.view(recv_off, (W, sets, pd, r), torch.float32)
         mine = torch.empty((sets, pd, r), device=Mb.device, dtype=torch.float32)

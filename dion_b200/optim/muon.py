@@ -412,7 +412,9 @@ class Muon(Optimizer):
                 full[i // W].zero_()
         ops.muon_momentum_([t.view(-1) for t in M], [g.reshape(-1) for g in G], dst_views, mu, nesterov, eps)
         heap.barrier()
-        ops.newton_schulz(full, self._coeffs, eps, clobber_input=False, out_ptrs=ptrs, rows_per_ptr=ms)
+        # row tiles of the next rank's shard first: concurrent ranks scatter to different GPUs
+        ops.newton_schulz(full, self._coeffs, eps, clobber_input=False, out_ptrs=ptrs, rows_per_ptr=ms,
+                          rot_rows=((me + 1) % W) * ms)
         heap.barrier()
         ret = heap.view(ret_off, (W, sets, ms, k), torch.bfloat16)
         upd = [ret[i % W, i // W] for i in range(n)]

@@ -18,6 +18,17 @@ def _rel(a, b):
     return ((a.float() - b.float()).norm() / (b.float().norm() + 1e-12)).item()
 
 
+@pytest.fixture(autouse=True, params=[0, 1], ids=["cta1", "cta_pair"])
+def gemm_kernel_mode(request):
+    """Every GEMM test runs with the single-CTA kernels and with the CTA-pair
+    (cta_group::2) kernels."""
+    E = ops.ext()
+    old = E.gemm_pair_mode()
+    E.set_gemm_pair_mode(request.param)
+    yield request.param
+    E.set_gemm_pair_mode(old)
+
+
 @pytest.mark.parametrize("a_t", [False, True])
 @pytest.mark.parametrize("b_t", [False, True])
 @pytest.mark.parametrize("shape", [(256, 512, 384), (200, 296, 72), (128, 128, 64), (3, 520, 1032, 264)])
