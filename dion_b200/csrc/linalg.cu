@@ -484,16 +484,16 @@ __global__ void __launch_bounds__(QR_CT, 1) qr_r_kernel(float* __restrict__ A_al
 
 }  // namespace
 
-// CTAs per matrix for the clustered kernels: enough to cover the SMs (up to
-// 16, the non-portable cluster size, when the device can co-schedule it;
-// otherwise at most 8), 1 when the batch alone fills the GPU.
+// CTAs per matrix for the clustered kernels: enough to cover the SMs, at
+// most 8 (the portable cluster size; 16-CTA clusters measured 2x slower for
+// a batch of 8: fewer of them are co-resident), 1 when the batch alone fills
+// the GPU.
 template <typename Kern, typename... Args>
 void launch_clustered(Kern kern, int batch, int threads, size_t smem, Args... args) {
   int sms = 0, dev = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   cudaLaunchConfig_t cfg = {};
   cfg.blockDim = dim3((unsigned)threads);
   cfg.dynamicSmemBytes = smem;
@@ -505,15 +505,7 @@ void launch_clustered(Kern kern, int batch, int threads, size_t smem, Args... ar
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int nclus = 1;
-  while (nclus < 16 && batch * nclus * 2 <= sms) nclus *= 2;
-  while (nclus > 8) {  // a 16-CTA cluster must fit in one GPC
-    cfg.gridDim = dim3((unsigned)(batch * nclus));
-    attr[0].val.clusterDim.x = (unsigned)nclus;
-    int active = 0;
-    if (cudaOccupancyMaxActiveClusters(&active, kern, &cfg) == cudaSuccess && active > 0) break;
-    cudaGetLastError();
-    nclus /= 2;
-  }
+  while (nclus < 8 && batch * nclus * 2 <= sms) nclus *= 2;
   cfg.gridDim = dim3((unsigned)(batch * nclus));
   attr[0].val.clusterDim.x = (unsigned)nclus;
   C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, args..., nclus));

@@ -36,6 +36,8 @@ __all__ = ["SymmetricHeap", "p2p_enabled", "heap_for"]
 
 _ALIGN = 256
 _UID = itertools.count()
+_GUARD = 256  # canary bytes after the data region
+_CANARY = 0x5A5AA5A5  # int32 pattern
 _SCALAR_TYPE = {torch.float32: 6, torch.bfloat16: 15, torch.int64: 4, torch.uint8: 0}
 
 
@@ -68,7 +70,7 @@ class SymmetricHeap:
         self._flag_off = 0
         self.data_off = _round(E.symm_flag_bytes())
         self.nbytes = _round(nbytes)
-        ptr, handle = E.symm_create(self.data_off + self.nbytes)
+        ptr, handle = E.symm_create(self.data_off + self.nbytes + _GUARD)
         hd = handle.to(self.device)
         allh = torch.empty(self.world * hd.numel(), dtype=torch.uint8, device=self.device)
         dist.all_gather_into_tensor(allh, hd, group=group)
@@ -80,6 +82,24 @@ class SymmetricHeap:
         self._flags = torch.tensor(self.bases, dtype=torch.int64).to(self.device)
         self._closed = False
         self.uid = next(_UID)  # never reused, unlike id()
+        # canaries: the gap between the flag words and the data, and a guard after the data
+        flag_end = E.symm_flag_bytes()
+        self._canary_regions = [(flag_end, self.data_off - flag_end), (self.data_off + self.nbytes, _GUARD)]
+        for off, size in self._canary_regions:
+            E.symm_view(self._own + off, size // 4, 3).fill_(_CANARY)  # 3 = int32
+        torch.cuda.synchronize(self.device)
+
+    def check_canaries(self) -> bool:
+        """True if no kernel wrote outside the data region of this rank's copy
+        (the words before and after it still hold the canary pattern)."""
+        E = ops.ext()
+        for off, size in self._canary_regions:
+            if size <= 0:
+                continue
+            v = E.symm_view(self._own + off, size // 4, 3)
+            if not bool((v == _CANARY).all()):
+                return False
+        return True
 
     # ------------------------------------------------------------ addressing
     def addr(self, rank: int, offset: int) -> int:

@@ -64,8 +64,12 @@ def main():
             print(json.dumps({"optimizer": kind, "world": dist.get_world_size(), "max_abs_diff": diff,
                               "max_abs": scale, "ms_nccl": t_nccl, "ms_p2p": t_p2p, "status": status}), flush=True)
         ok = ok and diff <= 1e-2 * max(scale, 1e-6) and status == 0
-    from dion_b200.parallel.symm import release_all
+    from dion_b200.parallel.symm import _HEAPS, release_all
 
+    canaries = all(h.check_canaries() for h in _HEAPS.values())  # all heaps of both paths
+    if rank == 0:
+        print(json.dumps({"canaries_intact": canaries, "heaps": len(_HEAPS)}), flush=True)
+    ok = ok and canaries
     release_all()
     dist.destroy_process_group()
     sys.exit(0 if ok else 1)

@@ -31,6 +31,8 @@ def test_p2p_collectives_match_nccl():
     out = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
     lines = [json.loads(l) for l in out.stdout.splitlines() if l.startswith("{")]
     assert out.returncode == 0, out.stdout[-3000:] + out.stderr[-3000:]
+    assert any(l.get("canaries_intact") for l in lines), "a kernel wrote outside a symmetric buffer"
+    lines = [l for l in lines if "optimizer" in l]
     assert {l["optimizer"] for l in lines} == {"muon", "dion"}
     for l in lines:
         assert l["status"] == 0
