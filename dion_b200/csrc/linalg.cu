@@ -385,20 +385,28 @@ __global__ void __launch_bounds__(QR_CT, 1) qr_r_kernel(float* __restrict__ A_al
       }
       __syncthreads();
     }
-    // trailing columns this CTA owns: C -= V (T^T (V^T C)), one column per thread
+    // trailing columns this CTA owns: C -= V (T^T (V^T C)). `spl` consecutive
+    // lanes share a column when the CTA owns fewer columns than threads: each
+    // takes the rows i % spl == part, the partial V^T C are summed with warp
+    // shuffles, and each lane updates its own rows.
     const int jb0 = k0 / NB + 1;
     const int jfirst = jb0 + ((crank - jb0 % nclus) % nclus + nclus) % nclus;
     const int owned = jfirst < nblk ? (nblk - 1 - jfirst) / nclus + 1 : 0;
-    for (int t = threadIdx.x; t < owned * NB; t += QR_CT) {
-      const int col = (jfirst + (t / NB) * nclus) * NB + t % NB;
+    const int owned_cols = owned * NB;
+    int spl = 1;
+    while (spl < 8 && owned_cols * spl * 2 <= QR_CT) spl *= 2;
+    for (int t = threadIdx.x; t < owned_cols * spl; t += QR_CT) {
+      const int ci = t / spl, part = t % spl;
+      const int col = (jfirst + (ci / NB) * nclus) * NB + ci % NB;
       if (col >= n) continue;
       float wv[NB];
 #pragma unroll
       for (int a = 0; a < NB; ++a) wv[a] = 0.f;
       float* Ac = A + (int64_t)k0 * n + col;
       const int ktri = min(kb, rows);
+      const int d0 = ktri + ((part - ktri % spl) % spl + spl) % spl;  // first dense row of this lane
       // rows inside the triangular head of V (unit diagonal, zeros above)
-      for (int i = 0; i < ktri; ++i) {
+      for (int i = part; i < ktri; i += spl) {
         const float cv = Ac[(int64_t)i * n];
 #pragma unroll
         for (int a = 0; a < NB; ++a) {
@@ -407,14 +415,14 @@ __global__ void __launch_bounds__(QR_CT, 1) qr_r_kernel(float* __restrict__ A_al
         }
       }
       // dense rows: 8 independent loads in flight, V rows read as float4 broadcasts
-      int i = ktri;
-      for (; i + 8 <= rows; i += 8) {
+      int i = d0;
+      for (; i + 7 * spl < rows; i += 8 * spl) {
         float cv[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) cv[u] = Ac[(int64_t)(i + u) * n];
+        for (int u = 0; u < 8; ++u) cv[u] = Ac[(int64_t)(i + u * spl) * n];
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
-          const float4* vr = reinterpret_cast<const float4*>(sV + (i + u) * QLD);
+          const float4* vr = reinterpret_cast<const float4*>(sV + (i + u * spl) * QLD);
 #pragma unroll
           for (int a4 = 0; a4 < NB / 4; ++a4) {
             const float4 v4 = vr[a4];
@@ -425,10 +433,16 @@ __global__ void __launch_bounds__(QR_CT, 1) qr_r_kernel(float* __restrict__ A_al
           }
         }
       }
-      for (; i < rows; ++i) {
+      for (; i < rows; i += spl) {
         const float cv = Ac[(int64_t)i * n];
 #pragma unroll
         for (int a = 0; a < NB; ++a) wv[a] += sV[i * QLD + a] * cv;
+      }
+      if (spl > 1) {  // the lanes of one column are consecutive in a warp and active together
+        const unsigned mask = __activemask();
+        for (int o = 1; o < spl; o <<= 1)
+#pragma unroll
+          for (int a = 0; a < NB; ++a) wv[a] += __shfl_xor_sync(mask, wv[a], o);
       }
       // wv <- T^T wv in place (row a only needs entries b <= a, so go downwards)
 #pragma unroll
@@ -440,7 +454,7 @@ __global__ void __launch_bounds__(QR_CT, 1) qr_r_kernel(float* __restrict__ A_al
         wv[a] = a < kb ? sacc : 0.f;
       }
       float* Rc = R + (int64_t)k0 * n + col;
-      for (int i2 = 0; i2 < ktri; ++i2) {
+      for (int i2 = part; i2 < ktri; i2 += spl) {
         float sacc = 0.f;
 #pragma unroll
         for (int a = 0; a < NB; ++a) {
@@ -451,14 +465,14 @@ __global__ void __launch_bounds__(QR_CT, 1) qr_r_kernel(float* __restrict__ A_al
         Ac[(int64_t)i2 * n] = nv;
         Rc[(int64_t)i2 * n] = nv;
       }
-      i = ktri;
-      for (; i + 8 <= rows; i += 8) {
+      i = d0;
+      for (; i + 7 * spl < rows; i += 8 * spl) {
         float sv8[8], cv[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) cv[u] = Ac[(int64_t)(i + u) * n];
+        for (int u = 0; u < 8; ++u) cv[u] = Ac[(int64_t)(i + u * spl) * n];
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
-          const float4* vr = reinterpret_cast<const float4*>(sV + (i + u) * QLD);
+          const float4* vr = reinterpret_cast<const float4*>(sV + (i + u * spl) * QLD);
           float sacc = 0.f;
 #pragma unroll
           for (int a4 = 0; a4 < NB / 4; ++a4) {
@@ -468,9 +482,9 @@ __global__ void __launch_bounds__(QR_CT, 1) qr_r_kernel(float* __restrict__ A_al
           sv8[u] = sacc;
         }
 #pragma unroll
-        for (int u = 0; u < 8; ++u) Ac[(int64_t)(i + u) * n] = cv[u] - sv8[u];
+        for (int u = 0; u < 8; ++u) Ac[(int64_t)(i + u * spl) * n] = cv[u] - sv8[u];
       }
-      for (; i < rows; ++i) {
+      for (; i < rows; i += spl) {
         float sacc = 0.f;
 #pragma unroll
         for (int a = 0; a < NB; ++a) sacc += sV[i * QLD + a] * wv[a];
