@@ -214,10 +214,17 @@ void gemm_ex(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10:
   TORCH_CHECK(out_t == at::kFloat || out_t == at::kBFloat16, "dion_b200 gemm: output dtype must be bf16 or fp32");
 
   cudaStream_t s = at::cuda::getCurrentCUDAStream();
-  if (fp32_in)
-    gemm_dispatch_tf32(a_mn, b_mn, bn, pair, ma, mb, args, s, out_t, param_mode);
-  else
-    gemm_dispatch_bf16(a_mn, b_mn, bn, pair, ma, mb, args, s, out_t, param_mode);
+  if (fp32_in) {
+    if (pair)
+      gemm_dispatch_tf32_pair(a_mn, b_mn, bn, ma, mb, args, s, out_t, param_mode);
+    else
+      gemm_dispatch_tf32_single(a_mn, b_mn, bn, ma, mb, args, s, out_t, param_mode);
+  } else {
+    if (pair)
+      gemm_dispatch_bf16_pair(a_mn, b_mn, bn, ma, mb, args, s, out_t, param_mode);
+    else
+      gemm_dispatch_bf16_single(a_mn, b_mn, bn, ma, mb, args, s, out_t, param_mode);
+  }
 }
 
 void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10::optional<at::Tensor>& C, double alpha,

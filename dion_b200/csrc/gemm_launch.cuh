@@ -57,40 +57,75 @@ void gemm_launch_typed2(const CUtensorMap& ma, const CUtensorMap& mb, const Gemm
   note_launch();
 }
 
-template <typename TIn, bool A_MN, bool B_MN, typename OutT, typename CT, bool PARAM>
-void gemm_launch_bn(int bn, bool pair, const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& args,
-                    cudaStream_t s) {
-  if (pair) {
+template <bool PAIR, typename TIn, bool A_MN, bool B_MN, typename OutT, typename CT, bool PARAM>
+void gemm_launch_bn(int bn, const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& args, cudaStream_t s) {
+  if constexpr (PAIR) {
     if (bn == 256)
       gemm_launch_typed2<TIn, 256, A_MN, B_MN, OutT, CT, PARAM>(ma, mb, args, s);
     else
       gemm_launch_typed2<TIn, 128, A_MN, B_MN, OutT, CT, PARAM>(ma, mb, args, s);
-    return;
+  } else {
+    if (bn == 256)
+      gemm_launch_typed<TIn, 256, A_MN, B_MN, OutT, CT, PARAM>(ma, mb, args, s);
+    else
+      gemm_launch_typed<TIn, 128, A_MN, B_MN, OutT, CT, PARAM>(ma, mb, args, s);
   }
-  if (bn == 256)
-    gemm_launch_typed<TIn, 256, A_MN, B_MN, OutT, CT, PARAM>(ma, mb, args, s);
-  else
-    gemm_launch_typed<TIn, 128, A_MN, B_MN, OutT, CT, PARAM>(ma, mb, args, s);
 }
 
-template <typename TIn, typename OutT, typename CT, bool PARAM>
-void gemm_launch_major(bool a_mn, bool b_mn, int bn, bool pair, const CUtensorMap& ma, const CUtensorMap& mb,
+template <bool PAIR, typename TIn, typename OutT, typename CT, bool PARAM>
+void gemm_launch_major(bool a_mn, bool b_mn, int bn, const CUtensorMap& ma, const CUtensorMap& mb,
                        const GemmArgs& args, cudaStream_t s) {
   if (!a_mn && !b_mn)
-    gemm_launch_bn<TIn, false, false, OutT, CT, PARAM>(bn, pair, ma, mb, args, s);
+    gemm_launch_bn<PAIR, TIn, false, false, OutT, CT, PARAM>(bn, ma, mb, args, s);
   else if (!a_mn && b_mn)
-    gemm_launch_bn<TIn, false, true, OutT, CT, PARAM>(bn, pair, ma, mb, args, s);
+    gemm_launch_bn<PAIR, TIn, false, true, OutT, CT, PARAM>(bn, ma, mb, args, s);
   else if (a_mn && !b_mn)
-    gemm_launch_bn<TIn, true, false, OutT, CT, PARAM>(bn, pair, ma, mb, args, s);
+    gemm_launch_bn<PAIR, TIn, true, false, OutT, CT, PARAM>(bn, ma, mb, args, s);
   else
-    gemm_launch_bn<TIn, true, true, OutT, CT, PARAM>(bn, pair, ma, mb, args, s);
+    gemm_launch_bn<PAIR, TIn, true, true, OutT, CT, PARAM>(bn, ma, mb, args, s);
 }
 
-// Entry points implemented in gemm_bf16.cu / gemm_tf32.cu.
-// mode: 0 = store (OutT = out dtype, CT = OutT), 1 = param update
-void gemm_dispatch_bf16(bool a_mn, bool b_mn, int bn, bool pair, const CUtensorMap& ma, const CUtensorMap& mb,
-                        const GemmArgs& args, cudaStream_t s, at::ScalarType out, bool param);
-void gemm_dispatch_tf32(bool a_mn, bool b_mn, int bn, bool pair, const CUtensorMap& ma, const CUtensorMap& mb,
-                        const GemmArgs& args, cudaStream_t s, at::ScalarType out, bool param);
+// Per-input-type instantiations, one translation unit per (type, kernel
+// family) so the build compiles them in parallel.
+template <bool PAIR>
+void gemm_dispatch_bf16_impl(bool a_mn, bool b_mn, int bn, const CUtensorMap& ma, const CUtensorMap& mb,
+                             const GemmArgs& args, cudaStream_t s, at::ScalarType out, bool param) {
+  using bf = __nv_bfloat16;
+  if (param) {
+    if (out == at::kFloat)
+      gemm_launch_major<PAIR, bf, float, bf, true>(a_mn, b_mn, bn, ma, mb, args, s);
+    else
+      gemm_launch_major<PAIR, bf, bf, bf, true>(a_mn, b_mn, bn, ma, mb, args, s);
+  } else {
+    if (out == at::kFloat)
+      gemm_launch_major<PAIR, bf, float, float, false>(a_mn, b_mn, bn, ma, mb, args, s);
+    else
+      gemm_launch_major<PAIR, bf, bf, bf, false>(a_mn, b_mn, bn, ma, mb, args, s);
+  }
+}
+
+template <bool PAIR>
+void gemm_dispatch_tf32_impl(bool a_mn, bool b_mn, int bn, const CUtensorMap& ma, const CUtensorMap& mb,
+                             const GemmArgs& args, cudaStream_t s, at::ScalarType out, bool param) {
+  using bf = __nv_bfloat16;
+  if (param) {
+    if (out == at::kFloat)
+      gemm_launch_major<PAIR, float, float, bf, true>(a_mn, b_mn, bn, ma, mb, args, s);
+    else
+      gemm_launch_major<PAIR, float, bf, bf, true>(a_mn, b_mn, bn, ma, mb, args, s);
+  } else {
+    TORCH_CHECK(out == at::kFloat, "dion_b200 gemm: tf32 path writes fp32 (store mode)");
+    gemm_launch_major<PAIR, float, float, float, false>(a_mn, b_mn, bn, ma, mb, args, s);
+  }
+}
+
+#define BDION_GEMM_DISPATCH_DECL(name)                                                                   \
+  void name(bool a_mn, bool b_mn, int bn, const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& args, \
+            cudaStream_t s, at::ScalarType out, bool param);
+BDION_GEMM_DISPATCH_DECL(gemm_dispatch_bf16_single)
+BDION_GEMM_DISPATCH_DECL(gemm_dispatch_bf16_pair)
+BDION_GEMM_DISPATCH_DECL(gemm_dispatch_tf32_single)
+BDION_GEMM_DISPATCH_DECL(gemm_dispatch_tf32_pair)
+#undef BDION_GEMM_DISPATCH_DECL
 
 }  // namespace bdion
