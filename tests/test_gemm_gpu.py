@@ -111,3 +111,28 @@ def test_gemm_ptr_array_param_update():
     torch.cuda.synchronize()
     for x, r in zip(Xs, ref):
         assert _rel(x, r) < 2e-3
+
+
+@pytest.mark.parametrize("rot_b,rot_rows", [(0, 0), (3, 0), (0, 512), (2, 384)])
+def test_matmul_to_ptrs_rotation_and_row_split(rot_b, rot_rows):
+    """Pointer-array outputs with the per-rank tile-order rotation: batch and
+    row-tile rotations only change the order tiles are produced in, and
+    row-split destinations receive exactly their rows (here the destinations
+    are slices of one local buffer)."""
+    torch.manual_seed(0)
+    b, M, K, N, rows_per = 5, 1024, 256, 384, 256
+    A = torch.randn(b, M, K, device="cuda", dtype=torch.bfloat16)
+    B = torch.randn(b, K, N, device="cuda", dtype=torch.bfloat16)
+    out = torch.zeros(b, M, N, device="cuda", dtype=torch.float32)
+    splits = M // rows_per
+    ptrs = torch.tensor([out[i, j * rows_per].data_ptr() for i in range(b) for j in range(splits)],
+                        dtype=torch.int64, device="cuda")
+    ops.matmul_to_ptrs(A, B, ptrs, N, torch.float32, rows_per_ptr=rows_per, rot_b=rot_b, rot_rows=rot_rows)
+    torch.testing.assert_close(out, _ref(A, B), rtol=2e-2, atol=2e-1)
+    # replicated destinations: every batch written to two buffers
+    out2 = torch.zeros(2, b, M, N, device="cuda", dtype=torch.float32)
+    ptrs2 = torch.tensor([out2[r, i].data_ptr() for i in range(b) for r in range(2)], dtype=torch.int64,
+                         device="cuda")
+    ops.matmul_to_ptrs(A, B, ptrs2, N, torch.float32, nrep=2, rot_b=rot_b, rot_rows=rot_rows)
+    torch.testing.assert_close(out2[0], out, rtol=0, atol=0)
+    torch.testing.assert_close(out2[1], out, rtol=0, atol=0)
