@@ -55,6 +55,7 @@ void dion_momentum_add(const std::vector<at::Tensor>& M, const std::vector<at::T
 void dion_fixup(at::Tensor& P, at::Tensor& R, const at::Tensor& Q0, const at::Tensor& nz);
 void col_sumsq(const at::Tensor& R, at::Tensor& out);
 void col_normalize(const at::Tensor& R, const at::Tensor& sumsq, double eps, at::Tensor& Q);
+void philox_normal(at::Tensor& out, int64_t key, int64_t stream, double scale);
 void effective_rank(const at::Tensor& sumsq, const at::Tensor& slots, const at::Tensor& ranks, at::Tensor& out);
 void cholesky_lower(at::Tensor& A, at::Tensor& info);
 void tri_inv_lower(const at::Tensor& S, at::Tensor& Z, bool upper);
@@ -105,6 +106,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("col_sumsq", &bdion::col_sumsq);
   m.def("col_normalize", &bdion::col_normalize);
   m.def("effective_rank", &bdion::effective_rank);
+  m.def("philox_normal", &bdion::philox_normal, "counter-based N(0, scale^2) fill (Philox-4x32-10 + Box-Muller)");
   m.def("cholesky_lower", &bdion::cholesky_lower);
   m.def("tri_inv_lower", &bdion::tri_inv_lower);
   m.def("qr_r", &bdion::qr_r);

@@ -19,6 +19,7 @@ __all__ = [
     "matmul",
     "matmul_update_",
     "matmul_to_ptrs",
+    "philox_normal",
     "newton_schulz",
     "muon_momentum_",
     "scaled_update_",
@@ -448,6 +449,55 @@ def col_sumsq(R: Tensor) -> Tensor:
     out = torch.empty(R.size(0), R.size(2), device=R.device, dtype=torch.float32)
     ext().col_sumsq(R.contiguous(), out)
     return out
+
+
+_PHILOX_M = (0xD2511F53, 0xCD9E8D57)
+_PHILOX_W = (0x9E3779B9, 0xBB67AE85)
+_MASK32 = 0xFFFFFFFF
+
+
+def _philox_cpu(nblk: int, key: int, stream: int) -> Tensor:
+    """Philox-4x32-10 blocks [nblk, 4] (uint32 values in int64), counter
+    (j_lo, j_hi, stream_lo, stream_hi), key (key_lo, key_hi)."""
+    j = torch.arange(nblk, dtype=torch.int64)
+    c = [j & _MASK32, (j >> 32) & _MASK32, torch.full_like(j, stream & _MASK32),
+         torch.full_like(j, (stream >> 32) & _MASK32)]
+    k0, k1 = key & _MASK32, (key >> 32) & _MASK32
+    for _ in range(10):
+        p0 = _PHILOX_M[0] * c[0]  # < 2^64: the int64 bit pattern is the unsigned product
+        p1 = _PHILOX_M[1] * c[2]
+        hi0, lo0 = (p0 >> 32) & _MASK32, p0 & _MASK32
+        hi1, lo1 = (p1 >> 32) & _MASK32, p1 & _MASK32
+        c = [hi1 ^ c[1] ^ k0, lo1, hi0 ^ c[3] ^ k1, lo0]
+        k0 = (k0 + _PHILOX_W[0]) & _MASK32
+        k1 = (k1 + _PHILOX_W[1]) & _MASK32
+    return torch.stack(c, dim=1)
+
+
+def philox_normal(shape: Sequence[int], key: int, stream: int, scale: float = 1.0,
+                  device: torch.device | str = "cuda") -> Tensor:
+    """N(0, scale^2) fp32 values that are a pure function of (key, stream,
+    index): Philox-4x32-10 counters (Salmon et al., SC'11) + Box-Muller.
+    The same call gives the same values on every rank and launch; the CPU
+    version (plain torch integer arithmetic) is the oracle for the kernel."""
+    n = 1
+    for d in shape:
+        n *= int(d)
+    key &= (1 << 64) - 1
+    stream &= (1 << 64) - 1
+    dev = torch.device(device)
+    if dev.type == "cuda":
+        out = torch.empty(n, device=dev, dtype=torch.float32)
+        ext().philox_normal(out, key - (1 << 64) if key >= (1 << 63) else key,
+                            stream - (1 << 64) if stream >= (1 << 63) else stream, float(scale))
+        return out.view(*shape)
+    blocks = _philox_cpu((n + 3) // 4, key, stream)
+    u = (blocks.to(torch.float32) + 1.0) * 2.3283064365386963e-10
+    ra = torch.sqrt(-2.0 * torch.log(u[:, 0]))
+    rb = torch.sqrt(-2.0 * torch.log(u[:, 2]))
+    ta, tb = 6.283185307179586 * u[:, 1], 6.283185307179586 * u[:, 3]
+    z = torch.stack([ra * torch.cos(ta), ra * torch.sin(ta), rb * torch.cos(tb), rb * torch.sin(tb)], dim=1)
+    return (z.reshape(-1)[:n] * scale).view(*shape).to(dev)
 
 
 def effective_rank(sumsq: Tensor, slots: Tensor, ranks: Tensor) -> Tensor:

@@ -18,6 +18,7 @@ matrix of the batch, and the triangular factors are all-gathered.
 """
 from __future__ import annotations
 
+import itertools
 import math
 from typing import Optional
 
@@ -91,6 +92,19 @@ def _apply_inv_lower_t(P: Tensor, Z: Tensor) -> Tensor:
     return P @ Z.mT
 
 
+_SKETCH_CALLS = itertools.count()
+
+
+def _sketch(b: int, k: int, d: int, device, generator: Optional[torch.Generator]) -> Tensor:
+    """S ~ N(0, 1/k) of shape [b, k, d]. On the GPU (no explicit generator):
+    the package's Philox kernel keyed by the process seed and a call counter,
+    so a run is reproducible whatever else consumes torch's RNG."""
+    if generator is None and torch.device(device).type == "cuda" and ops.has_ext():
+        return ops.philox_normal((b, k, d), torch.initial_seed(), next(_SKETCH_CALLS), math.sqrt(1.0 / k), device)
+    S = torch.randn((b, k, d), device=device, dtype=torch.float32, generator=generator)
+    return S.mul_(math.sqrt(1.0 / k))
+
+
 def orthogonalize(P: Tensor, oversample: float = 1.25, generator: Optional[torch.Generator] = None,
                   out_ptrs: Optional[Tensor] = None, nrep: int = 1) -> Optional[Tensor]:
     """Orthonormal-column basis of every P[i] (see module doc).
@@ -115,8 +129,7 @@ def orthogonalize(P: Tensor, oversample: float = 1.25, generator: Optional[torch
             return None
         return Q.to(dtype)
     k = sketch_size(r, oversample)
-    S = torch.randn((b, k, d), device=P.device, dtype=torch.float32, generator=generator)
-    S.mul_(math.sqrt(1.0 / k))
+    S = _sketch(b, k, d, P.device, generator)
     SP = ops.matmul(S, Pf) if P.is_cuda else S @ Pf
     if P.is_cuda:
         # P <- P R1^-1 with R1 = qr(SP).R ; then CholeskyQR: P <- P chol(P^T P)^-T
@@ -165,7 +178,7 @@ def distributed_orthogonalize(P: DTensor, oversample: float = 1.25, shard_mesh_d
         return out.redistribute(placements=orig)
     k = sketch_size(r, oversample)
     P_local = P.to_local().float().contiguous()
-    S_local = torch.randn((P_local.size(0), k, P_local.size(1)), device=P_local.device) * math.sqrt(1.0 / k)
+    S_local = _sketch(P_local.size(0), k, P_local.size(1), P_local.device, None)
     SP_local = ops.matmul(S_local, P_local) if P_local.is_cuda else S_local @ P_local
     sp_pl = [pl if not (pl.is_shard() and pl.dim == P.ndim - 2) else None for pl in orig]
     from torch.distributed.tensor import Partial

@@ -126,3 +126,31 @@ def test_scalar_algorithms_route():
     opt.step()
     assert set(opt.state[b].keys()) == {"momentum", "variance"}
     assert set(opt.state[e].keys()) == {"momentum"}
+
+
+def test_philox_known_answers_and_statistics():
+    """Integer stage against the published Philox-4x32-10 known-answer vectors
+    (Random123 kat_vectors); the normals have mean 0 / std 1 and depend only
+    on (key, stream, index)."""
+    from dion_b200.ops import _MASK32, _PHILOX_M, _PHILOX_W, philox_normal
+
+    def philox(ctr, key):
+        c = [torch.tensor([v], dtype=torch.int64) for v in ctr]
+        k0, k1 = key
+        for _ in range(10):
+            p0, p1 = _PHILOX_M[0] * c[0], _PHILOX_M[1] * c[2]
+            c = [((p1 >> 32) & _MASK32) ^ c[1] ^ k0, p1 & _MASK32, ((p0 >> 32) & _MASK32) ^ c[3] ^ k1, p0 & _MASK32]
+            k0, k1 = (k0 + _PHILOX_W[0]) & _MASK32, (k1 + _PHILOX_W[1]) & _MASK32
+        return [int(x) for x in c]
+
+    assert philox([0, 0, 0, 0], (0, 0)) == [0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8]
+    m = 0xFFFFFFFF
+    assert philox([m, m, m, m], (m, m)) == [0x408F276D, 0x41C83B0E, 0xA20BC7C6, 0x6D5451FD]
+    assert philox([0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344], (0xA4093822, 0x299F31D0)) == \
+        [0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1]
+    x = philox_normal((200, 500), 123, 9, 1.0, "cpu")
+    assert abs(float(x.mean())) < 0.01 and abs(float(x.std()) - 1.0) < 0.01
+    assert torch.equal(x, philox_normal((200, 500), 123, 9, 1.0, "cpu"))
+    assert not torch.equal(x, philox_normal((200, 500), 123, 10, 1.0, "cpu"))
+    # element i does not depend on the requested size
+    assert torch.equal(philox_normal((7,), 5, 1, 2.0, "cpu"), philox_normal((10,), 5, 1, 2.0, "cpu")[:7])

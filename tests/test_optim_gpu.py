@@ -89,3 +89,15 @@ def test_column_norm_kernels(r, qdtype):
     tol = 1e-5 if qdtype == torch.float32 else 1e-2
     torch.testing.assert_close(Q.float(), ref, rtol=tol, atol=tol)
     assert float(wide[:, :, r:].abs().max()) == 0.0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("n", [4096, 1001, 3])
+def test_philox_kernel_matches_cpu_oracle(n):
+    from dion_b200 import ops
+
+    for key, stream in ((0, 0), (1234567, 42), ((1 << 64) - 5, (1 << 63) + 7)):
+        g = ops.philox_normal((n,), key, stream, 0.5, "cuda")
+        c = ops.philox_normal((n,), key, stream, 0.5, "cpu")
+        torch.testing.assert_close(g.cpu(), c, rtol=1e-5, atol=1e-5)
+        assert torch.equal(g, ops.philox_normal((n,), key, stream, 0.5, "cuda"))
