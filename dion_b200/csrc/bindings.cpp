@@ -28,7 +28,7 @@ void symm_push(const at::Tensor& src, const at::Tensor& dsts);
 int64_t symm_flag_bytes();
 void newton_schulz_ex(at::Tensor& U, const at::Tensor& scale, const std::vector<double>& coeffs, at::Tensor& out,
                       bool clobber_input, const c10::optional<at::Tensor>& out_ptrs, int64_t rows_per_ptr,
-                      int64_t rot_rows);
+                      int64_t rot_rows, int64_t nrep);
 void newton_schulz(at::Tensor& U, const at::Tensor& scale, const std::vector<double>& coeffs, at::Tensor& out,
                    bool clobber_input);
 void muon_momentum(const std::vector<at::Tensor>& M, const std::vector<at::Tensor>& G,
@@ -89,7 +89,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("coeffs"), py::arg("out"), py::arg("clobber_input") = false);
   m.def("newton_schulz_ex", &bdion::newton_schulz_ex, "Newton-Schulz whose last GEMM scatters rows",
         py::arg("U"), py::arg("scale"), py::arg("coeffs"), py::arg("out"), py::arg("clobber_input"),
-        py::arg("out_ptrs"), py::arg("rows_per_ptr"), py::arg("rot_rows") = 0);
+        py::arg("out_ptrs"), py::arg("rows_per_ptr"), py::arg("rot_rows") = 0, py::arg("nrep") = 1);
   m.def("muon_momentum", &bdion::muon_momentum);
   m.def("multi_sumsq", &bdion::multi_sumsq);
   m.def("scaled_update", &bdion::scaled_update);

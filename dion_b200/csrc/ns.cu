@@ -34,11 +34,12 @@ void gemm_ex(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10:
 // U: [batch, m, n] bf16 contiguous (not normalised). scale: [batch] fp32.
 // out: [batch, m, n] bf16. If clobber_input, U may be used as scratch.
 // With out_ptrs the last iteration's GEMM does not write `out`: rows
-// [j*rows_per_ptr, (j+1)*rows_per_ptr) of matrix b go to out_ptrs[b*splits + j]
-// (row stride n), e.g. straight into the ranks that own those rows.
+// [j*rows_per_ptr, (j+1)*rows_per_ptr) of matrix b go to
+// out_ptrs[(b*splits + j)*nrep + rep] for rep < nrep (row stride n), e.g.
+// straight into the ranks that own those rows, or into every rank.
 void newton_schulz_ex(at::Tensor& U, const at::Tensor& scale, const std::vector<double>& coeffs, at::Tensor& out,
                       bool clobber_input, const c10::optional<at::Tensor>& out_ptrs, int64_t rows_per_ptr,
-                      int64_t rot_rows) {
+                      int64_t rot_rows, int64_t nrep) {
   TORCH_CHECK(U.dim() == 3 && U.is_contiguous() && U.scalar_type() == at::kBFloat16,
               "dion_b200 newton_schulz: U must be a contiguous [batch, m, n] bf16 tensor");
   TORCH_CHECK(out.sizes() == U.sizes() && out.is_contiguous() && out.scalar_type() == at::kBFloat16,
@@ -73,8 +74,8 @@ void newton_schulz_ex(at::Tensor& U, const at::Tensor& scale, const std::vector<
       gemm(A, A.transpose(1, 2), Bm, A, c, b, none, 0, 0, true, false, 0, 0, 0, none, 0, 0);
       // X' = a X + B X : B-operand X [K=m, N=n] N-major
       if (i == iters - 1 && out_ptrs.has_value())
-        gemm_ex(Bm, src, dst, src, 1.0, a, sc, 1, 1, false, false, 0, 0, 0, out_ptrs, n, (int64_t)at::kBFloat16, 1,
-                rows_per_ptr, 0, rot_rows);
+        gemm_ex(Bm, src, dst, src, 1.0, a, sc, 1, 1, false, false, 0, 0, 0, out_ptrs, n, (int64_t)at::kBFloat16,
+                nrep, rows_per_ptr, 0, rot_rows);
       else
         gemm(Bm, src, dst, src, 1.0, a, sc, 1, 1, false, false, 0, 0, 0, none, 0, 0);
     } else {
@@ -84,7 +85,7 @@ void newton_schulz_ex(at::Tensor& U, const at::Tensor& scale, const std::vector<
       // X' = a X + X B : A-operand X [m, K=n] K-major; B-operand B [K=n, N=n] (symmetric) K-major view
       if (i == iters - 1 && out_ptrs.has_value())
         gemm_ex(src, Bm.transpose(1, 2), dst, src, 1.0, a, sc, 1, 1, false, false, 0, 0, 0, out_ptrs, n,
-                (int64_t)at::kBFloat16, 1, rows_per_ptr, 0, rot_rows);
+                (int64_t)at::kBFloat16, nrep, rows_per_ptr, 0, rot_rows);
       else
         gemm(src, Bm.transpose(1, 2), dst, src, 1.0, a, sc, 1, 1, false, false, 0, 0, 0, none, 0, 0);
     }
@@ -94,7 +95,7 @@ void newton_schulz_ex(at::Tensor& U, const at::Tensor& scale, const std::vector<
 
 void newton_schulz(at::Tensor& U, const at::Tensor& scale, const std::vector<double>& coeffs, at::Tensor& out,
                    bool clobber_input) {
-  newton_schulz_ex(U, scale, coeffs, out, clobber_input, c10::nullopt, 0, 0);
+  newton_schulz_ex(U, scale, coeffs, out, clobber_input, c10::nullopt, 0, 0, 1);
 }
 
 }  // namespace bdion

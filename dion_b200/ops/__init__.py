@@ -248,6 +248,7 @@ def newton_schulz(
     out_ptrs: Optional[Tensor] = None,
     rows_per_ptr: int = 0,
     rot_rows: int = 0,
+    nrep: int = 1,
 ) -> Tensor:
     """Orthogonalise each matrix of ``U`` (``[batch, m, n]`` or ``[m, n]``).
 
@@ -258,7 +259,9 @@ def newton_schulz(
     With ``out_ptrs`` (int64 device array, ``batch * m/rows_per_ptr``
     addresses) the result is not written to ``out``: the last GEMM stores rows
     ``[j*rows_per_ptr, (j+1)*rows_per_ptr)`` of matrix b at ``out_ptrs[b*splits + j]``
-    (row stride n). Used to scatter row shards straight to their owner GPUs.
+    (row stride n), and with ``nrep`` > 1 to ``out_ptrs[(b*splits + j)*nrep + rep]``
+    for every rep. Used to scatter row shards straight to their owner GPUs,
+    or to broadcast each result to every GPU.
     """
     squeeze = U.dim() == 2
     U3 = _as3d(U)
@@ -273,14 +276,14 @@ def newton_schulz(
         clobber_input = True
     m, n = U3.shape[-2:]
     if out_ptrs is not None:
-        assert m % 8 == 0 and n % 8 == 0 and rows_per_ptr > 0, "row-scatter Newton-Schulz needs 8-aligned shapes"
+        assert m % 8 == 0 and n % 8 == 0 and rows_per_ptr >= 0, "pointer-output Newton-Schulz needs 8-aligned shapes"
         if scale is None:
             ss = multi_sumsq(list(U3.unbind(0)))
             scale = 1.0 / (ss.sqrt() + eps)
         out3 = _as3d(out) if out is not None else torch.empty_like(U3)
         flat = [float(x) for abc in coeffs for x in abc]
         ext().newton_schulz_ex(U3, scale.float().contiguous(), flat, out3, bool(clobber_input), out_ptrs,
-                               int(rows_per_ptr), int(rot_rows))
+                               int(rows_per_ptr), int(rot_rows), int(nrep))
         return out3
     if (m % 8) or (n % 8):
         # pad both dims with zeros: orthogonalisation of [[X, 0], [0, 0]] keeps X's block

@@ -89,6 +89,7 @@ class Dion2(Optimizer):
         self._tp_pg = tp_mesh.get_group() if isinstance(tp_mesh, DeviceMesh) and tp_mesh.size() > 1 else None
         self._tp = tp_mesh.size() if self._tp_pg is not None else 1
         self._gen: Optional[torch.Generator] = None
+        self._p2p_cache: Dict[Any, Any] = {}
         self._seed = seed
 
     def _state(self, p: Tensor, algo: str) -> Dict[str, Any]:
@@ -239,6 +240,8 @@ class Dion2(Optimizer):
         W, r = self._world, self._rank
         n, k, c = sel.shape
         sets = (n + W - 1) // W
+        if tp_dim is None and dp_dim == 0 and self._p2p_ok(sel, W):
+            return self._orthogonalize_sharded_p2p(sel, eps)
         send = torch.zeros((W, sets, k, c), device=sel.device, dtype=sel.dtype)
         for i in range(n):
             send[i % W, i // W] = sel[i]
@@ -259,3 +262,50 @@ class Dion2(Optimizer):
         ret = torch.empty_like(back)
         dist.all_to_all_single(ret.view(W, -1), back.view(W, -1), group=self._pg)
         return torch.stack([ret[i % W, i // W] for i in range(n)])
+
+    # ---- in-kernel row exchange over symmetric peer memory
+    def _p2p_ok(self, sel: Tensor, W: int) -> bool:
+        from ..parallel.symm import p2p_enabled
+
+        n, k, c = sel.shape
+        return (W > 1 and self._pg is not None and p2p_enabled(self._pg, sel.device) and c % 8 == 0
+                and (W * k) % 8 == 0)
+
+    def _orthogonalize_sharded_p2p(self, sel: Tensor, eps: float) -> Tensor:
+        """The selected rows go straight into the owner's [sets, W*k, cols]
+        buffer (peer stores, next ranks first), one device barrier, the owner
+        orthogonalises, the last Newton-Schulz GEMM stores each rank's k rows
+        into that rank's return buffer, one more barrier."""
+        from ..parallel.symm import heap_for
+
+        W, me = self._world, self._rank
+        n, k, c = sel.shape
+        sets = (n + W - 1) // W
+        blk = k * c * 2
+        mat = W * blk
+        gather_off, ret_off = 0, sets * mat
+        heap = heap_for(self._pg, 2 * sets * mat, "dion2", sel.device)
+        key = (heap.uid, n, k, c)
+        cached = self._p2p_cache.get(key)
+        if cached is None:
+            dsts = [heap.ptr_tensor([heap.addr(i % W, gather_off + (i // W) * mat + me * blk)]) for i in range(n)]
+            ptrs = heap.ptr_tensor([heap.addr(j, ret_off + (me * sets + s_) * blk) for s_ in range(sets)
+                                    for j in range(W)])
+            cached = (dsts, ptrs)
+            self._p2p_cache[key] = cached
+        dsts, ptrs = cached
+        full = heap.view(gather_off, (sets, W * k, c), torch.bfloat16)
+        for i in range(n, sets * W):
+            if i % W == me:  # this rank owns an absent matrix of the last set
+                full[i // W].zero_()
+        sel = sel.contiguous()
+        for t in range(n):
+            i = (me + 1 + t) % n if n > 1 else t  # next ranks' matrices first
+            heap.push(sel[i], dsts[i])
+        heap.barrier()
+        ops.newton_schulz(full, self._coeffs, eps, clobber_input=False, out_ptrs=ptrs, rows_per_ptr=k,
+                          rot_rows=((me + 1) % W) * k)
+        heap.barrier()
+        ret = heap.view(ret_off, (W, sets, k, c), torch.bfloat16)
+        return torch.stack([ret[i % W, i // W] for i in range(n)])
+

@@ -297,6 +297,10 @@ class Muon(Optimizer):
         full_scale[:n] = scale
         # matrices s*W + r belong to this rank
         mine = U.view(sets, W, m, k)[:, r].contiguous()
+        if self._ns_func is None and self._p2p_ok((m, k), 1, dev):
+            O = self._ns_allgather_p2p(mine, full_scale.view(sets, W)[:, r].contiguous(), sets, m, k, eps)[:n]
+            ops.scaled_update_(X, [o.view(shape) for o in O.unbind(0)], decay, [adj_lr] * n)
+            return
         O_mine = self._ns(mine, full_scale.view(sets, W)[:, r].contiguous(), eps)
         gathered = torch.empty((W, sets, m, k), device=dev, dtype=torch.bfloat16)
         dist.all_gather_into_tensor(gathered.view(W * sets, m, k), O_mine.contiguous(), group=self._pg)
@@ -374,6 +378,33 @@ class Muon(Optimizer):
 
         m, k = full_shape
         return p2p_enabled(self._pg, dev) and m % 8 == 0 and k % 8 == 0 and (m // W) % 8 == 0
+
+    def _ns_allgather_p2p(self, mine: Tensor, scale: Tensor, sets: int, m: int, k: int, eps: float) -> Tensor:
+        """DDP Muon without NCCL (DION/muon.py:493-520 all-gathers the
+        orthogonalised matrices): the last Newton-Schulz GEMM stores each
+        result into every rank's [sets, W, m, k] buffer (replicated epilogue
+        stores, next ranks first); one device barrier. Successive calls
+        alternate between two halves of the buffer: a rank that is still
+        reading call t's results cannot be overwritten by call t+1, and call
+        t+2 waits behind call t+1's barrier, which that rank reaches only
+        after its reads."""
+        from ..parallel.symm import heap_for
+
+        W, me = self._world, self._rank
+        half = sets * W * m * k * 2
+        heap = heap_for(self._pg, 2 * half, "muon_ddp", mine.device)
+        self._ddp_parity = par = 1 - getattr(self, "_ddp_parity", 1)
+        base = par * half
+        key = ("ddp", heap.uid, par, sets, m, k)
+        ptrs = self._p2p_cache.get(key)
+        if ptrs is None:
+            order = [(me + 1 + i) % W for i in range(W)]
+            ptrs = heap.ptr_tensor([heap.addr(j, base + (s_ * W + me) * m * k * 2) for s_ in range(sets)
+                                    for j in order])
+            self._p2p_cache[key] = ptrs
+        ops.newton_schulz(mine, self._coeffs, eps, scale=scale, clobber_input=True, out_ptrs=ptrs, nrep=W)
+        heap.barrier()
+        return heap.view(base, (sets * W, m, k), torch.bfloat16)
 
     def _muon_fsdp_p2p(self, X, G, M, full_shape, local_shape, n, sets, mu, nesterov, eps, decay, adj_lr) -> None:
         """Row-sharded FSDP Muon without NCCL (DION/muon.py:448-491 does two all_to_all calls).

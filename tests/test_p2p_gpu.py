@@ -33,7 +33,7 @@ def test_p2p_collectives_match_nccl():
     assert out.returncode == 0, out.stdout[-3000:] + out.stderr[-3000:]
     assert any(l.get("canaries_intact") for l in lines), "a kernel wrote outside a symmetric buffer"
     lines = [l for l in lines if "optimizer" in l]
-    assert {l["optimizer"] for l in lines} == {"muon", "dion"}
+    assert {l["optimizer"] for l in lines} == {"muon", "dion", "muon_ddp", "dion2"}
     for l in lines:
         assert l["status"] == 0
         assert l["max_abs_diff"] <= 1e-2 * l["max_abs"], l
