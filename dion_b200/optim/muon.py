@@ -154,6 +154,7 @@ class Muon(Optimizer):
         self._distributed_mesh = distributed_mesh
         self._ns_func = newton_schulz_func
         self._p2p_cache: Dict[Tuple, Any] = {}
+        self._ddp_parity = 1  # buffer half of the last replicated Newton-Schulz call
         self._coeffs = _resolve_coeffs(ns_coeffs)
         self.fsdp_mesh_dim = fsdp_mesh_dim
         self._world_mesh = world_mesh
@@ -393,7 +394,7 @@ class Muon(Optimizer):
         W, me = self._world, self._rank
         half = sets * W * m * k * 2
         heap = heap_for(self._pg, 2 * half, "muon_ddp", mine.device)
-        self._ddp_parity = par = 1 - getattr(self, "_ddp_parity", 1)
+        self._ddp_parity = par = 1 - self._ddp_parity
         base = par * half
         key = ("ddp", heap.uid, par, sets, m, k)
         ptrs = self._p2p_cache.get(key)
