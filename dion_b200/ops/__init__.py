@@ -7,6 +7,7 @@ extension is missing the op raises.
 """
 from __future__ import annotations
 
+import itertools
 import math
 from typing import List, Optional, Sequence, Tuple
 
@@ -525,6 +526,46 @@ def col_normalize(R: Tensor, sumsq: Tensor, eps: float, out: Tensor) -> Tensor:
         out.copy_((R.float() / (sumsq.unsqueeze(-2).sqrt() + eps)).to(out.dtype))
         return out
     ext().col_normalize(R.contiguous(), sumsq.contiguous(), float(eps), out)
+    return out
+
+
+_REFILL_CALLS = itertools.count()
+_REFILL_STREAM_TAG = 0x5146 << 48  # keeps refill streams apart from the sketch's call counter
+
+
+def random_unit_columns_(Q: Tensor, key: Optional[int] = None, stream: Optional[int] = None) -> Tensor:
+    """Fill the 2-D (column-strided allowed) view ``Q`` with unit-norm Gaussian
+    columns: Philox normals, column sums of squares, column normalise (three
+    kernels, written straight into ``Q``). Keyed by the process seed and a
+    call counter unless given, so every rank that makes the same calls gets
+    the same columns. CPU tensors use torch's generator."""
+    rows, cols = Q.shape
+    if rows == 0 or cols == 0:
+        return Q
+    if not Q.is_cuda:
+        z = torch.randn(rows, cols, dtype=torch.float32)
+        Q.copy_((z / z.norm(dim=0, keepdim=True).clamp_min(1e-12)).to(Q.dtype))
+        return Q
+    key = torch.initial_seed() if key is None else key
+    stream = _REFILL_STREAM_TAG | next(_REFILL_CALLS) if stream is None else stream
+    z = philox_normal((1, rows, cols), key, stream, 1.0, Q.device)
+    if Q.stride(1) == 1 and Q.dtype in (torch.float32, torch.bfloat16):
+        return col_normalize(z, col_sumsq(z), 1e-12, Q.unsqueeze(0))[0]
+    Q.copy_(col_normalize(z, col_sumsq(z), 1e-12, torch.empty_like(z))[0])
+    return Q
+
+
+def col_normalize_2d(V: Tensor, eps: float = 1e-12, sumsq: Optional[Tensor] = None) -> Tensor:
+    """``V`` with unit-norm columns (norms from ``sumsq`` [cols] when given,
+    e.g. after an all-reduce), as a new tensor of V's dtype; column kernels
+    on CUDA."""
+    if not V.is_cuda:
+        sq = V.float().square().sum(dim=0) if sumsq is None else sumsq.float()
+        return V / sq.sqrt().clamp(min=eps).to(V.dtype)
+    Vf = V.float().contiguous().unsqueeze(0)
+    sq = col_sumsq(Vf) if sumsq is None else sumsq.float().contiguous().view(1, -1)
+    out = torch.empty(V.shape, device=V.device, dtype=V.dtype)
+    col_normalize(Vf, sq, eps, out.unsqueeze(0))
     return out
 
 

@@ -43,7 +43,14 @@ def quantize_int(x: float, q: int) -> int:
     return int(round(x / q) * q) if q > 1 else int(round(x))
 
 
+def _col_kernels(V: Tensor) -> bool:
+    return V.is_cuda and V.dim() == 2 and ops.has_ext()
+
+
 def col_norm(V: Tensor, eps: float = 1e-12) -> Tensor:
+    """Unit-norm columns (the column sum-of-squares / normalise kernels on CUDA)."""
+    if _col_kernels(V):
+        return ops.col_normalize_2d(V, eps)
     return V / torch.linalg.vector_norm(V.float(), dim=0).clamp(min=eps).to(V.dtype)
 
 
@@ -80,8 +87,15 @@ class LowRankEngine:
         return dist.get_world_size() if dist.is_initialized() else 1
 
     def col_norm_dist(self, V: Tensor, eps: float = 1e-12) -> Tensor:
-        sq = torch.linalg.vector_norm(V.float(), dim=0).pow(2)
+        """Columns normalised by their norms over all row shards (sums of
+        squares all-reduced)."""
+        if _col_kernels(V):
+            sq = ops.col_sumsq(V.float().contiguous().unsqueeze(0)).view(-1)
+        else:
+            sq = torch.linalg.vector_norm(V.float(), dim=0).pow(2)
         self.all_reduce(sq) if (self.pg is not None or dist.is_initialized()) else None
+        if _col_kernels(V):
+            return ops.col_normalize_2d(V, eps, sumsq=sq)
         return V / sq.sqrt().clamp(min=eps).to(V.dtype)
 
     # ---- power step
@@ -284,8 +298,11 @@ class LowRankOptimizer(Optimizer):
 
     @staticmethod
     def _refill(Qbuf: Tensor, lo: int, hi: int, gen: Optional[torch.Generator] = None) -> None:
-        """Fresh unit-norm Gaussian columns [lo, hi) of Qbuf."""
-        if hi > lo:
+        """Fresh unit-norm Gaussian columns [lo, hi) of Qbuf (on CUDA without
+        an explicit generator: the Philox + column-normalise kernels)."""
+        if hi > lo and gen is None and _col_kernels(Qbuf):
+            ops.random_unit_columns_(Qbuf[:, lo:hi])
+        elif hi > lo:
             Qbuf[:, lo:hi].copy_(F.normalize(
                 torch.randn(Qbuf.shape[0], hi - lo, device=Qbuf.device, dtype=Qbuf.dtype, generator=gen), dim=0))
 

@@ -197,8 +197,11 @@ class AdaDionV2(Dion):
             r_next = int(min(max(c["rank_min"], r_next), r_cap))
             if r_next > r:
                 Q = self._q_full[id(p)]
-                Q[:, r:r_next].copy_(F.normalize(
-                    torch.randn(Q.shape[0], r_next - r, device=Q.device, dtype=Q.dtype), dim=0))
+                if Q.is_cuda and ops.has_ext():
+                    ops.random_unit_columns_(Q[:, r:r_next])  # Philox + column-normalise kernels
+                else:
+                    Q[:, r:r_next].copy_(F.normalize(
+                        torch.randn(Q.shape[0], r_next - r, device=Q.device, dtype=Q.dtype), dim=0))
             st["r"] = r_next
 
     # ------------------------------------------------------------------ diagnostics
