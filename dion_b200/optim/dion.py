@@ -587,7 +587,10 @@ class Dion(Optimizer):
             R = self._all_reduce_replicate([R])[0]
         ops.dion_fixup_(P_all, R, Qb, nz)
         sumsq = ops.col_sumsq(R)
-        dist.all_reduce(sumsq, op=dist.ReduceOp.SUM, group=pg)
+        if heap is not None:
+            sumsq = self._p2p_sum(heap, sumsq, sets, W, me, P_all.size(1))
+        else:
+            dist.all_reduce(sumsq, op=dist.ReduceOp.SUM, group=pg)
         self._update(group, params, order, Mb, Qb, P_all, R, nz, t, sumsq)
         self._after_update(group, params, order, sumsq, ranks)
 
@@ -605,7 +608,27 @@ class Dion(Optimizer):
         if r % 4:
             return None
         slot = pd * r * 4
-        return heap_for(pg, 2 * W * sets * slot, "dion", Mb.device)
+        return heap_for(pg, 2 * W * sets * slot + W * sets * W * r * 4, "dion", Mb.device)
+
+    def _p2p_sum(self, heap, sumsq: Tensor, sets: int, W: int, me: int, pd: int) -> Tensor:
+        """All-reduce (sum) of the column sums of squares [sets*W, r] without
+        NCCL: every rank stores its copy into slot ``me`` of every rank's
+        sum region (after recv and P_all, so the next group's P stores cannot
+        overwrite slots still being summed), one device barrier, a fixed-order
+        sum of the W slots. Replaces ada_dion/optim/adadion_v2.py:1091-1096."""
+        r = sumsq.size(1)
+        nb = sets * W * r * 4
+        base = 2 * W * sets * pd * r * 4
+        key = ("p2p_sum", heap.uid, sets, W, pd, r)
+        ptrs = self._p2p_ptrs.get(key)
+        if ptrs is None:
+            ptrs = heap.ptr_tensor([heap.addr((me + 1 + i) % W, base + me * nb) for i in range(W)])
+            self._p2p_ptrs[key] = ptrs
+        heap.push(sumsq.contiguous(), ptrs)
+        heap.barrier()
+        out = torch.empty_like(sumsq)
+        heap.reduce_slots(heap.view(base, (W, sets * W, r), torch.float32), out, W)
+        return out
 
     def _p2p_power_orth(self, heap, group: dict, Mb: Tensor, Qb: Tensor, transposed: bool, sets: int, W: int,
                         me: int, my_ranks, compressed: bool) -> Tensor:
