@@ -6,7 +6,11 @@ mesh (FSDP2 layout). One step of
   * ``muon``: momentum, all-to-all to owners, 5 Newton-Schulz iterations with
     Keller Jordan's (3.4445, -4.7750, 2.0315), all-to-all back, update;
   * ``dion``: rank-1024 (fraction 1/4) power iteration, orthogonalisation,
-    error feedback, update.
+    error feedback, update;
+  * ``dion2``: top-L1 quarter of the rows of each momentum shard, rows sent
+    to the matrix owner, Newton-Schulz, rows back, selective decay;
+  * ``adadion_v2``: Dion with the adaptive rank schedule (effective rank of
+    the column norms, one host read per shape group per step).
 is timed on the device with CUDA events (max over ranks, mean over steps).
 
     python -m dion_b200.benchmarks.optimizer_bench --optimizer muon [--impl reference]
@@ -38,7 +42,7 @@ REF_PATH = os.path.join(os.path.dirname(os.path.dirname(HERE)), "baseline", "_re
 
 def parse(argv=None):
     p = argparse.ArgumentParser()
-    p.add_argument("--optimizer", choices=["muon", "dion"], default="muon")
+    p.add_argument("--optimizer", choices=["muon", "dion", "dion2", "adadion_v2"], default="muon")
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--steps", type=int, default=5)
     p.add_argument("--warmup", type=int, default=3)
@@ -81,10 +85,15 @@ def build_params(args, mesh):
 
 def build_optimizer(args, params, mesh, world):
     if args.impl == "ours":
-        from dion_b200.optim import Dion, Muon
+        from dion_b200.optim import AdaDionV2, Dion, Dion2, Muon
 
         if args.optimizer == "muon":
             return Muon(params, distributed_mesh=mesh, lr=0.02, mu=0.95, weight_decay=0.01, ns_coeffs="keller")
+        if args.optimizer == "dion2":
+            return Dion2(params, distributed_mesh=mesh, lr=0.02, fraction=args.rank_fraction, weight_decay=0.01)
+        if args.optimizer == "adadion_v2":
+            return AdaDionV2(params, outer_shard_mesh=mesh, lr=0.02, mu=0.95, weight_decay=0.01,
+                             adaptive_rank=True, rank_fraction_max=args.rank_fraction)
         return Dion(params, outer_shard_mesh=mesh, lr=0.02, mu=0.95, weight_decay=0.01,
                     rank_fraction=args.rank_fraction)
     sys.path.insert(0, REF_PATH)
@@ -103,12 +112,19 @@ def build_optimizer(args, params, mesh, world):
                     weight_decay=0.01, newton_schulz_func=keller)
     from ada_dion.optim.adadion_v2 import AdaDionV2
 
+    if args.optimizer == "adadion_v2":
+        return AdaDionV2(params, outer_shard_mesh=mesh, lr=0.02, mu=0.95, weight_decay=0.01, adaptive_rank=True,
+                         rank_fraction_max=args.rank_fraction)
     return AdaDionV2(params, outer_shard_mesh=mesh, lr=0.02, mu=0.95, weight_decay=0.01,
                      rank_fraction_max=args.rank_fraction)
 
 
 def main(argv=None):
     args = parse(argv)
+    if args.impl == "reference" and args.optimizer == "dion2":
+        print(json.dumps({"metric": "optimizer_step_ms", "optimizer": "dion2", "impl": "reference",
+                          "unavailable": "the reference environment has no Dion2 (dion.Dion2 is absent)"}))
+        return
     rank, world, local = _init()
     mesh = init_device_mesh("cuda", (world,), mesh_dim_names=("dp_shard",))
     params = build_params(args, mesh)
@@ -133,7 +149,7 @@ def main(argv=None):
             "metric": "optimizer_step_ms", "optimizer": args.optimizer, "impl": args.impl, "n_gpus": world,
             "ms": float(t[0]), "wall_ms": float(t[1]), "steps": args.steps, "warmup": args.warmup,
             "matrices": f"{args.n_square}x{args.dim}^2 + {args.n_wide}x{args.dim}x{args.wide} bf16, Shard(0)",
-            "rank_fraction": args.rank_fraction if args.optimizer == "dion" else None,
+            "rank_fraction": args.rank_fraction if args.optimizer != "muon" else None,
         }))
     dist.barrier()
     dist.destroy_process_group()
