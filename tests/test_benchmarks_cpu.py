@@ -145,3 +145,17 @@ def test_cifar10_benchmark_runs(tmp_path):
     for l in logs.values():
         assert l["eval/val_acc"] and all(v == v for v in l["train_loss"])
     assert (tmp_path / "results.json").exists() and (tmp_path / "cifar10.svg").exists()
+
+
+def test_optimizer_bench_cli_cases(capsys):
+    """Every optimizer case parses; the reference arm of Dion2 reports that
+    the reference environment has no Dion2 instead of failing."""
+    import json
+
+    from dion_b200.benchmarks import optimizer_bench as ob
+
+    for name in ("muon", "dion", "dion2", "adadion_v2"):
+        assert ob.parse(["--optimizer", name]).optimizer == name
+    ob.main(["--optimizer", "dion2", "--impl", "reference"])
+    line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and "unavailable" in line
