@@ -41,20 +41,23 @@ def save(folder: str, model, optimizers, step: int, model_only: bool = False) ->
     return path
 
 
+def _has_optimizer_state(path: str) -> bool:
+    """Whether the checkpoint at ``path`` holds optimizer entries (a
+    model-only save does not); read from the DCP metadata only."""
+    md = dcp.FileSystemReader(path).read_metadata()
+    return any(k.startswith("optimizer.") for k in md.state_dict_metadata)
+
+
 def load(path: str, model, optimizers=None) -> int:
+    """Load model (and, when the checkpoint has them, optimizer and step)
+    state; returns the saved step, 0 for a model-only checkpoint. Errors in
+    loading the optimizer state are raised, never skipped."""
     sd: Dict[str, Any] = {"model": get_model_state_dict(model)}
-    has_opt = optimizers is not None and os.path.exists(path)
+    has_opt = optimizers is not None and _has_optimizer_state(path)
     if has_opt:
         sd["optimizer"] = optimizers.state_dict()
         sd["train_state"] = {"step": torch.tensor(0)}
-    try:
-        dcp.load(sd, checkpoint_id=path)
-    except Exception:
-        if not has_opt:
-            raise
-        sd = {"model": get_model_state_dict(model)}
-        dcp.load(sd, checkpoint_id=path)
-        has_opt = False
+    dcp.load(sd, checkpoint_id=path)
     set_model_state_dict(model, sd["model"])
     if has_opt:
         optimizers.load_state_dict(sd["optimizer"])

@@ -199,3 +199,34 @@ def test_train_module_flag():
     b = _load_config("ada_dion.integration.config_registry", "llama3_debug_dion")
     c = _load_config("dion_b200.integration.config_registry", "llama3_debug_dion")
     assert a.optimizer.name == b.optimizer.name == c.optimizer.name == "Dion"
+
+
+def test_checkpoint_load_model_only_and_full(tmp_path):
+    """A model-only checkpoint loads into a job with optimizers (step 0,
+    optimizer untouched); a full one restores the optimizer and step; an
+    optimizer state that does not fit the checkpoint raises instead of being
+    skipped."""
+    from dion_b200 import checkpoint as ckpt
+
+    torch.manual_seed(0)
+    m = _MockLlama()
+    cfg = HybridOptimizersContainer.Config(name="Muon", lr=0.01)
+    c = HybridOptimizersContainer(cfg, model_parts=[m])
+    x = torch.randint(0, 64, (3,))
+    out = m.output(m.layers["0"].attention.wq(m.tok_embeddings(x)))
+    (out.sum() + sum(p.sum() for p in m.parameters())).backward()  # every parameter gets a gradient
+    c.step()
+    ckpt.save(str(tmp_path), m, c, step=3, model_only=True)
+    ckpt.save(str(tmp_path), m, c, step=5)
+    m2 = _MockLlama()
+    c2 = HybridOptimizersContainer(cfg, model_parts=[m2])
+    assert ckpt.load(str(tmp_path / "step-3"), m2, c2) == 0
+    assert all(torch.equal(a, b) for a, b in zip(m.state_dict().values(), m2.state_dict().values()))
+    assert ckpt.load(str(tmp_path / "step-5"), m2, c2) == 5
+    mom = [v for k, v in c2.state_dict().items() if k.endswith("momentum_buffer") or k.endswith("momentum")]
+    assert mom and any(float(t.abs().sum()) > 0 for t in mom)
+    c3 = HybridOptimizersContainer(HybridOptimizersContainer.Config(name="AdamW", lr=0.01), model_parts=[_MockLlama()])
+    from torch.distributed.checkpoint.api import CheckpointException  # a BaseException subclass
+
+    with pytest.raises((CheckpointException, RuntimeError, KeyError)):
+        ckpt.load(str(tmp_path / "step-5"), _MockLlama(), c3)
