@@ -51,6 +51,8 @@ def parse(argv=None):
     p.add_argument("--dim", type=int, default=4096)
     p.add_argument("--wide", type=int, default=14336)
     p.add_argument("--rank-fraction", type=float, default=0.25)
+    p.add_argument("--replicated", action="store_true",
+                   help="plain replicated tensors (DDP layout) instead of Shard(0) DTensors")
     return p.parse_args(argv)
 
 
@@ -74,9 +76,13 @@ def build_params(args, mesh):
     params = []
     for shp in shapes:
         full = torch.randn(shp, device="cuda", generator=gen, dtype=torch.float32).to(torch.bfloat16)
-        p = torch.nn.Parameter(distribute_tensor(full, mesh, [Shard(0)]))
         g = torch.randn(shp, device="cuda", generator=gen, dtype=torch.float32).to(torch.bfloat16)
-        p.grad = distribute_tensor(g, mesh, [Shard(0)])
+        if args.replicated:
+            p = torch.nn.Parameter(full.clone())
+            p.grad = g.clone()
+        else:
+            p = torch.nn.Parameter(distribute_tensor(full, mesh, [Shard(0)]))
+            p.grad = distribute_tensor(g, mesh, [Shard(0)])
         del full, g
         params.append(p)
     torch.cuda.empty_cache()
@@ -148,7 +154,9 @@ def main(argv=None):
         print(json.dumps({
             "metric": "optimizer_step_ms", "optimizer": args.optimizer, "impl": args.impl, "n_gpus": world,
             "ms": float(t[0]), "wall_ms": float(t[1]), "steps": args.steps, "warmup": args.warmup,
-            "matrices": f"{args.n_square}x{args.dim}^2 + {args.n_wide}x{args.dim}x{args.wide} bf16, Shard(0)",
+            "matrices": f"{args.n_square}x{args.dim}^2 + {args.n_wide}x{args.dim}x{args.wide} bf16, "
+                        + ("replicated" if args.replicated else "Shard(0)"),
+            "p2p": os.environ.get("DION_B200_P2P", "1") != "0",
             "rank_fraction": args.rank_fraction if args.optimizer != "muon" else None,
         }))
     dist.barrier()
