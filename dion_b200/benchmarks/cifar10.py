@@ -215,9 +215,9 @@ def run_one(cfg: dict, data, device: torch.device, rank: int = 0, world: int = 1
             opt.zero_grad(set_to_none=True)
             sched.step()
             step += 1
-            ep_loss += float(loss)
+            ep_loss += float(loss.detach())
             if step % cfg["log_freq"] == 0 and rank == 0:
-                row = {"step": step, "epoch": epoch, "train_loss": float(loss), "lr": sched.get_last_lr()[0],
+                row = {"step": step, "epoch": epoch, "train_loss": float(loss.detach()), "lr": sched.get_last_lr()[0],
                        "grad_norm": gnorm, "elapsed": time.time() - t0,
                        "throughput": step * bs * world / (time.time() - t0),
                        "mem_mb": torch.cuda.max_memory_allocated(device) / 1e6 if device.type == "cuda" else 0.0}

@@ -87,7 +87,8 @@ def test_plots_write_svg(tmp_path):
     out = plots.save_all_plots(str(tmp_path), runs=runs, dion_data=dd, dion2_data=d2, adadion_data=ad)
     assert len(out) == 10
     for p in out:
-        s = open(p).read()
+        with open(p) as fh:
+            s = fh.read()
         assert s.startswith("<svg") and s.rstrip().endswith("</svg>")
 
 
@@ -108,7 +109,8 @@ def test_logparse(tmp_path):
                     "tflops: 400.50  mfu: 20.00%\n")
     out = logparse.generate_plots([str(log), str(ours)], str(tmp_path / "plots"), tokens_per_step=4096)
     assert any(p.endswith(".svg") for p in out)
-    assert "| muon_run | muon | 10 | 7.1234 | 98,765 |" in open(out[-1]).read()
+    with open(out[-1]) as fh:
+        assert "| muon_run | muon | 10 | 7.1234 | 98,765 |" in fh.read()
 
 
 def test_optimizer_phases_show_in_profiler_trace(tmp_path):

@@ -123,7 +123,8 @@ def test_train_entry_and_metrics(tmp_path):
                          "--training.seq_len", "32", "--training.local_batch_size", "2",
                          "--metrics.save_jsonl", str(out)])
     assert len(losses) == 2 and all(math.isfinite(v) for v in losses)
-    recs = [json.loads(l) for l in open(out / "optimizer_metrics.jsonl")]
+    with open(out / "optimizer_metrics.jsonl") as fh:
+        recs = [json.loads(l) for l in fh]
     assert [r["step"] for r in recs] == [2, 4] and recs[0]["opt_0/type"] == "Muon"
 
 
@@ -186,9 +187,11 @@ def test_launch_scripts_are_valid_bash():
     for f in files:
         r = subprocess.run(["bash", "-n", f], capture_output=True, text=True)
         assert r.returncode == 0, (f, r.stderr)
-        text = open(f).read()
+        with open(f) as fh:
+            text = fh.read()
         assert "torchtitan" not in text
-    single = open(os.path.join(root, "run_single_node.sh")).read()
+    with open(os.path.join(root, "run_single_node.sh")) as fh:
+        single = fh.read()
     assert "-m dion_b200.train" in single and "--parallelism.data_parallel_shard_degree" in single
 
 

@@ -18,7 +18,8 @@ def test_gsdion_ladder_tiny(tmp_path):
                               str(tmp_path), "--data-dir", str(tmp_path / "none")])
     assert set(res) == {"1_dion_baseline", "2_ranknorm_lrcomp", "7_full_gsdion"}
     assert res["2_ranknorm_lrcomp"]["lr"] == pytest.approx(0.02 * 8 ** 0.5)
-    assert json.load(open(tmp_path / "gsdion_ladder.json"))["data"] == "synthetic"
+    with open(tmp_path / "gsdion_ladder.json") as fh:
+        assert json.load(fh)["data"] == "synthetic"
 
 
 def test_seed_confirmation_tiny(tmp_path):
