@@ -130,11 +130,26 @@ def bench_linalg(small: bool):
     A = torch.randn(b, m, r, device="cuda")
     ms = _time(lambda: LA.qr_r(A), warmup=1, iters=3)
     ref = _time(lambda: torch.linalg.qr(A, mode="r"), warmup=1, iters=3)
-    out.append({"case": f"qr_r_{b}x{m}x{r}", "ms": ms, "ref_ms": ref})
+
+    def unblocked_qr():
+        W, R = A.clone(), torch.empty(b, r, r, device="cuda")
+        ops.ext().qr_r(W, R)
+
+    old = _time(unblocked_qr, warmup=1, iters=3)
+    out.append({"case": f"qr_r_{b}x{m}x{r}", "ms": ms, "ref_ms": ref, "unblocked_ms": old})
+    if not small:
+        A6 = A[:6].contiguous()  # the matrices one rank of 8 factors per shape group (48 matrices)
+        out.append({"case": f"qr_r_6x{m}x{r}", "ms": _time(lambda: LA.qr_r(A6), warmup=1, iters=3)})
     G = A.mT @ A / m + torch.eye(r, device="cuda")
     ms = _time(lambda: LA.cholesky_lower(G), warmup=1, iters=3)
     ref = _time(lambda: torch.linalg.cholesky_ex(G), warmup=1, iters=3)
-    out.append({"case": f"cholesky_{b}x{r}", "ms": ms, "ref_ms": ref})
+
+    def unblocked_chol():
+        L, info = G.clone(), torch.empty(b, dtype=torch.int32, device="cuda")
+        ops.ext().cholesky_lower(L, info)
+
+    old = _time(unblocked_chol, warmup=1, iters=3)
+    out.append({"case": f"cholesky_{b}x{r}", "ms": ms, "ref_ms": ref, "unblocked_ms": old})
     L = torch.linalg.cholesky(G)
     ms = _time(lambda: LA.tri_inv_lower(L), warmup=1, iters=3)
     eye = torch.eye(r, device="cuda").expand(b, r, r)

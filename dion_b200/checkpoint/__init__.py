@@ -31,7 +31,10 @@ def _sync_for_checkpoint(optimizers) -> None:
 
 
 def save(folder: str, model, optimizers, step: int, model_only: bool = False) -> str:
-    path = os.path.join(folder, f"step-{step}")
+    """Write a DCP checkpoint. Full checkpoints go to ``step-<N>``; a
+    model-only save goes to ``step-<N>-model``, a name that resuming never
+    picks (it holds no optimizer state to resume from)."""
+    path = os.path.join(folder, f"step-{step}-model" if model_only else f"step-{step}")
     _sync_for_checkpoint(optimizers)
     sd: Dict[str, Any] = {"model": get_model_state_dict(model)}
     if not model_only:
@@ -74,6 +77,8 @@ class CheckpointManager:
         self.model_only_last = model_only_last
 
     def latest(self) -> Optional[str]:
+        """Newest full checkpoint (``step-<N>``); model-only final saves
+        (``step-<N>-model``) are not resume points."""
         if not os.path.isdir(self.folder):
             return None
         steps = [int(m.group(1)) for d in os.listdir(self.folder) if (m := re.fullmatch(r"step-(\d+)", d))]
@@ -85,8 +90,16 @@ class CheckpointManager:
             trainer.step_idx = load(p, self.model, self.optimizers)
 
     def maybe_save(self, trainer, step: int, final: bool = False) -> Optional[str]:
-        if final:
-            return save(self.folder, self.model, self.optimizers, step, model_only=self.model_only_last)
+        """Full checkpoint every ``interval`` steps (the final step included);
+        the final step additionally gets a model-only export when
+        ``model_only_last``, or a full checkpoint when that step is off the
+        interval and ``model_only_last`` is False."""
+        path = None
         if self.interval > 0 and step % self.interval == 0:
-            return save(self.folder, self.model, self.optimizers, step)
-        return None
+            path = save(self.folder, self.model, self.optimizers, step)
+        if final:
+            if self.model_only_last:
+                path = save(self.folder, self.model, self.optimizers, step, model_only=True)
+            elif path is None:
+                path = save(self.folder, self.model, self.optimizers, step)
+        return path

@@ -60,6 +60,8 @@ void effective_rank(const at::Tensor& sumsq, const at::Tensor& slots, const at::
 void cholesky_lower(at::Tensor& A, at::Tensor& info);
 void tri_inv_lower(const at::Tensor& S, at::Tensor& Z, bool upper);
 void qr_r(at::Tensor& A, at::Tensor& R);
+void qr_r_blocked(at::Tensor& A, at::Tensor& R);
+void cholesky_blocked(at::Tensor& A, at::Tensor& info);
 }  // namespace bdion
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -110,6 +112,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("cholesky_lower", &bdion::cholesky_lower);
   m.def("tri_inv_lower", &bdion::tri_inv_lower);
   m.def("qr_r", &bdion::qr_r);
+  m.def("qr_r_blocked", &bdion::qr_r_blocked, "blocked Householder QR (R only), tcgen05 3xTF32 trailing update");
+  m.def("cholesky_blocked", &bdion::cholesky_blocked, "blocked Cholesky, tcgen05 3xTF32 trailing SYRK");
   m.def("status_read", &bdion::status_read);
   m.def("status_clear", &bdion::status_clear);
   m.def("set_wait_limit_ns", &bdion::set_wait_limit_ns);

@@ -485,6 +485,8 @@ extern "C" __attribute__((visibility("default"))) int bdion_batched_sumsq_noallo
                  (long long)batch, (long long)numel, (long long)(batch * chunks_per), BDION_NOALLOC_MAX_PARTIALS);
     return BDION_NOALLOC_TOO_LARGE;
   }
+  // an error left by earlier work is reported as such and stays set (peek, not get)
+  if (cudaPeekAtLastError() != cudaSuccess) return BDION_NOALLOC_PENDING_ERROR;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return BDION_NOALLOC_SETUP_FAILED;
   float* scratch = noalloc_scratch(dev);
@@ -512,9 +514,9 @@ extern "C" __attribute__((visibility("default"))) int bdion_batched_sumsq_noallo
       sumsq_kernel<float><<<chunks, kThreads, 0, s>>>(a, vec ? 1 : 0, part);
     else
       sumsq_kernel<__nv_bfloat16><<<chunks, kThreads, 0, s>>>(a, vec ? 1 : 0, part);
-    if (cudaGetLastError() != cudaSuccess) return BDION_NOALLOC_LAUNCH_FAILED;
+    if (cudaPeekAtLastError() != cudaSuccess) return BDION_NOALLOC_LAUNCH_FAILED;
     finalize_sumsq_kernel<<<n, kThreads, 0, s>>>(a, part, out + b0, nullptr, 0.f);
-    if (cudaGetLastError() != cudaSuccess) return BDION_NOALLOC_LAUNCH_FAILED;
+    if (cudaPeekAtLastError() != cudaSuccess) return BDION_NOALLOC_LAUNCH_FAILED;
     note_launch(2);
     used += chunks;
   }

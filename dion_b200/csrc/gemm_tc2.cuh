@@ -91,8 +91,9 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* empty_bar = bars + S;         // both CTAs
   uint64_t* tfull_bar = bars + 2 * S;     // both CTAs
   uint64_t* tempty_bar = bars + 2 * S + 2;  // used in the leader (8 arrivals: 4 warps x 2 CTAs)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 4);
-  volatile int* s_abort = reinterpret_cast<volatile int*>(bars + 2 * S + 5);
+  uint64_t* drain_bar = bars + 2 * S + 4;  // leader: completion of the MMAs issued before an abort
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(bars + 2 * S + 6);
   float* staging = reinterpret_cast<float*>(smem + S * Cfg::kStageBytes + 256);
 
   const int warp = threadIdx.x / 32;
@@ -111,6 +112,7 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&tfull_bar[i], 1);
       mbar_init(&tempty_bar[i], 8);
     }
+    mbar_init(drain_bar, 1);
     *s_abort = 0;
     fence_mbar_init();
   }
@@ -136,6 +138,7 @@ __global__ void __launch_bounds__(192, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      long issued = 0;
       for (int t = pair; t < args.total_tiles && ok; t += npairs) {
         int b, tm, tn;
         map_tile2<BN>(args, t, b, tm, tn);
@@ -165,17 +168,28 @@ __global__ void __launch_bounds__(192, 1)
             for (int h = 0; h < kHalfN / kBK; ++h)
               tma_load_3d_pair(&tmB, lbar, b_dst + h * kBoxBytes, col0 + h * kBK, kb * kBK, b);
           }
+          ++issued;
           if (++stage == S) {
             stage = 0;
             phase ^= 1;
           }
         }
       }
-      if (!ok) {
-        // loads already issued complete on the leader's barrier; give them time before the
-        // final cluster barrier and exit (bounded)
-        const uint64_t t0 = globaltimer_ns();
-        while (globaltimer_ns() - t0 < 1000000ull) {
+      if (!ok && half == 0) {
+        // Drain: both CTAs' loads of a stage complete on the leader's full barrier (its
+        // expect_tx counts both halves), so the leader waits (bounded) for the phases of
+        // the last S stages it armed. The peer CTA cannot wait on a remote barrier; it is
+        // held at the final cluster barrier until this drain is over.
+        int st = stage;
+        uint32_t ph = phase;
+        for (long i = 0; i < min(issued, (long)S); ++i) {
+          if (--st < 0) {
+            st = S - 1;
+            ph ^= 1;
+          }
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(&full_bar[st], ph) && globaltimer_ns() - t0 < 100000000ull) {
+          }
         }
       }
     }
@@ -187,6 +201,7 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t phase = 0;
       int local_tile = 0;
       bool ok = true;
+      bool issued_any = false;
       for (int t = pair; t < args.total_tiles && ok; t += npairs, ++local_tile) {
         const int acc = local_tile & 1;
         const uint32_t acc_phase = (local_tile >> 1) & 1;
@@ -217,6 +232,7 @@ __global__ void __launch_bounds__(192, 1)
             else
               umma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
           }
+          issued_any = true;
           umma_commit_pair(&empty_bar[stage], (uint16_t)(3u << leader));
           if (++stage == S) {
             stage = 0;
@@ -226,10 +242,12 @@ __global__ void __launch_bounds__(192, 1)
         if (!ok) break;
         umma_commit_pair(&tfull_bar[acc], (uint16_t)(3u << leader));
       }
-      if (!ok) {
-        // let MMAs already issued finish before TMEM is released (bounded)
+      if (!ok && issued_any) {
+        // Wait (bounded) for the MMAs already issued before TMEM is released: a commit
+        // to the leader's own drain barrier arrives once all of them have completed.
+        umma_commit_pair(drain_bar, (uint16_t)(1u << leader));
         const uint64_t t0 = globaltimer_ns();
-        while (globaltimer_ns() - t0 < 1000000ull) {
+        while (!mbar_try_wait(drain_bar, 0) && globaltimer_ns() - t0 < 100000000ull) {
         }
       }
     }

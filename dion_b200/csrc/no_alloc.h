@@ -30,6 +30,7 @@ extern "C" {
 #define BDION_NOALLOC_TOO_LARGE (-2)
 #define BDION_NOALLOC_SETUP_FAILED (-3)
 #define BDION_NOALLOC_LAUNCH_FAILED (-4)
+#define BDION_NOALLOC_PENDING_ERROR (-5)
 
 // Per-matrix sum of squares of a batch of equally sized tensors:
 //   out[b] = sum_i x[b * stride + i]^2   for b < batch, i < numel
@@ -38,6 +39,12 @@ extern "C" {
 // out: device pointer to `batch` fp32 results;
 // stream: the cudaStream_t to launch on (NULL = the legacy default stream).
 // The work is queued on `stream`; the function does not synchronise.
+//
+// Errors: a CUDA error that is already pending when the call starts (left by
+// earlier, unrelated work) is not this call's failure: the call then launches
+// nothing, returns BDION_NOALLOC_PENDING_ERROR and leaves that error set for
+// the caller's own check. A launch that fails returns
+// BDION_NOALLOC_LAUNCH_FAILED, also leaving the CUDA error set.
 //
 // Same kernels and summation order as the extension's multi_sumsq op, so the
 // results match it bit for bit.

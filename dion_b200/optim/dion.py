@@ -33,7 +33,7 @@ from __future__ import annotations
 
 import math
 from dataclasses import dataclass
-from typing import Any, Dict, List, Optional, Tuple, Union
+from typing import Any, Dict, Iterator, List, Optional, Tuple, Union
 
 import torch
 import torch.distributed as dist
@@ -45,7 +45,7 @@ from torch.distributed.tensor import DTensor, Partial, Placement, Replicate, Sha
 from torch.optim.optimizer import Optimizer, ParamsT
 
 from .. import ops
-from ._utils import group_by_signature, scalar_update, to_local
+from ._utils import AsyncRuntime, AsyncTask, group_by_signature, scalar_update, to_local
 from ..utils.trace import phase
 from .linalg import orthogonalize
 
@@ -55,6 +55,14 @@ except ImportError:  # pragma: no cover
     _StridedShard = None
 
 __all__ = ["Dion", "DionMixedPrecisionConfig", "DionParamConfig"]
+
+
+def _sync_task(name: str, fn, *args):
+    """A task that does all its work on its first step (no collective to overlap)."""
+    with phase(name):
+        fn(*args)
+    return
+    yield  # noqa: unreachable -- makes this a generator
 
 
 @dataclass
@@ -110,33 +118,33 @@ class Dion(Optimizer):
         mixed_precision_config: Optional[DionMixedPrecisionConfig] = None,
     ):
         if lr < 0.0:
-            raise ValueError(f"Invalid learning rate: {lr}")
+            raise ValueError(f"lr must be non-negative, got {lr}")
         if mu < 0.0:
-            raise ValueError(f"Invalid momentum factor (mu): {mu}")
+            raise ValueError(f"mu must be non-negative, got {mu}")
         if len(betas) != 2 or betas[0] < 0.0 or betas[1] < 0.0:
-            raise ValueError(f"Invalid betas: {betas}")
+            raise ValueError(f"betas must be two non-negative numbers, got {betas}")
         if weight_decay < 0.0:
-            raise ValueError(f"Invalid weight_decay value: {weight_decay}")
+            raise ValueError(f"weight_decay must be non-negative, got {weight_decay}")
         if rank_fraction <= 0 or rank_fraction > 1:
-            raise ValueError(f"Invalid rank fraction: {rank_fraction}")
+            raise ValueError(f"rank_fraction must lie in (0, 1], got {rank_fraction}")
         if rank_multiple_of <= 0:
-            raise ValueError(f"Invalid rank multiple of: {rank_multiple_of}")
+            raise ValueError(f"rank_multiple_of must be a positive integer, got {rank_multiple_of}")
         if power_iters != 1:
-            raise ValueError("Async Dion only supports power_iters=1")
+            raise ValueError(f"this Dion runs one power iteration per step (power_iters=1), got {power_iters}")
         if qr_method != "rcqr":
-            raise ValueError("Async Dion only supports qr_method='rcqr'")
+            raise ValueError(f"this Dion orthogonalises with randomised Cholesky QR only (qr_method='rcqr'), got {qr_method!r}")
         if replicate_mesh is not None and not isinstance(replicate_mesh, (DeviceMesh, ProcessGroup)):
-            raise TypeError(f"Replicate mesh must be a DeviceMesh or ProcessGroup, but got {type(replicate_mesh)}.")
+            raise TypeError(f"replicate_mesh: expected a DeviceMesh or a ProcessGroup, not {type(replicate_mesh).__name__}")
         for name, mesh in (("Outer", outer_shard_mesh), ("Inner", inner_shard_mesh)):
             if mesh is not None:
                 if not isinstance(mesh, DeviceMesh):
-                    raise TypeError(f"{name} shard mesh must be a DeviceMesh, but got {type(mesh)}.")
+                    raise TypeError(f"{name.lower()}_shard_mesh: expected a DeviceMesh, not {type(mesh).__name__}")
                 if mesh.ndim != 1:
-                    raise ValueError(f"{name} shard mesh must be 1D, but got {mesh.ndim}D. Try using a 1D sub-mesh.")
+                    raise ValueError(f"{name.lower()}_shard_mesh has {mesh.ndim} dimensions; pass the 1-D sub-mesh of the sharding dimension")
                 if mesh == replicate_mesh:
-                    raise ValueError(f"{name} shard mesh must be different from replicate mesh.")
+                    raise ValueError(f"{name.lower()}_shard_mesh and replicate_mesh are the same mesh; they must differ")
         if inner_shard_mesh is not None and inner_shard_mesh == outer_shard_mesh:
-            raise ValueError("Outer and inner shard meshes must be different.")
+            raise ValueError("outer_shard_mesh and inner_shard_mesh are the same mesh; they must differ")
 
         defaults = dict(
             rank_fraction=rank_fraction,
@@ -172,6 +180,8 @@ class Dion(Optimizer):
         self._mixed_precision_config = mixed_precision_config or DionMixedPrecisionConfig()
         self._arenas: Dict[Tuple, Dict[str, Any]] = {}
         self._p2p_ptrs: Dict[Tuple, Any] = {}
+        # signature sets in flight at once (the reference keeps three, adadion_v2.py:286)
+        self._max_concurrent_tasks = 3
         self._q_init_calls = 0
 
     # ------------------------------------------------------------------ step
@@ -183,14 +193,20 @@ class Dion(Optimizer):
                 loss = closure()
         for group in self.param_groups:
             group["step"] += 1
+        # Dion shape groups run as tasks, up to three in flight: a task yields
+        # after issuing an asynchronous collective, so that collective overlaps
+        # the next task's GEMMs (ada_dion/optim/adadion_v2.py:284-287,
+        # ada_dion/optim/dion_utils.py:121-145)
+        dion_groups = [(g, [p for p in g["params"] if p.grad is not None]) for g in self.param_groups
+                       if g["algorithm"] == "dion"]
+        AsyncRuntime((t for g, ps in dion_groups if ps for t in self._dion_tasks(g, ps)),
+                     max_concurrent_tasks=self._max_concurrent_tasks).run()
         for group in self.param_groups:
             algo = group["algorithm"]
             params = [p for p in group["params"] if p.grad is not None]
-            if not params:
+            if not params or algo == "dion":
                 continue
-            if algo == "dion":
-                self._dion_group(group, params)
-            elif algo in ("adamw", "lion"):
+            if algo in ("adamw", "lion"):
                 states = [self._get_or_initialize_state(p, group) for p in params]
                 grads = [p.grad for p in params]
                 if self._replicate_mesh is not None and self._replicate_mesh_grad_sync:
@@ -219,14 +235,14 @@ class Dion(Optimizer):
         if x in self._param_config:
             return self._param_config[x]
         if x.ndim > 2:
-            raise NotImplementedError(f"Tensors with more than 2 dimensions are not supported. Got {x.ndim}D tensor.")
+            raise NotImplementedError(f"Dion handles matrices (at most 2 dimensions); this parameter has {x.ndim}")
         using_mesh = any(isinstance(m, DeviceMesh) for m in (self._replicate_mesh, self._outer_shard_mesh,
                                                                self._inner_shard_mesh))
         if using_mesh and not isinstance(x, DTensor):
-            raise TypeError("When using DeviceMesh, all parameters must be DTensor.")
+            raise TypeError("with a DeviceMesh configured, every Dion parameter has to be a DTensor")
         if isinstance(self._replicate_mesh, ProcessGroup) and isinstance(x, DTensor):
             raise TypeError(
-                "When using DTensor parameters, the data parallel group must be specified by a DeviceMesh instead of ProcessGroup."
+                "DTensor parameters need the replicate group as a DeviceMesh; a ProcessGroup was given"
             )
         cfg = DionParamConfig()
         if x.ndim == 2:
@@ -238,13 +254,14 @@ class Dion(Optimizer):
             for mdim, pl in enumerate(x.placements):
                 if _StridedShard is not None and isinstance(pl, _StridedShard):
                     raise NotImplementedError(
-                        "StridedShard is not supported. Ensure that FSDP and TP shard different dimensions of each matrix."
+                        "a strided-sharded matrix (_StridedShard) cannot be orthogonalised per shard: let FSDP and TP "
+                        "shard different dimensions of each matrix"
                     )
                 if not pl.is_shard():
                     continue
                 tdim = pl.dim
                 if used[tdim] is not None:
-                    raise RuntimeError(f"Got double-sharded DTensor for tensor dimension {tdim}.")
+                    raise RuntimeError(f"tensor dimension {tdim} is sharded over two mesh dimensions")
                 used[tdim] = mdim
                 ranks = dist.get_process_group_ranks(mesh.get_group(mdim))
                 outer = ranks == self._outer_shard_ranks
@@ -254,10 +271,10 @@ class Dion(Optimizer):
                 if inner:
                     cfg.inner_shard_tensor_dim, cfg.inner_shard_mesh_dim = tdim, mdim
                 if outer and inner:
-                    raise RuntimeError("Cannot have outer and inner sharding over the same process group.")
+                    raise RuntimeError("the outer and inner shardings resolve to one process group")
                 if mesh.size(mdim) > 1 and not outer and not inner:
                     raise RuntimeError(
-                        f"Got DTensor sharded on unrecognized mesh_dim={mdim}, which does not match outer_shard_mesh or inner_shard_mesh."
+                        f"mesh dimension {mdim} shards this parameter but is neither the outer nor the inner shard mesh"
                     )
             if cfg.inner_shard_tensor_dim == 0 or cfg.outer_shard_tensor_dim == 1:
                 cfg.is_transposed = False
@@ -309,8 +326,8 @@ class Dion(Optimizer):
         p0 = params[0]
         if p0.ndim != 2:
             raise ValueError(
-                f"Expected Dion parameters to be 2D matrix, but got {p0.ndim}D. "
-                "For scalar parameters, set 'algorithm' to 'lion' or 'adamw' when creating param group."
+                f"the Dion algorithm updates matrices; this group holds a {p0.ndim}-D parameter (put vectors and "
+                "scalars in a group with algorithm='adamw' or 'lion')"
             )
         cfg = self._get_dion_param_config(p0)
         m, n = p0.shape
@@ -414,6 +431,21 @@ class Dion(Optimizer):
         else:
             dist.broadcast(t, group=rm, group_src=0)
 
+    def _all_reduce_replicate_async(self, ts: List[Tensor]):
+        """Generator form of the replicate-mesh average (in place): issues one
+        coalesced asynchronous all-reduce, yields, then waits for it."""
+        rm = self._replicate_mesh
+        if rm is None:
+            return ts
+        pg = _group_of(rm)
+        ts = [t if t.is_contiguous() else t.contiguous() for t in ts]
+        with dist._coalescing_manager(group=pg, async_ops=True) as cm:
+            for t in ts:
+                dist.all_reduce(t, op=dist.ReduceOp.AVG, group=pg)
+        yield
+        cm.wait()
+        return ts
+
     def _all_reduce_replicate(self, ts: List[Tensor], op: str = "avg") -> List[Tensor]:
         rm = self._replicate_mesh
         if rm is None:
@@ -424,19 +456,24 @@ class Dion(Optimizer):
         return [x.wait() if hasattr(x, "wait") else x for x in funcol.all_reduce_coalesced(ts, reduceOp=op, group=pg)]
 
     # ------------------------------------------------------------------ dion
-    def _dion_group(self, group: dict, params: List[Tensor]) -> None:
+    def _dion_tasks(self, group: dict, params: List[Tensor]) -> Iterator[AsyncTask]:
+        """One task per same-signature set of this group (created lazily, so
+        the runtime holds at most ``max_concurrent_tasks`` sets' buffers)."""
         for same in group_by_signature(params).values():
             cfg = self._get_dion_param_config(same[0])
             shape = "x".join(str(d) for d in same[0].shape)
             if cfg.inner_shard_mesh_dim is not None:
-                with phase(f"dion/fsdp_tp/{shape}"):
-                    self._dion_fsdp_tp(group, same, cfg)
+                yield AsyncTask(_sync_task(f"dion/fsdp_tp/{shape}", self._dion_fsdp_tp, group, same, cfg))
             elif cfg.outer_shard_mesh_dim is not None and self._outer_shard_mesh.size() > 1:
-                with phase(f"dion/sharded/{shape}"):
-                    self._dion_sharded(group, same, cfg)
+                yield AsyncTask(self._dion_sharded_gen(group, same, cfg, f"dion/sharded/{shape}"))
             else:
-                with phase(f"dion/replicated/{shape}"):
-                    self._dion_replicated(group, same, cfg)
+                yield AsyncTask(self._dion_replicated_gen(group, same, cfg, f"dion/replicated/{shape}"))
+
+    def _dion_group(self, group: dict, params: List[Tensor]) -> None:
+        """All of one group's sets, one after the other (no overlap)."""
+        for t in self._dion_tasks(group, params):
+            while t.step():
+                pass
 
     # hooks overridden by the adaptive-rank subclass
     def _active_q(self, params, order, Qb):
@@ -504,6 +541,12 @@ class Dion(Optimizer):
 
     # ---- single device / DDP (replicated parameters)
     def _dion_replicated(self, group: dict, params: List[Tensor], cfg: DionParamConfig) -> None:
+        for _ in self._dion_replicated_gen(group, params, cfg, "dion/replicated"):
+            pass
+
+    def _dion_replicated_gen(self, group: dict, params: List[Tensor], cfg: DionParamConfig, name: str):
+        """Single device / DDP / HSDP-replicated update of one signature set;
+        yields after each asynchronous collective."""
         n = len(params)
         order = list(range(n))
         Mb, Qb = self._arena(params, group, order, n)
@@ -514,11 +557,12 @@ class Dion(Optimizer):
         multi = rm is not None and world > 1
         compressed = self._replicate_mesh_grad_sync and cfg.compressed_all_reduce and multi
         if self._replicate_mesh_grad_sync and not cfg.compressed_all_reduce and multi:
-            G = self._all_reduce_replicate(G)
-        nz = ops.dion_momentum_add_(list(Mb.unbind(0)), G)
-        t = cfg.is_transposed
-        P = self._power_p(Mb, Qb, t)
-        pd, r = P.shape[1:]
+            G = yield from self._all_reduce_replicate_async(G)
+        with phase(name):
+            nz = ops.dion_momentum_add_(list(Mb.unbind(0)), G)
+            t = cfg.is_transposed
+            P = self._power_p(Mb, Qb, t)
+            pd, r = P.shape[1:]
         if multi:
             # each replica orthogonalises every world-th matrix, then all-gather
             pg = _group_of(rm)
@@ -529,26 +573,43 @@ class Dion(Optimizer):
             Pv = Pp.view(sets, world, pd, r).transpose(0, 1).contiguous()  # [world, sets, pd, r]
             if compressed:
                 mine = torch.empty((sets, pd, r), device=P.device, dtype=P.dtype)
-                dist.reduce_scatter_tensor(mine, Pv.view(world * sets, pd, r), op=dist.ReduceOp.AVG, group=pg)
+                work = dist.reduce_scatter_tensor(mine, Pv.view(world * sets, pd, r), op=dist.ReduceOp.AVG,
+                                                  group=pg, async_op=True)
+                yield
+                work.wait()
             else:
                 mine = Pv[rank].contiguous()
-            mine = self._orth(mine, group, None if ranks is None else
-                              [ranks[s * world + rank] if s * world + rank < n else 0 for s in range(sets)])
+            with phase(name):
+                mine = self._orth(mine, group, None if ranks is None else
+                                  [ranks[s * world + rank] if s * world + rank < n else 0 for s in range(sets)])
             allp = torch.empty((world, sets, pd, r), device=P.device, dtype=P.dtype)
-            dist.all_gather_into_tensor(allp.view(world * sets, pd, r), mine.contiguous(), group=pg)
+            work = dist.all_gather_into_tensor(allp.view(world * sets, pd, r), mine.contiguous(), group=pg,
+                                               async_op=True)
+            yield
+            work.wait()
             P = allp.transpose(0, 1).reshape(sets * world, pd, r)[:n].contiguous()
         else:
-            P = self._orth(P, group, ranks)
-        R = self._power_r(Mb, P, t)
+            with phase(name):
+                P = self._orth(P, group, ranks)
+        with phase(name):
+            R = self._power_r(Mb, P, t)
         if compressed:
-            R = self._all_reduce_replicate([R])[0]
-        ops.dion_fixup_(P, R, Qb, nz)
-        sumsq = ops.col_sumsq(R)
-        self._update(group, params, order, Mb, Qb, P, R, nz, t, sumsq)
-        self._after_update(group, params, order, sumsq, ranks)
+            R = (yield from self._all_reduce_replicate_async([R]))[0]
+        with phase(name):
+            ops.dion_fixup_(P, R, Qb, nz)
+            sumsq = ops.col_sumsq(R)
+            self._update(group, params, order, Mb, Qb, P, R, nz, t, sumsq)
+            self._after_update(group, params, order, sumsq, ranks)
 
     # ---- FSDP (outer-sharded) parameters
     def _dion_sharded(self, group: dict, params: List[Tensor], cfg: DionParamConfig) -> None:
+        for _ in self._dion_sharded_gen(group, params, cfg, "dion/sharded"):
+            pass
+
+    def _dion_sharded_gen(self, group: dict, params: List[Tensor], cfg: DionParamConfig, name: str):
+        """FSDP (outer-sharded) update of one signature set; on the NCCL path
+        it yields after each asynchronous collective (reduce-scatter of P,
+        all-gather of the orthogonalised P, all-reduce of the column norms)."""
         mesh = self._outer_shard_mesh
         pg = mesh.get_group()
         W = mesh.size()
@@ -562,37 +623,57 @@ class Dion(Optimizer):
         rm = self._replicate_mesh
         compressed = self._replicate_mesh_grad_sync and cfg.compressed_all_reduce and rm is not None
         if self._replicate_mesh_grad_sync and not cfg.compressed_all_reduce and rm is not None:
-            G = self._all_reduce_replicate(G)
-        nz_p = ops.dion_momentum_add_([Mb[o] for o in order], G)
-        nz = torch.zeros(sets * W, device=Mb.device, dtype=torch.float32)
-        nz[torch.tensor(order, device=Mb.device)] = nz_p
+            G = yield from self._all_reduce_replicate_async(G)
+        with phase(name):
+            nz_p = ops.dion_momentum_add_([Mb[o] for o in order], G)
+            nz = torch.zeros(sets * W, device=Mb.device, dtype=torch.float32)
+            nz[torch.tensor(order, device=Mb.device)] = nz_p
         t = cfg.is_transposed
         me = mesh.get_local_rank()
         my_ranks = None if ranks is None else ranks[me * sets:(me + 1) * sets]
         heap = self._p2p_heap(pg, Mb, Qb, t, sets, W)
         if heap is not None:
-            P_all = self._p2p_power_orth(heap, group, Mb, Qb, t, sets, W, me, my_ranks, compressed)
+            # fused path: the transfers ride in the GEMM epilogues (no NCCL to overlap)
+            with phase(name):
+                P_all = self._p2p_power_orth(heap, group, Mb, Qb, t, sets, W, me, my_ranks, compressed)
         else:
-            P_part = self._power_p(Mb, Qb, t)  # partial sums over this rank's shard
+            with phase(name):
+                P_part = self._power_p(Mb, Qb, t)  # partial sums over this rank's shard
             pd, r = P_part.shape[1:]
             mine = torch.empty((sets, pd, r), device=Mb.device, dtype=torch.float32)
-            dist.reduce_scatter_tensor(mine, P_part, op=dist.ReduceOp.SUM, group=pg)
+            work = dist.reduce_scatter_tensor(mine, P_part, op=dist.ReduceOp.SUM, group=pg, async_op=True)
+            yield
+            work.wait()
+            del P_part
             if compressed:
-                mine = self._all_reduce_replicate([mine])[0]
-            mine = self._orth(mine, group, my_ranks)
+                mine = (yield from self._all_reduce_replicate_async([mine]))[0]
+            with phase(name):
+                mine = self._orth(mine, group, my_ranks)
             P_all = torch.empty((sets * W, pd, r), device=Mb.device, dtype=torch.float32)
-            dist.all_gather_into_tensor(P_all, mine.contiguous(), group=pg)
-        R = self._power_r(Mb, P_all, t)
+            work = dist.all_gather_into_tensor(P_all, mine.contiguous(), group=pg, async_op=True)
+            yield
+            work.wait()
+        with phase(name):
+            R = self._power_r(Mb, P_all, t)
         if compressed:
-            R = self._all_reduce_replicate([R])[0]
-        ops.dion_fixup_(P_all, R, Qb, nz)
-        sumsq = ops.col_sumsq(R)
+            if heap is not None:
+                # P_all lives in the shared heap until the update below: no other set may run here
+                R = self._all_reduce_replicate([R])[0]
+            else:
+                R = (yield from self._all_reduce_replicate_async([R]))[0]
+        with phase(name):
+            ops.dion_fixup_(P_all, R, Qb, nz)
+            sumsq = ops.col_sumsq(R)
         if heap is not None:
-            sumsq = self._p2p_sum(heap, sumsq, sets, W, me, P_all.size(1))
+            with phase(name):
+                sumsq = self._p2p_sum(heap, sumsq, sets, W, me, P_all.size(1))
         else:
-            dist.all_reduce(sumsq, op=dist.ReduceOp.SUM, group=pg)
-        self._update(group, params, order, Mb, Qb, P_all, R, nz, t, sumsq)
-        self._after_update(group, params, order, sumsq, ranks)
+            work = dist.all_reduce(sumsq, op=dist.ReduceOp.SUM, group=pg, async_op=True)
+            yield
+            work.wait()
+        with phase(name):
+            self._update(group, params, order, Mb, Qb, P_all, R, nz, t, sumsq)
+            self._after_update(group, params, order, sumsq, ranks)
 
     # ---- in-kernel collectives over symmetric peer memory
     def _p2p_heap(self, pg, Mb: Tensor, Qb: Tensor, transposed: bool, sets: int, W: int):
@@ -616,14 +697,14 @@ class Dion(Optimizer):
         sum region (after recv and P_all, so the next group's P stores cannot
         overwrite slots still being summed), one device barrier, a fixed-order
         sum of the W slots. Replaces ada_dion/optim/adadion_v2.py:1091-1096."""
+        from ..parallel.symm import cached_for_heap
+
         r = sumsq.size(1)
         nb = sets * W * r * 4
         base = 2 * W * sets * pd * r * 4
         key = ("p2p_sum", heap.uid, sets, W, pd, r)
-        ptrs = self._p2p_ptrs.get(key)
-        if ptrs is None:
-            ptrs = heap.ptr_tensor([heap.addr((me + 1 + i) % W, base + me * nb) for i in range(W)])
-            self._p2p_ptrs[key] = ptrs
+        ptrs = cached_for_heap(self._p2p_ptrs, heap, key, lambda: heap.ptr_tensor(
+            [heap.addr((me + 1 + i) % W, base + me * nb) for i in range(W)]))
         heap.push(sumsq.contiguous(), ptrs)
         heap.barrier()
         out = torch.empty_like(sumsq)
@@ -642,20 +723,22 @@ class Dion(Optimizer):
              of every rank (nrep = W); 5. device barrier.
         Replaces ada_dion/optim/adadion_v2.py:1051-1071 (reduce-scatter, orthogonalize, all-gather).
         """
+        from ..parallel.symm import cached_for_heap
+
         dt = self._op_dtype(Mb.dtype)
         A = Mb.transpose(1, 2) if transposed else Mb
         pd, r = A.size(1), Qb.size(-1)
         slot = pd * r * 4
         recv_off, pall_off = 0, W * sets * slot
         key = ("p2p", heap.uid, sets, W, pd, r)
-        cached = self._p2p_ptrs.get(key)
-        if cached is None:
+
+        def build():
             rs = [heap.addr(k // sets, recv_off + (me * sets + k % sets) * slot) for k in range(W * sets)]
             order = [(me + 1 + i) % W for i in range(W)]  # replicas to the next ranks first
             ag = [heap.addr(j, pall_off + (me * sets + s) * slot) for s in range(sets) for j in order]
-            cached = (heap.ptr_tensor(rs), heap.ptr_tensor(ag))
-            self._p2p_ptrs[key] = cached
-        rs_ptrs, ag_ptrs = cached
+            return heap.ptr_tensor(rs), heap.ptr_tensor(ag)
+
+        rs_ptrs, ag_ptrs = cached_for_heap(self._p2p_ptrs, heap, key, build)
         # start with the matrices owned by the next rank: concurrent ranks store to different GPUs
         ops.matmul_to_ptrs(A.to(dt), Qb.to(dt), rs_ptrs, r, torch.float32, rot_b=((me + 1) % W) * sets)
         heap.barrier()

@@ -276,7 +276,7 @@ class Dion2(Optimizer):
         buffer (peer stores, next ranks first), one device barrier, the owner
         orthogonalises, the last Newton-Schulz GEMM stores each rank's k rows
         into that rank's return buffer, one more barrier."""
-        from ..parallel.symm import heap_for
+        from ..parallel.symm import cached_for_heap, heap_for
 
         W, me = self._world, self._rank
         n, k, c = sel.shape
@@ -286,14 +286,14 @@ class Dion2(Optimizer):
         gather_off, ret_off = 0, sets * mat
         heap = heap_for(self._pg, 2 * sets * mat, "dion2", sel.device)
         key = (heap.uid, n, k, c)
-        cached = self._p2p_cache.get(key)
-        if cached is None:
+
+        def build():
             dsts = [heap.ptr_tensor([heap.addr(i % W, gather_off + (i // W) * mat + me * blk)]) for i in range(n)]
             ptrs = heap.ptr_tensor([heap.addr(j, ret_off + (me * sets + s_) * blk) for s_ in range(sets)
                                     for j in range(W)])
-            cached = (dsts, ptrs)
-            self._p2p_cache[key] = cached
-        dsts, ptrs = cached
+            return dsts, ptrs
+
+        dsts, ptrs = cached_for_heap(self._p2p_cache, heap, key, build)
         full = heap.view(gather_off, (sets, W * k, c), torch.bfloat16)
         for i in range(n, sets * W):
             if i % W == me:  # this rank owns an absent matrix of the last set

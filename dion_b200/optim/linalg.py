@@ -1,15 +1,19 @@
 """Orthogonalisation for Dion's power iteration.
 
 ``orthogonalize(P)`` for a batch of fp32 matrices P (b, d, r):
-  * d <= r : QR of P (reduced Q);
-  * d >  r : randomised Cholesky QR (the reference's "rcqr",
+  * d <  r : QR of P (reduced Q), torch.linalg;
+  * d >= r : randomised Cholesky QR (the reference's "rcqr",
     ada_dion/optim/adadion_v2.py:1645-1685):
         S ~ N(0, 1/k), k = ceil(oversample*r/128)*128
         R1 = qr(S P).R ;  P = P R1^-1
         R2 = chol(P^T P) ;  P = P R2^-1
 The big products (S P, P R^-1, P^T P) run on the tcgen05 tensor cores
-(tf32, fp32 accumulate); the r x r / k x r factorisations use the package's
-sm_100a kernels when present and torch.linalg otherwise.
+(tf32, fp32 accumulate); the r x r / k x r factorisations are the package's
+blocked sm_100a kernels (fp32 panels, tcgen05 3xTF32 trailing updates).
+Square P (d == r, the reference's QR branch at adadion_v2.py:1660-1662) also
+takes the randomised path on the GPU: both give the orthonormal factor of P
+up to column signs, and Dion's update P Q^T and error feedback P R^T are
+unchanged by a sign flip of a column of P (R = M^T P flips with it).
 
 ``distributed_orthogonalize`` is the inner-sharded (TP) variant
 (adadion_v2.py:1690-1790): rows of P are split across the inner mesh, the
@@ -36,16 +40,21 @@ def sketch_size(r: int, oversample: float) -> int:
     return int(math.ceil(oversample * r / 128.0) * 128)
 
 
-_MAX_KERNEL_DIM = 1600  # single-CTA kernels keep a 32-column panel of this many rows in shared memory
+_MAX_KERNEL_DIM = 1600  # the unblocked cluster kernels keep a panel of this many rows in shared memory
+_QR_MAX_ROWS = 11200     # blocked QR: panel rows split over at most 8 CTAs of 1400 rows
 
 
 def _use_kernels(t: Tensor, rows: int) -> bool:
     return t.is_cuda and ops.has_ext() and rows <= _MAX_KERNEL_DIM
 
 
+def _cuda_ext(t: Tensor) -> bool:
+    return t.is_cuda and ops.has_ext()
+
+
 def tri_inv_lower(S: Tensor, upper: bool = False) -> Tensor:
     """Z = L^-1 (lower) for L = lower(S), or L = upper(S)^T when ``upper``."""
-    if _use_kernels(S, S.size(-1)):
+    if _cuda_ext(S):
         Z = torch.empty(S.shape, device=S.device, dtype=S.dtype)
         ops.ext().tri_inv_lower(S.contiguous(), Z, bool(upper))
         return Z
@@ -61,8 +70,18 @@ def tri_inv_upper(R: Tensor) -> Tensor:
 
 def cholesky_lower(A: Tensor) -> Tensor:
     """Lower Cholesky factor of a batch of SPD matrices; non-SPD matrices give
-    NaN entries that the Dion guard later discards (as cholesky_ex does)."""
-    if _use_kernels(A, A.size(-1)):
+    NaN entries that the Dion guard later discards (as cholesky_ex does).
+
+    CUDA: blocked right-looking Cholesky whose trailing update (SYRK) runs
+    on the tcgen05 GEMM in 3xTF32 (any r with 16-byte rows), else the
+    unblocked cluster kernel (r <= 1600)."""
+    r = A.size(-1)
+    if _cuda_ext(A) and r % 4 == 0:
+        L = A.contiguous().clone()
+        info = torch.empty(A.size(0), dtype=torch.int32, device=A.device)
+        ops.ext().cholesky_blocked(L, info)
+        return torch.tril(L)
+    if _use_kernels(A, r):
         L = A.contiguous().clone()
         info = torch.empty(A.size(0), dtype=torch.int32, device=A.device)
         ops.ext().cholesky_lower(L, info)
@@ -76,10 +95,20 @@ def cholesky_upper(A: Tensor) -> Tensor:
 
 
 def qr_r(A: Tensor) -> Tensor:
-    """R factor (upper) of the Householder QR of a batch of tall matrices."""
-    if _use_kernels(A, A.size(-2)):
+    """R factor (upper) of the Householder QR of a batch of tall matrices.
+
+    CUDA: blocked Householder with the compact-WY trailing update on the
+    tcgen05 GEMM in 3xTF32 (n % 4 == 0, m <= 11200), else the unblocked
+    cluster kernel (m <= 1600)."""
+    m, n = A.size(-2), A.size(-1)
+    if _cuda_ext(A) and n % 4 == 0 and m <= _QR_MAX_ROWS:
         W = A.contiguous().clone()
-        R = torch.empty(A.size(0), A.size(-1), A.size(-1), device=A.device, dtype=A.dtype)
+        R = torch.empty(A.size(0), n, n, device=A.device, dtype=A.dtype)
+        ops.ext().qr_r_blocked(W, R)
+        return R
+    if _use_kernels(A, m):
+        W = A.contiguous().clone()
+        R = torch.empty(A.size(0), n, n, device=A.device, dtype=A.dtype)
         ops.ext().qr_r(W, R)
         return R
     return torch.linalg.qr(A, mode="r")[1]
@@ -120,7 +149,8 @@ def orthogonalize(P: Tensor, oversample: float = 1.25, generator: Optional[torch
     Pf = P.float().contiguous()
     b, d, r = Pf.shape
     assert out_ptrs is None or P.is_cuda, "out_ptrs needs CUDA tensors"
-    if d <= r:
+    if d < r or (d == r and not (P.is_cuda and ops.has_ext())):
+        # wide P (d < r: Q is d x d) is not produced by Dion's rank rule (r <= min(m, n))
         Q, _ = torch.linalg.qr(Pf)
         if out_ptrs is not None:
             Qc = Q.float().contiguous()
@@ -172,7 +202,11 @@ def distributed_orthogonalize(P: DTensor, oversample: float = 1.25, shard_mesh_d
     d, r = P.shape[-2:]
     if d <= r:
         single = P.redistribute(placements=batch_sharded)
-        Q, _ = torch.linalg.qr(single.to_local().float(), mode="reduced")
+        loc = single.to_local().float()
+        if d == r and loc.is_cuda and ops.has_ext() and loc.size(0) > 0:
+            Q = orthogonalize(loc.contiguous(), oversample)  # square: the kernels' randomised path
+        else:
+            Q, _ = torch.linalg.qr(loc, mode="reduced")
         out = DTensor.from_local(Q.to(dtype).contiguous(), mesh, single.placements, run_check=False,
                                  shape=single.shape, stride=single.stride())
         return out.redistribute(placements=orig)

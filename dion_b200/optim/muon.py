@@ -389,7 +389,7 @@ class Muon(Optimizer):
         reading call t's results cannot be overwritten by call t+1, and call
         t+2 waits behind call t+1's barrier, which that rank reaches only
         after its reads."""
-        from ..parallel.symm import heap_for
+        from ..parallel.symm import cached_for_heap, heap_for
 
         W, me = self._world, self._rank
         half = sets * W * m * k * 2
@@ -397,12 +397,9 @@ class Muon(Optimizer):
         self._ddp_parity = par = 1 - self._ddp_parity
         base = par * half
         key = ("ddp", heap.uid, par, sets, m, k)
-        ptrs = self._p2p_cache.get(key)
-        if ptrs is None:
-            order = [(me + 1 + i) % W for i in range(W)]
-            ptrs = heap.ptr_tensor([heap.addr(j, base + (s_ * W + me) * m * k * 2) for s_ in range(sets)
-                                    for j in order])
-            self._p2p_cache[key] = ptrs
+        order = [(me + 1 + i) % W for i in range(W)]
+        ptrs = cached_for_heap(self._p2p_cache, heap, key, lambda: heap.ptr_tensor(
+            [heap.addr(j, base + (s_ * W + me) * m * k * 2) for s_ in range(sets) for j in order]))
         ops.newton_schulz(mine, self._coeffs, eps, scale=scale, clobber_input=True, out_ptrs=ptrs, nrep=W)
         heap.barrier()
         return heap.view(base, (sets * W, m, k), torch.bfloat16)
@@ -419,7 +416,7 @@ class Muon(Optimizer):
              stores row shard j of matrix s into rank j's ret[me, s];
           4. device barrier; 5. scaled weight update from ret.
         """
-        from ..parallel.symm import heap_for
+        from ..parallel.symm import cached_for_heap, heap_for
 
         W, me = self._world, self._rank
         m, k = full_shape
@@ -428,16 +425,16 @@ class Muon(Optimizer):
         gather_off, ret_off = 0, sets * mat
         heap = heap_for(self._pg, 2 * sets * mat, "muon", X[0].device)
         key = (heap.uid, sets, m, k)
-        cached = self._p2p_cache.get(key)
-        if cached is None:
+
+        def build():
             # peer rows written only by this extension's kernels (the momentum kernel)
             dst_views = [ops.ext().symm_view(heap.addr(i % W, gather_off + (i // W) * mat + me * ms * k * 2),
                                              ms * k, 15) for i in range(n)]
             ptrs = heap.ptr_tensor([heap.addr(j, ret_off + ((me * sets + s_) * ms * k) * 2)
                                     for s_ in range(sets) for j in range(W)])
-            cached = (dst_views, ptrs)
-            self._p2p_cache[key] = cached
-        dst_views, ptrs = cached
+            return dst_views, ptrs
+
+        dst_views, ptrs = cached_for_heap(self._p2p_cache, heap, key, build)
         full = heap.view(gather_off, (sets, m, k), torch.bfloat16)
         for i in range(n + (-n) % W):
             if i >= n and i % W == me:  # this rank owns an absent matrix of the last set

@@ -24,7 +24,7 @@ from __future__ import annotations
 
 import itertools
 import os
-from typing import Dict, List, Optional, Sequence, Tuple
+from typing import Any, Callable, Dict, List, Optional, Sequence, Tuple
 
 import torch
 import torch.distributed as dist
@@ -32,7 +32,7 @@ from torch import Tensor
 
 from .. import ops
 
-__all__ = ["SymmetricHeap", "p2p_enabled", "heap_for"]
+__all__ = ["SymmetricHeap", "p2p_enabled", "heap_for", "cached_for_heap"]
 
 _ALIGN = 256
 _UID = itertools.count()
@@ -82,6 +82,7 @@ class SymmetricHeap:
         self._flags = torch.tensor(self.bases, dtype=torch.int64).to(self.device)
         self._closed = False
         self.uid = next(_UID)  # never reused, unlike id()
+        self._close_hooks: List[Callable[[], None]] = []
         # canaries: the gap between the flag words and the data, and a guard after the data
         flag_end = E.symm_flag_bytes()
         self._canary_regions = [(flag_end, self.data_off - flag_end), (self.data_off + self.nbytes, _GUARD)]
@@ -126,10 +127,17 @@ class SymmetricHeap:
     def push(self, src: Tensor, dst_addrs: Tensor) -> None:
         ops.ext().symm_push(src, dst_addrs)
 
+    def on_close(self, fn: Callable[[], None]) -> None:
+        """Run ``fn`` when the heap is closed (before its memory is unmapped)."""
+        self._close_hooks.append(fn)
+
     def close(self) -> None:
         if self._closed:
             return
         self._closed = True
+        hooks, self._close_hooks = self._close_hooks, []
+        for fn in hooks:
+            fn()
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
         E = ops.ext()
@@ -152,6 +160,19 @@ def heap_for(group, nbytes: int, tag: str, device: torch.device) -> SymmetricHea
         h = SymmetricHeap(group, nbytes, device)
         _HEAPS[key] = h
     return h
+
+
+def cached_for_heap(cache: dict, heap: "SymmetricHeap", key, build: Callable[[], Any]) -> Any:
+    """``cache[key]``, built by ``build()`` on first use. Entries hold peer
+    addresses and views into ``heap``; each is dropped when the heap closes
+    (for example when a larger heap replaces it), so no cached pointer can
+    outlive the mapping it points into."""
+    v = cache.get(key)
+    if v is None:
+        v = build()
+        cache[key] = v
+        heap.on_close(lambda: cache.pop(key, None))
+    return v
 
 
 def release_all() -> None:

@@ -143,6 +143,26 @@ def test_dcp_checkpoint_roundtrip(tmp_path):
     assert (ck / "step-4").exists()
 
 
+def test_resume_after_model_only_final_save(tmp_path):
+    """Interval saves, then the final model-only export: a longer rerun
+    resumes from the last full checkpoint (optimizer state and step), not
+    from the model-only export; a final step on the interval still gets its
+    full checkpoint."""
+    from dion_b200 import train
+    from dion_b200.checkpoint import CheckpointManager
+
+    ck = tmp_path / "ck"
+    args = ["--config", "llama3_debug_dion", "--training.seq_len", "32", "--training.local_batch_size", "2",
+            "--checkpoint.enable", "--checkpoint.folder", str(ck), "--checkpoint.interval", "2",
+            "--checkpoint.last_save_model_only"]
+    train.main(args + ["--training.steps", "3"])
+    assert (ck / "step-2").exists() and (ck / "step-3-model").exists() and not (ck / "step-3").exists()
+    assert CheckpointManager(str(ck), None, None).latest() == str(ck / "step-2")
+    losses = train.main(args + ["--training.steps", "4", "--metrics.log_freq", "1"])
+    assert len(losses) == 2  # steps 3 and 4 only: resumed at step 2
+    assert (ck / "step-4").exists() and (ck / "step-4-model").exists()
+
+
 @pytest.mark.parametrize("mode,option", [("full", "1"), ("selective", "op"), ("selective", "2")])
 def test_activation_checkpointing_matches(mode, option):
     """Checkpointed blocks give the same loss and gradients as plain ones."""
@@ -223,7 +243,7 @@ def test_checkpoint_load_model_only_and_full(tmp_path):
     ckpt.save(str(tmp_path), m, c, step=5)
     m2 = _MockLlama()
     c2 = HybridOptimizersContainer(cfg, model_parts=[m2])
-    assert ckpt.load(str(tmp_path / "step-3"), m2, c2) == 0
+    assert ckpt.load(str(tmp_path / "step-3-model"), m2, c2) == 0
     assert all(torch.equal(a, b) for a, b in zip(m.state_dict().values(), m2.state_dict().values()))
     assert ckpt.load(str(tmp_path / "step-5"), m2, c2) == 5
     mom = [v for k, v in c2.state_dict().items() if k.endswith("momentum_buffer") or k.endswith("momentum")]
