@@ -62,15 +62,14 @@ def make_data(kind: str, steps: int, batch: int, seq: int, vocab: int, seed: int
         return lambda s: (seqs[s][:, :-1], seqs[s][:, 1:])
     if kind == "markov":
         perm = torch.randperm(vocab, generator=g)
-        seqs = []
-        for _ in range(steps):
-            x = torch.empty(batch, seq + 1, dtype=torch.long)
-            x[:, 0] = torch.randint(0, vocab, (batch,), generator=g)
-            noise = torch.rand(batch, seq, generator=g) >= 0.9
-            rnd = torch.randint(0, vocab, (batch, seq), generator=g)
-            for t in range(seq):
-                x[:, t + 1] = torch.where(noise[:, t], rnd[:, t], perm[x[:, t]])
-            seqs.append(x)
+        nseq = steps * batch  # every step's sequences generated together, one position at a time
+        x = torch.empty(nseq, seq + 1, dtype=torch.long)
+        x[:, 0] = torch.randint(0, vocab, (nseq,), generator=g)
+        noise = torch.rand(nseq, seq, generator=g) >= 0.9
+        rnd = torch.randint(0, vocab, (nseq, seq), generator=g)
+        for t in range(seq):
+            x[:, t + 1] = torch.where(noise[:, t], rnd[:, t], perm[x[:, t]])
+        seqs = list(x.view(steps, batch, seq + 1).unbind(0))
         return lambda s: (seqs[s][:, :-1], seqs[s][:, 1:])
     raise ValueError(kind)
 
@@ -142,25 +141,28 @@ def _matrix_names(model) -> List[str]:
     return [n for n, p in model.named_parameters() if id(p) in ids]
 
 
-def _build_optimizer(impl: str, optimizer: str, model, matrix_names, a):
+def _build_optimizer(impl: str, optimizer: str, model, matrix_names, a, mesh=None):
     named = list(model.named_parameters())
     groups = _groups(named, set(matrix_names), a.scalar_lr, a.scalar_wd)
     if impl == "ours":
         from ..optim import Dion, Muon
 
         if optimizer == "dion":
-            return Dion(groups, lr=a.lr, mu=a.mu, rank_fraction=a.rank_fraction, weight_decay=a.wd)
-        return Muon(groups, lr=a.lr, mu=a.mu, weight_decay=a.wd, nesterov=False, adjust_lr="spectral_norm")
+            return Dion(groups, outer_shard_mesh=mesh, lr=a.lr, mu=a.mu, rank_fraction=a.rank_fraction,
+                        weight_decay=a.wd)
+        return Muon(groups, distributed_mesh=mesh, lr=a.lr, mu=a.mu, weight_decay=a.wd, nesterov=False,
+                    adjust_lr="spectral_norm")
     if REF_PATH not in sys.path:
         sys.path.insert(0, REF_PATH)
     if optimizer == "dion":
         from ada_dion.optim.adadion_v2 import AdaDionV2
 
+        # one rank: no outer shard mesh (the same call the benchmark's reference arm makes)
         return AdaDionV2(groups, lr=a.lr, mu=a.mu, rank_fraction_max=a.rank_fraction, weight_decay=a.wd)
     from dion import Muon as RefMuon
 
-    return RefMuon(groups, fsdp_mesh_dim=0, world_mesh=None, lr=a.lr, mu=a.mu, weight_decay=a.wd, nesterov=False,
-                   adjust_lr="spectral_norm")
+    return RefMuon(groups, fsdp_mesh_dim=0, world_mesh=mesh, distributed_mesh=mesh, lr=a.lr, mu=a.mu,
+                   weight_decay=a.wd, nesterov=False, adjust_lr="spectral_norm")
 
 
 def _prepare_inductor():
@@ -184,16 +186,37 @@ def state_layout(opt, model) -> Dict[str, Dict[str, List[int]]]:
 
 
 # ---------------------------------------------------------------- one arm
+def _one_rank_mesh():
+    """A 1-rank NCCL process group and device mesh for FSDP2 on one GPU."""
+    import datetime
+
+    import torch.distributed as dist
+    from torch.distributed.device_mesh import init_device_mesh
+
+    if not dist.is_initialized():
+        dist.init_process_group("nccl", store=dist.HashStore(), rank=0, world_size=1,
+                                timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", 0))
+    return init_device_mesh("cuda", (1,), mesh_dim_names=("dp_shard",))
+
+
 def run_arm(impl: str, a, init_state=None, opt_seed: int = 0) -> Dict:
+    """One training run; ``a.dtype``: fp32, bf16 (bf16 weights and state) or
+    mixed (FSDP2 on one GPU: fp32 master weights and optimizer state, bf16
+    compute, fp32 gradient reduction -- the benchmark's setting)."""
     device = torch.device(a.device)
     model, cfg = _our_model(a.preset, a.seq_len, "cpu", a.seed, a.init)
     matrix_names = _matrix_names(model)
     if init_state is None:
         init_state = {k: v.detach().clone() for k, v in model.state_dict().items()}
+    mesh = _one_rank_mesh() if a.dtype == "mixed" else None
     if impl == "ours":
         model = model.to(device)
         if a.dtype == "bf16":
             model = model.to(torch.bfloat16)
+        if mesh is not None:
+            from ..parallel.fsdp import apply_fsdp
+
+            apply_fsdp(model, mesh)
 
         def loss_fn(t, l):
             return model.loss(t, l)
@@ -202,11 +225,19 @@ def run_arm(impl: str, a, init_state=None, opt_seed: int = 0) -> Dict:
         model = _reference_model(cfg, init_state, device)
         if a.dtype == "bf16":
             model = model.to(torch.bfloat16)
+        if mesh is not None:
+            from torch.distributed.fsdp import MixedPrecisionPolicy, fully_shard
+
+            mp = MixedPrecisionPolicy(param_dtype=torch.bfloat16, reduce_dtype=torch.float32)
+            blocks = list(model.layers.values())
+            for i, b in enumerate(blocks):
+                fully_shard(b, mesh=mesh, mp_policy=mp, reshard_after_forward=i < len(blocks) - 1)
+            fully_shard(model, mesh=mesh, mp_policy=mp)
 
         def loss_fn(t, l):
             return F.cross_entropy(model(t).flatten(0, 1).float(), l.flatten(0, 1))
     torch.manual_seed(opt_seed)  # the optimizer's own random draws (Q init, sketches)
-    opt = _build_optimizer(impl, a.optimizer, model, matrix_names, a)
+    opt = _build_optimizer(impl, a.optimizer, model, matrix_names, a, mesh)
     base = [g["lr"] for g in opt.param_groups]
     get = make_data(a.data, a.steps, a.batch, a.seq_len, cfg.vocab_size, a.data_seed)
     losses = []
@@ -245,7 +276,7 @@ def parse(argv=None):
     p.add_argument("--optimizer", choices=["dion", "muon"], default="dion")
     p.add_argument("--impl", choices=["ours", "reference", "both"], default="both")
     p.add_argument("--device", default="cpu")
-    p.add_argument("--dtype", choices=["fp32", "bf16"], default="fp32")
+    p.add_argument("--dtype", choices=["fp32", "bf16", "mixed"], default="fp32")
     p.add_argument("--steps", type=int, default=50)
     p.add_argument("--warmup", type=int, default=0)
     p.add_argument("--batch", type=int, default=8)
@@ -262,12 +293,27 @@ def parse(argv=None):
     p.add_argument("--scalar-wd", type=float, default=0.1)
     p.add_argument("--ref-seeds", type=int, default=1, help="reference runs with optimizer seeds 0..n-1")
     p.add_argument("--out", default="")
+    p.add_argument("--golden", default="", help="also write the compact golden file used by the tests")
     return p.parse_args(argv)
+
+
+def golden_record(res: Dict) -> Dict:
+    """The compact form committed as a golden file: the run's configuration,
+    the reference's loss curves (every optimizer seed), this package's curve
+    and the reference's optimizer-state layout."""
+    ref = res["reference"]
+    rec = {"config": res["config"],
+           "reference_losses": [ref["losses"]] + [o["losses"] for o in res.get("reference_other_seeds", [])],
+           "ours_losses": res["ours"]["losses"],
+           "reference_state_layout": ref["state_layout"],
+           "comparison": res.get("comparison")}
+    rec["config"].pop("golden", None)
+    return rec
 
 
 def main(argv=None) -> Dict:
     a = parse(argv)
-    res: Dict = {"config": {k: v for k, v in vars(a).items() if k != "out"}}
+    res: Dict = {"config": {k: v for k, v in vars(a).items() if k not in ("out", "golden")}}
     init_state = None
     if a.impl in ("ours", "both"):
         r = run_arm("ours", a)
@@ -298,6 +344,9 @@ def main(argv=None) -> Dict:
     if a.out:
         with open(a.out, "w") as fh:
             json.dump(res, fh, indent=1)
+    if a.golden and "comparison" in res:
+        with open(a.golden, "w") as fh:
+            json.dump(golden_record(res), fh)
     return res
 
 

@@ -140,6 +140,43 @@ def adamw():
 
 
 @case
+def lion():
+    n = 1 << 24
+    X = [torch.randn(n, device="cuda") for _ in range(4)]
+    G = [torch.randn(n, device="cuda") for _ in range(4)]
+    M = [torch.zeros(n, device="cuda") for _ in range(4)]
+    return lambda: ops.lion_(X, G, M, 1e-4, 0.9, 0.99, 0.1)
+
+
+@case
+def dion_momentum_add():
+    """M += G with the per-matrix all-zero flags (8 x 4096^2 fp32 state, bf16 gradients)."""
+    M = [torch.zeros(4096, 4096, device="cuda") for _ in range(8)]
+    G = [torch.randn(4096, 4096, device="cuda", dtype=torch.bfloat16) for _ in range(8)]
+    return lambda: ops.dion_momentum_add_(M, G)
+
+
+@case
+def dion2_select():
+    """Dion2 row scores + top-k + gather/decay + sparse update (16 x 4096 x 4096 fp32, fraction 1/4)."""
+    M = [torch.randn(4096, 4096, device="cuda") for _ in range(16)]
+    X = [torch.randn(4096, 4096, device="cuda") for _ in range(16)]
+
+    def run():
+        idx, pos = ops.dion2_select_rows(M, 1024)
+        sel = ops.dion2_gather_decay_(M, idx, 0.999)
+        ops.dion2_update_(X, pos, sel, 0.999, 0.01)
+    return run
+
+
+@case
+def orthogonalize():
+    """Dion's randomised Cholesky QR for 6 matrices 4096 x 1024 (one rank of 8, one shape group)."""
+    P = torch.randn(6, 4096, 1024, device="cuda")
+    return lambda: LA.orthogonalize(P)
+
+
+@case
 def rms_norm():
     x = torch.randn(32768, 2048, device="cuda", dtype=torch.bfloat16)
     w = torch.ones(2048, device="cuda")

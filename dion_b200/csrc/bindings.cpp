@@ -62,6 +62,13 @@ void tri_inv_lower(const at::Tensor& S, at::Tensor& Z, bool upper);
 void qr_r(at::Tensor& A, at::Tensor& R);
 void qr_r_blocked(at::Tensor& A, at::Tensor& R);
 void cholesky_blocked(at::Tensor& A, at::Tensor& info);
+void dion2_row_scores(const at::Tensor& ptrs, int64_t rows, int64_t cols, int64_t ld, int64_t dtype,
+                      at::Tensor& scores);
+void dion2_topk_rows(const at::Tensor& scores, int64_t k, at::Tensor& idx, at::Tensor& pos);
+void dion2_gather_decay(const at::Tensor& ptrs, int64_t cols, int64_t ld, int64_t dtype, const at::Tensor& idx,
+                        double decay, at::Tensor& sel);
+void dion2_update(const at::Tensor& ptrs, int64_t rows, int64_t cols, int64_t ld, int64_t dtype,
+                  const at::Tensor& pos, const at::Tensor& U, double keep, double alpha);
 }  // namespace bdion
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -114,6 +121,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qr_r", &bdion::qr_r);
   m.def("qr_r_blocked", &bdion::qr_r_blocked, "blocked Householder QR (R only), tcgen05 3xTF32 trailing update");
   m.def("cholesky_blocked", &bdion::cholesky_blocked, "blocked Cholesky, tcgen05 3xTF32 trailing SYRK");
+  m.def("dion2_row_scores", &bdion::dion2_row_scores, "L1 row norms of a set of matrices (pointer array)");
+  m.def("dion2_topk_rows", &bdion::dion2_topk_rows, "per-matrix top-k rows (ascending) and row->slot map");
+  m.def("dion2_gather_decay", &bdion::dion2_gather_decay, "gather selected rows (bf16) and decay them in place");
+  m.def("dion2_update", &bdion::dion2_update, "row-sparse weight update with weight decay on every row");
   m.def("status_read", &bdion::status_read);
   m.def("status_clear", &bdion::status_clear);
   m.def("set_wait_limit_ns", &bdion::set_wait_limit_ns);

@@ -20,6 +20,7 @@ __all__ = [
     "matmul",
     "matmul_update_",
     "matmul_to_ptrs",
+    "matmul_precise",
     "philox_normal",
     "newton_schulz",
     "muon_momentum_",
@@ -27,6 +28,9 @@ __all__ = [
     "adamw_",
     "lion_",
     "multi_sumsq",
+    "dion2_select_rows",
+    "dion2_gather_decay_",
+    "dion2_update_",
     "check_status",
     "clear_status",
     "StatusError",
@@ -137,6 +141,50 @@ def matmul(
         return out3.squeeze(0) if squeeze else out3
     ext().gemm(A3, B3, out3, C3, float(alpha), float(beta), None, 0, 0, bool(symmetric), False, 1.0, 1.0, 0)
     return out3.squeeze(0) if squeeze else out3
+
+
+def _tf32_split(x: Tensor) -> Tuple[Tensor, Tensor]:
+    """x = hi + lo with hi exactly representable in tf32 (the low 13 mantissa
+    bits cleared) and lo = x - hi exact in fp32."""
+    x = x.contiguous()
+    hi = (x.view(torch.int32) & -8192).view(torch.float32)
+    return hi, x - hi
+
+
+_PRECISE_KC = 256
+
+
+def matmul_precise(A: Tensor, B: Tensor) -> Tensor:
+    """fp32 ``A @ B`` with about fp32 accuracy on the tf32 tensor cores.
+
+    A B ~ Ahi Bhi + Ahi Blo + Alo Bhi (the dropped Alo Blo term and the tf32
+    reading of the lo parts are ~2^-21 relative; Markidis et al. 2018),
+    evaluated per K chunk of 256 as ONE GEMM on operands concatenated along
+    K ([Ahi | Ahi | Alo] times [Bhi ; Blo ; Bhi]). The tensor cores' fp32
+    accumulator drops low bits at every k step, an error that grows with the
+    number of steps, so the chunks run as a batch with short accumulators and
+    are summed in fp32 afterwards. CPU: plain fp32 matmul."""
+    if not A.is_cuda:
+        return A.float() @ B.float()
+    squeeze = A.dim() == 2
+    A3, B3 = _as3d(A.float()), _as3d(B.float())
+    b, m, K = A3.shape
+    n = B3.size(-1)
+    kc = min(_PRECISE_KC, K)
+    c = -(-K // kc)
+    Ah, Al = _tf32_split(A3)
+    Bh, Bl = _tf32_split(B3)
+    if c * kc != K:
+        pad = c * kc - K
+        Ah, Al = (torch.nn.functional.pad(t, (0, pad)) for t in (Ah, Al))
+        Bh, Bl = (torch.nn.functional.pad(t, (0, 0, 0, pad)) for t in (Bh, Bl))
+    Ah, Al = (t.view(b, m, c, kc).transpose(1, 2) for t in (Ah, Al))
+    Bh, Bl = (t.view(b, c, kc, n) for t in (Bh, Bl))
+    Acat = torch.cat([Ah, Ah, Al], dim=-1).reshape(b * c, m, 3 * kc)
+    Bcat = torch.cat([Bh, Bl, Bh], dim=-2).reshape(b * c, 3 * kc, n)
+    out = matmul(Acat, Bcat).view(b, c, m, n)
+    out = out[:, 0] if c == 1 else out.sum(dim=1)
+    return out[0] if squeeze else out
 
 
 _SCALAR_TYPE = {torch.float32: 6, torch.bfloat16: 15}
@@ -591,3 +639,50 @@ def as_batch(ts: Sequence[Tensor]) -> Optional[Tensor]:
         if t.data_ptr() != t0.data_ptr() + i * d:
             return None
     return t0.as_strided((len(ts),) + tuple(t0.shape), (step,) + tuple(t0.stride()))
+
+
+# ---------------------------------------------------------------- Dion2 row selection
+def _uniform_matrices(ts: Sequence[Tensor]) -> bool:
+    t0 = ts[0]
+    return (t0.dim() == 2 and t0.stride(1) == 1 and t0.dtype in (torch.float32, torch.bfloat16)
+            and all(t.shape == t0.shape and t.stride() == t0.stride() and t.dtype == t0.dtype for t in ts))
+
+
+def dion2_select_rows(M: Sequence[Tensor], k: int, scores: Optional[Tensor] = None,
+                      reduce_scores=None) -> Tuple[Tensor, Tensor]:
+    """Top-``k`` rows of each matrix by L1 row norm (or by the given
+    ``scores`` [n, rows]); returns ``idx`` [n, k] (int64, ascending rows) and
+    ``pos`` [n, rows] (int32 slot of each row in ``idx``, -1 if unselected).
+    ``reduce_scores(scores)`` may sum the scores over ranks that hold other
+    columns, so that all of them pick the same rows."""
+    n = len(M)
+    rows, cols = M[0].shape
+    dev = M[0].device
+    if scores is None:
+        scores = torch.empty((n, rows), device=dev, dtype=torch.float32)
+        ext().dion2_row_scores(_ptr_tensor(M), rows, cols, M[0].stride(0), _SCALAR_TYPE[M[0].dtype], scores)
+    if reduce_scores is not None:
+        reduce_scores(scores)
+    idx = torch.empty((n, k), device=dev, dtype=torch.int64)
+    pos = torch.empty((n, rows), device=dev, dtype=torch.int32)
+    ext().dion2_topk_rows(scores.contiguous(), k, idx, pos)
+    return idx, pos
+
+
+def dion2_gather_decay_(M: Sequence[Tensor], idx: Tensor, decay: float) -> Tensor:
+    """``sel[b] = bf16(M[b][idx[b]])`` and, in the same pass, ``M[b][idx[b]] *= decay``."""
+    n, k = idx.shape
+    cols = M[0].shape[1]
+    sel = torch.empty((n, k, cols), device=M[0].device, dtype=torch.bfloat16)
+    ext().dion2_gather_decay(_ptr_tensor(M), cols, M[0].stride(0), _SCALAR_TYPE[M[0].dtype], idx.contiguous(),
+                             float(decay), sel)
+    return sel
+
+
+def dion2_update_(X: Sequence[Tensor], pos: Tensor, U: Tensor, keep: float, alpha: float) -> None:
+    """``X[b] = keep * X[b] - alpha * U[b][pos[b][i]]`` on the selected rows,
+    ``keep * X[b]`` on the others (one launch over every matrix)."""
+    rows, cols = X[0].shape
+    ext().dion2_update(_ptr_tensor(X), rows, cols, X[0].stride(0), _SCALAR_TYPE[X[0].dtype], pos.contiguous(),
+                       U.contiguous(), float(keep), float(alpha))
+

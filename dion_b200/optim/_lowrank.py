@@ -98,6 +98,38 @@ class LowRankEngine:
             return ops.col_normalize_2d(V, eps, sumsq=sq)
         return V / sq.sqrt().clamp(min=eps).to(V.dtype)
 
+    # ---- orthonormal basis of P
+    def _orthonormal_rows_sharded(self, Pf: Tensor) -> Tensor:
+        """Orthonormal basis of span(P) for a P whose rows may be split over
+        the process group: Gram + 1e-6 I, Cholesky, P L^-T, with a QR of P
+        when the factor is not finite (adadion.py:258-270). The shift keeps a
+        rank-deficient P factorable, as in the reference.
+
+        CUDA: the Gram and P L^-T on the tcgen05 GEMM in 3xTF32 (fp32-level
+        accuracy), the blocked Cholesky kernel and the triangular-inverse
+        kernel; one host read decides the QR fallback (the reference's own
+        check of the factor)."""
+        if Pf.is_cuda and ops.has_ext():
+            from .linalg import cholesky_lower, tri_inv_lower
+
+            gram = ops.matmul_precise(Pf.T, Pf)  # fp32-accurate: the Cholesky squares its error
+            self.all_reduce(gram)
+            gram.diagonal().add_(1e-6)
+            L = cholesky_lower(gram.unsqueeze(0))
+            if bool(torch.isfinite(L).all()):
+                Z = tri_inv_lower(L)[0]
+                return ops.matmul_precise(Pf, Z.T)
+            Po, _ = torch.linalg.qr(Pf)
+            return Po
+        gram = Pf.T @ Pf
+        self.all_reduce(gram)
+        gram.diagonal().add_(1e-6)
+        L, info = torch.linalg.cholesky_ex(gram)
+        if int(info.max().item()) == 0:
+            return torch.linalg.solve_triangular(L, Pf.T, upper=False).T
+        Po, _ = torch.linalg.qr(Pf)
+        return Po
+
     # ---- power step
     def power_step(self, B: Tensor, Qbuf: Tensor, r: int, tr: bool, ml: int, n: int,
                    anchor: Optional[Tensor] = None, anchor_alpha: float = 0.0):
@@ -106,14 +138,7 @@ class LowRankEngine:
         if not tr:
             Qp = Qbuf[:n, :r]
             Pf = _mm(B, Qp.to(dt)).float()
-            gram = Pf.T @ Pf
-            self.all_reduce(gram)
-            gram.diagonal().add_(1e-6)
-            L, info = torch.linalg.cholesky_ex(gram)
-            if int(info.max().item()) == 0:
-                Po = torch.linalg.solve_triangular(L, Pf.T, upper=False).T
-            else:
-                Po, _ = torch.linalg.qr(Pf)
+            Po = self._orthonormal_rows_sharded(Pf)
             Pd = Po.to(dt)
             R = _mm(B.float().T.contiguous(), Po).to(dt)
             self.all_reduce(R)
@@ -128,7 +153,7 @@ class LowRankEngine:
         Qp = Qbuf[:ml, :r]
         Phf = _mm(B.float().T.contiguous(), Qp.float())
         self.all_reduce(Phf)
-        Po, _ = torch.linalg.qr(Phf, mode="reduced")
+        Po, _ = torch.linalg.qr(Phf, mode="reduced")  # Householder: defined for rank-deficient P too
         Pd = Po.to(dt)
         R = _mm(B, Pd)
         approx = _mm(R, Pd.T.contiguous())
@@ -154,18 +179,31 @@ class LowRankEngine:
     def sq_sum(self, X: Tensor) -> Tensor:
         return self.all_reduce(X.float().pow(2).sum())
 
+    def sq_sums(self, *xs: Tensor, reduce: Optional[List[bool]] = None) -> List[float]:
+        """Sums of squares of several tensors with ONE all-reduce and ONE
+        host read: the per-matrix measurements of a step are packed into a
+        vector instead of a blocking collective per quantity. ``reduce[i]``
+        False keeps entry i local (a quantity that is already replicated)."""
+        v = torch.stack([x.float().pow(2).sum() for x in xs])
+        if reduce is None or all(reduce):
+            self.all_reduce(v)
+        elif any(reduce):
+            mask = torch.tensor(reduce, device=v.device)
+            part = torch.where(mask, v, torch.zeros_like(v))
+            self.all_reduce(part)
+            v = torch.where(mask, part, v)
+        return v.tolist()
+
     def rel_residual(self, A: Tensor, B: Tensor) -> float:
         """||A - B||_F / ||A||_F over all shards."""
-        num = self.sq_sum(A - B)
-        den = self.sq_sum(A)
-        return (num.sqrt() / (den.sqrt() + 1e-12)).item()
+        num, den = self.sq_sums(A - B, A)
+        return math.sqrt(num) / (math.sqrt(den) + 1e-12)
 
     def tail(self, M: Tensor, Q: Tensor, tr: bool) -> float:
         """||(I - Q Q^T) M||_F / ||M||_F on the basis side of the orientation."""
         proj = _mm(Q, _mm(Q.T.contiguous(), M)) if tr else _mm(_mm(M, Q), Q.T.contiguous())
-        t = self.sq_sum(M - proj)
-        m = self.sq_sum(M)
-        return (t.sqrt() / (m.sqrt() + 1e-12)).item()
+        t, m = self.sq_sums(M - proj, M)
+        return math.sqrt(t) / (math.sqrt(m) + 1e-12)
 
     def drift(self, Qn: Tensor, anchor: Optional[Tensor], r: int, tr: bool) -> float:
         if anchor is None:

@@ -78,16 +78,22 @@ class AsyncTask:
     """A generator-backed unit of optimizer work; each ``yield`` marks a point
     where the task waits on an asynchronous collective."""
 
-    def __init__(self, gen: Generator[None, None, None]):
+    def __init__(self, gen: Generator[None, None, None], stream: Optional["torch.cuda.Stream"] = None):
         self._gen = gen
+        self._stream = stream
         self.done = False
         self.step()
 
     def step(self) -> bool:
+        """Run the task to its next ``yield`` (on its own CUDA stream, if it has one)."""
         if self.done:
             return False
         try:
-            next(self._gen)
+            if self._stream is None:
+                next(self._gen)
+            else:
+                with torch.cuda.stream(self._stream):
+                    next(self._gen)
             return True
         except StopIteration:
             self.done = True

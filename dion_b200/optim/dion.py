@@ -32,6 +32,7 @@ B200 design:
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 from typing import Any, Dict, Iterator, List, Optional, Tuple, Union
 
@@ -182,6 +183,9 @@ class Dion(Optimizer):
         self._p2p_ptrs: Dict[Tuple, Any] = {}
         # signature sets in flight at once (the reference keeps three, adadion_v2.py:286)
         self._max_concurrent_tasks = 3
+        self._side_streams: Dict[Any, List[Any]] = {}
+        self._next_stream = 0
+        self._use_side_streams = os.environ.get("DION_B200_SIDE_STREAMS", "1") != "0"
         self._q_init_calls = 0
 
     # ------------------------------------------------------------------ step
@@ -199,8 +203,13 @@ class Dion(Optimizer):
         # ada_dion/optim/dion_utils.py:121-145)
         dion_groups = [(g, [p for p in g["params"] if p.grad is not None]) for g in self.param_groups
                        if g["algorithm"] == "dion"]
-        AsyncRuntime((t for g, ps in dion_groups if ps for t in self._dion_tasks(g, ps)),
+        used_streams: List[Any] = []
+        AsyncRuntime((t for g, ps in dion_groups if ps for t in self._dion_tasks(g, ps, used_streams)),
                      max_concurrent_tasks=self._max_concurrent_tasks).run()
+        if used_streams:  # the rest of the step (and of training) sees every set's update
+            main = torch.cuda.current_stream()
+            for st in used_streams:
+                main.wait_stream(st)
         for group in self.param_groups:
             algo = group["algorithm"]
             params = [p for p in group["params"] if p.grad is not None]
@@ -456,24 +465,51 @@ class Dion(Optimizer):
         return [x.wait() if hasattr(x, "wait") else x for x in funcol.all_reduce_coalesced(ts, reduceOp=op, group=pg)]
 
     # ------------------------------------------------------------------ dion
-    def _dion_tasks(self, group: dict, params: List[Tensor]) -> Iterator[AsyncTask]:
+    def _task_stream(self, device: torch.device, used: List[Any]):
+        """CUDA stream for the next signature set: a pool of
+        ``max_concurrent_tasks`` side streams, so the sets in flight also run
+        concurrently on the GPU (the factorisations of one set are latency-
+        bound and leave most SMs to the next set's GEMMs). Each stream first
+        waits for the work already queued on the current stream (the
+        gradients)."""
+        if device.type != "cuda" or not self._use_side_streams:
+            return None
+        pool = self._side_streams.get(device)
+        if pool is None:
+            pool = [torch.cuda.Stream(device=device) for _ in range(self._max_concurrent_tasks)]
+            self._side_streams[device] = pool
+        st = pool[self._next_stream % len(pool)]
+        self._next_stream += 1
+        st.wait_stream(torch.cuda.current_stream(device))
+        if st not in used:
+            used.append(st)
+        return st
+
+    def _dion_tasks(self, group: dict, params: List[Tensor], used_streams: Optional[List[Any]] = None
+                    ) -> Iterator[AsyncTask]:
         """One task per same-signature set of this group (created lazily, so
         the runtime holds at most ``max_concurrent_tasks`` sets' buffers)."""
+        used = used_streams if used_streams is not None else []
+        self._next_stream = 0
         for same in group_by_signature(params).values():
             cfg = self._get_dion_param_config(same[0])
             shape = "x".join(str(d) for d in same[0].shape)
+            st = self._task_stream(to_local(same[0]).device, used)
             if cfg.inner_shard_mesh_dim is not None:
-                yield AsyncTask(_sync_task(f"dion/fsdp_tp/{shape}", self._dion_fsdp_tp, group, same, cfg))
+                yield AsyncTask(_sync_task(f"dion/fsdp_tp/{shape}", self._dion_fsdp_tp, group, same, cfg), st)
             elif cfg.outer_shard_mesh_dim is not None and self._outer_shard_mesh.size() > 1:
-                yield AsyncTask(self._dion_sharded_gen(group, same, cfg, f"dion/sharded/{shape}"))
+                yield AsyncTask(self._dion_sharded_gen(group, same, cfg, f"dion/sharded/{shape}"), st)
             else:
-                yield AsyncTask(self._dion_replicated_gen(group, same, cfg, f"dion/replicated/{shape}"))
+                yield AsyncTask(self._dion_replicated_gen(group, same, cfg, f"dion/replicated/{shape}"), st)
 
     def _dion_group(self, group: dict, params: List[Tensor]) -> None:
         """All of one group's sets, one after the other (no overlap)."""
-        for t in self._dion_tasks(group, params):
+        used: List[Any] = []
+        for t in self._dion_tasks(group, params, used):
             while t.step():
                 pass
+        for st in used:
+            torch.cuda.current_stream().wait_stream(st)
 
     # hooks overridden by the adaptive-rank subclass
     def _active_q(self, params, order, Qb):
@@ -689,7 +725,8 @@ class Dion(Optimizer):
         if r % 4:
             return None
         slot = pd * r * 4
-        return heap_for(pg, 2 * W * sets * slot + W * sets * W * r * 4, "dion", Mb.device)
+        # one heap per signature: sets on different streams never share peer buffers
+        return heap_for(pg, 2 * W * sets * slot + W * sets * W * r * 4, f"dion:{pd}x{r}:{sets}", Mb.device)
 
     def _p2p_sum(self, heap, sumsq: Tensor, sets: int, W: int, me: int, pd: int) -> Tensor:
         """All-reduce (sum) of the column sums of squares [sets*W, r] without
@@ -789,12 +826,17 @@ class Dion(Optimizer):
             R = R.redistribute(placements=[Replicate() if pl.is_partial() else pl for pl in R.placements])
             Pl, Rl = to_local(P).float().unsqueeze(0), to_local(R).float().unsqueeze(0).contiguous()
             Pl = Pl.contiguous()
-            nz = torch.tensor([float(bool((to_local(M) != 0).any()))], device=Pl.device)
+            # all-zero flag on the device (no host read per parameter)
+            nz = (to_local(M) != 0).any().to(torch.float32).view(1)
             Q0 = to_local(Qd).float().unsqueeze(0).contiguous()
             ops.dion_fixup_(Pl, Rl, Q0, nz)
             Ml = to_local(M)
-            upd = (Pl[0] @ Rl[0].mT)
-            Ml.add_((upd.mT if cfg.is_transposed else upd).to(Ml.dtype), alpha=-(1.0 - mu))
+            dt = self._op_dtype(Ml.dtype)
+            # M -= (1 - mu) P R^T (R P^T when transposed), in place on the tcgen05 GEMM
+            if cfg.is_transposed:
+                ops.matmul_update_([Ml], Rl.to(dt), Pl.to(dt).transpose(1, 2), gamma=1.0, delta=-(1.0 - mu))
+            else:
+                ops.matmul_update_([Ml], Pl.to(dt), Rl.to(dt).transpose(1, 2), gamma=1.0, delta=-(1.0 - mu))
             sumsq = ops.col_sumsq(Rl)
             if cfg.outer_shard_mesh_dim is not None:
                 dist.all_reduce(sumsq, group=R.device_mesh.get_group(cfg.outer_shard_mesh_dim))
@@ -802,8 +844,12 @@ class Dion(Optimizer):
             ops.col_normalize(Rl, sumsq, eps, Qn)
             s_lr = self._scaled_lr(p.shape, lr)
             Xl = to_local(p)
-            u = Pl[0] @ Qn[0].mT
-            Xl.mul_(1.0 - lr * wd).add_((u.mT if cfg.is_transposed else u).to(Xl.dtype), alpha=-s_lr)
+            xdt = self._op_dtype(Xl.dtype)
+            # X = (1 - lr wd) X - s_lr P Q^T (Q P^T when transposed), in place
+            if cfg.is_transposed:
+                ops.matmul_update_([Xl], Qn.to(xdt), Pl.to(xdt).transpose(1, 2), gamma=1.0 - lr * wd, delta=-s_lr)
+            else:
+                ops.matmul_update_([Xl], Pl.to(xdt), Qn.to(xdt).transpose(1, 2), gamma=1.0 - lr * wd, delta=-s_lr)
             Qfull = DTensor.from_local(Qn[0].to(to_local(Qd).dtype), Qd.device_mesh, Qd.placements, run_check=False,
                                        shape=Qd.shape, stride=Qd.stride())
             to_local(st["Q"]).copy_(to_local(Qfull.redistribute(placements=cfg.Q_sharded_placements)))

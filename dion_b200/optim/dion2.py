@@ -175,6 +175,9 @@ class Dion2(Optimizer):
         eps = float(g["epsilon"])
         sharded = isinstance(p0, DTensor) and any(
             pl.is_shard() and p0.device_mesh.size(i) > 1 for i, pl in enumerate(p0.placements))
+        if M[0].is_cuda and ops.has_ext() and ops._uniform_matrices(M) and ops._uniform_matrices(X):
+            self._dion2_group_kernels(g, p0, X, M, lr, wd, adj, eps, sharded)
+            return
         Mb = ops.as_batch(M)
         stacked = Mb is None
         if stacked:
@@ -204,6 +207,42 @@ class Dion2(Optimizer):
         if stacked:
             for m, mb in zip(M, Mb.unbind(0)):
                 m.copy_(mb)
+
+    def _orthogonalize(self, sel: Tensor, eps: float, p0: Tensor, sharded: bool, tp_dim, dp_dim) -> Tensor:
+        if tp_dim is not None and self._world == 1:
+            return self._ns_tp_gathered(sel, tp_dim, eps)
+        if sharded and self._world > 1 and dp_dim is not None:
+            return self._orthogonalize_sharded(sel, eps, tp_dim, dp_dim)
+        if self._pg is not None and self._world > 1:
+            return self._orthogonalize_replicated(sel, eps)
+        return ops.newton_schulz(sel.contiguous(), self._coeffs, eps, clobber_input=True)
+
+    def _dion2_group_kernels(self, g, p0, X, M, lr, wd, adj, eps, sharded) -> None:
+        """The update on the package's kernels: L1 row scores, per-matrix top-k,
+        gather of the selected rows with their selective decay in the same pass,
+        Newton-Schulz, and one row-sparse weight update over every matrix (no
+        stacking copy of the momentum, no per-matrix loop)."""
+        rows = M[0].shape[0]
+        k = max(1, int(math.ceil(float(g["fraction"]) * rows)))
+        k = min(k, rows)
+        tp_dim = self._tp_dim(p0)
+        dp_dim = self._dp_dim(p0) if sharded else None
+        col_groups = [pg for pg, d in ((self._tp_pg, tp_dim), (self._pg, dp_dim)) if d == 1 and pg is not None]
+        scores = None
+        if g["selection_method"] == "random":
+            if self._gen is None or self._gen.device != M[0].device:
+                self._gen = torch.Generator(device=M[0].device).manual_seed(self._seed)
+            scores = torch.rand((len(M), rows), device=M[0].device, generator=self._gen)
+
+        def reduce_scores(sc):
+            if scores is None:
+                for pg in col_groups:
+                    dist.all_reduce(sc, group=pg)
+
+        idx, pos = ops.dion2_select_rows(M, k, scores, reduce_scores)
+        sel = ops.dion2_gather_decay_(M, idx, float(g["ef_decay"]))
+        U = self._orthogonalize(sel, eps, p0, sharded, tp_dim, dp_dim)
+        ops.dion2_update_(X, pos, U, 1.0 - lr * wd, adj)
 
     def _orthogonalize_replicated(self, sel: Tensor, eps: float) -> Tensor:
         W, r = self._world, self._rank

@@ -88,10 +88,9 @@ class GSDion(LowRankOptimizer):
         """RMS over the whole (possibly row-sharded) matrix."""
         if not tr:
             return _rms(X).item()
-        s = self.engine.all_reduce(X.float().pow(2).sum())
-        c = torch.tensor(float(X.numel()), device=X.device)
-        self.engine.all_reduce(c)
-        return (s / c).sqrt().item()
+        # every row shard holds the same number of entries: one all-reduce of the sum of squares
+        (s,) = self.engine.sq_sums(X)
+        return math.sqrt(s / (X.numel() * self.engine.world_size()))
 
     def _matrix_step(self, p, g: Dict[str, Any], st: Dict[str, Any]) -> None:
         eng = self.engine

@@ -13,6 +13,7 @@ from __future__ import annotations
 import math
 from typing import Any, Dict, Optional
 
+import torch
 from torch.distributed.device_mesh import DeviceMesh
 
 from ._lowrank import LowRankOptimizer, _mm
@@ -75,18 +76,18 @@ class QCDion(LowRankOptimizer):
         M.mul_(mu).add_(grad)
         B = M + grad
         D, approx, Qn, _ = eng.power_step(B, Qbuf, r, tr, ml, n)
-        M_fro = eng.sq_sum(M).sqrt().item() + 1e-12
-        q_t = eng.sq_sum(B - approx).sqrt().item() / (M_fro + 1e-12)
         proj = _mm(Qn, Qn.T.contiguous())
-        if st["Q_prev_proj"] is not None and proj.shape == st["Q_prev_proj"].shape:
-            d = (proj - st["Q_prev_proj"]).float().pow(2).sum()
-            if tr:
-                eng.all_reduce(d)
-            d_t = d.sqrt().item()
-        else:
-            d_t = 0.0
+        has_prev = st["Q_prev_proj"] is not None and proj.shape == st["Q_prev_proj"].shape
+        dproj = proj - st["Q_prev_proj"] if has_prev else torch.zeros((), device=proj.device)
+        # the step's four measurements: one all-reduce, one host read (the
+        # projector difference is replicated unless the basis is row-sharded)
+        m_sq, q_sq, e_sq, d_sq = eng.sq_sums(M, B - approx, B - (1.0 - mu) * approx - M, dproj,
+                                             reduce=[True, True, True, bool(tr)])
+        M_fro = math.sqrt(m_sq) + 1e-12
+        q_t = math.sqrt(q_sq) / (M_fro + 1e-12)
+        d_t = math.sqrt(d_sq) if has_prev else 0.0
         st["Q_prev_proj"] = proj.clone()
-        e_t = eng.sq_sum(B - (1.0 - mu) * approx - M).sqrt().item() / (M_fro + 1e-12)
+        e_t = math.sqrt(e_sq) / (M_fro + 1e-12)
         z_t = g["gate_w_q"] * q_t + g["gate_w_d"] * d_t + g["gate_w_e"] * e_t
         extra = False
         if g["use_extra_power"] and q_t > g["tau_extra"]:

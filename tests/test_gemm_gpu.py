@@ -136,3 +136,19 @@ def test_matmul_to_ptrs_rotation_and_row_split(rot_b, rot_rows):
     ops.matmul_to_ptrs(A, B, ptrs2, N, torch.float32, nrep=2, rot_b=rot_b, rot_rows=rot_rows)
     torch.testing.assert_close(out2[0], out, rtol=0, atol=0)
     torch.testing.assert_close(out2[1], out, rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("shape", [(256, 4096, 256), (64, 1000, 96), (3, 512, 300, 64)])
+def test_matmul_precise_is_fp32_accurate(shape):
+    """3xTF32 on the tensor cores in K chunks: relative error near fp32
+    SGEMM's (plain tf32 is ~1e-3)."""
+    g = torch.Generator(device="cuda").manual_seed(4)
+    *b, m, k, n = shape
+    A = torch.randn(*b, m, k, device="cuda", generator=g)
+    B = torch.randn(*b, k, n, device="cuda", generator=g)
+    ref = A.double() @ B.double()
+    out = ops.matmul_precise(A, B)
+    rel = ((out.double() - ref).norm() / ref.norm()).item()
+    assert rel < 5e-6, rel
+    plain = ops.matmul(A, B)
+    assert ((plain.double() - ref).norm() / ref.norm()).item() > 10 * rel
