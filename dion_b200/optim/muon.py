@@ -232,10 +232,13 @@ class Muon(Optimizer):
     def _shard_dim(self, p: Tensor) -> Optional[int]:
         if not isinstance(p, DTensor):
             return None
-        if not isinstance(self._distributed_mesh, DeviceMesh):
-            raise RuntimeError("Must create optimizer with DeviceMesh if using DTensor parameters.")
         shards = [(i, pl) for i, pl in enumerate(p.placements) if pl.is_shard() and p.device_mesh.size(i) > 1]
         names = p.device_mesh.mesh_dim_names or ()
+        if not isinstance(self._distributed_mesh, DeviceMesh):
+            # tensor parallelism alone (no FSDP mesh): the TP blocks are gathered per matrix
+            if self._tp_pg is not None and all(names and names[i] == "tp" for i, _ in shards):
+                return None
+            raise RuntimeError("Must create optimizer with DeviceMesh if using DTensor parameters.")
         if "tp" in names:
             shards = [(i, pl) for i, pl in shards if names[i] != "tp"]
         if not shards:
@@ -277,7 +280,12 @@ class Muon(Optimizer):
         if mats > 1:
             # per-matrix norms for stacked 3-D params
             scale = None
-        O = self._ns(U, scale, eps)
+        tp_dim = self._tp_dim(params[0]) if mats == 1 and X[0].ndim == 2 else None
+        if tp_dim is not None:
+            # TP without FSDP: every rank of the TP group orthogonalises the whole matrices
+            O = self._ns_tp_gathered(U, tp_dim, eps)
+        else:
+            O = self._ns(U, scale, eps)
         ops.scaled_update_(X, [o.view(shape) for o in O.view(n, *shape).unbind(0)], decay, [adj_lr] * n)
 
     def _muon_ddp(self, params, states, mu, nesterov, eps, decay, adj_lr, group) -> None:
