@@ -31,6 +31,29 @@ struct AddArgs {
 
 __device__ __forceinline__ float nan0(float v) { return (v != v) ? 0.f : (isinf(v) ? copysignf(3.402823466e38f, v) : v); }
 
+// 4-element vector load / store of fp32 (16 bytes) or bf16 (8 bytes), as fp32
+__device__ __forceinline__ void load4(const float* p, float (&v)[4]) {
+  const float4 x = *reinterpret_cast<const float4*>(p);
+  v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+}
+__device__ __forceinline__ void load4(const __nv_bfloat16* p, float (&v)[4]) {
+  const uint2 x = *reinterpret_cast<const uint2*>(p);
+  const __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(&x.x);
+  const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(&x.y);
+  v[0] = __low2float(lo); v[1] = __high2float(lo); v[2] = __low2float(hi); v[3] = __high2float(hi);
+}
+__device__ __forceinline__ void store4(float* p, const float (&v)[4]) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+}
+__device__ __forceinline__ void store4(__nv_bfloat16* p, const float (&v)[4]) {
+  const __nv_bfloat162 lo = __floats2bfloat162_rn(v[0], v[1]);
+  const __nv_bfloat162 hi = __floats2bfloat162_rn(v[2], v[3]);
+  uint2 x;
+  x.x = *reinterpret_cast<const uint32_t*>(&lo);
+  x.y = *reinterpret_cast<const uint32_t*>(&hi);
+  *reinterpret_cast<uint2*>(p) = x;
+}
+
 template <typename MT, typename GT>
 __global__ void __launch_bounds__(kThreads) momentum_add_kernel(AddArgs a, float* partial_max) {
   __shared__ float sh[32];
@@ -42,10 +65,28 @@ __global__ void __launch_bounds__(kThreads) momentum_add_kernel(AddArgs a, float
   MT* M = reinterpret_cast<MT*>(a.m[t]);
   const GT* G = reinterpret_cast<const GT*>(a.g[t]);
   float mx = 0.f;
-  for (int64_t i = lo + threadIdx.x; i < hi; i += kThreads) {
-    const float v = to_f<MT>(M[i]) + to_f<GT>(G[i]);
-    M[i] = from_f<MT>(v);
-    mx = fmaxf(mx, fabsf(v) + (v != v ? 1.f : 0.f));
+  // four elements a thread per access when both rows of storage allow it
+  // (16-byte fp32 / 8-byte bf16 groups); chunks start at multiples of 4
+  const bool vec = (a.numel[t] % 4 == 0) && (reinterpret_cast<uintptr_t>(M) % (4 * sizeof(MT)) == 0) &&
+                   (reinterpret_cast<uintptr_t>(G) % (4 * sizeof(GT)) == 0);
+  if (vec) {
+    for (int64_t i = lo + 4 * threadIdx.x; i < hi; i += 4 * kThreads) {
+      float m4[4], g4[4];
+      load4(M + i, m4);
+      load4(G + i, g4);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        m4[e] += g4[e];
+        mx = fmaxf(mx, fabsf(m4[e]) + (m4[e] != m4[e] ? 1.f : 0.f));
+      }
+      store4(M + i, m4);
+    }
+  } else {
+    for (int64_t i = lo + threadIdx.x; i < hi; i += kThreads) {
+      const float v = to_f<MT>(M[i]) + to_f<GT>(G[i]);
+      M[i] = from_f<MT>(v);
+      mx = fmaxf(mx, fabsf(v) + (v != v ? 1.f : 0.f));
+    }
   }
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffff, mx, o));
   if ((threadIdx.x & 31) == 0) sh[threadIdx.x / 32] = mx;
@@ -73,7 +114,45 @@ __global__ void fixup_kernel(float* P, int64_t pn, float* R, const QT* Q0, int64
   float* Pb = P + (int64_t)b * pn;
   float* Rb = R + (int64_t)b * rn;
   const QT* Qb = Q0 + (int64_t)b * rn;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < max(pn, rn); i += (int64_t)gridDim.x * blockDim.x) {
+  // kept matrices are read and rewritten only where a value is not finite
+  // (normally nothing is written); dropped ones take P = 0, R = Q0
+  const bool vec = pn % 4 == 0 && rn % 4 == 0 && reinterpret_cast<uintptr_t>(Pb) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(Rb) % 16 == 0 && reinterpret_cast<uintptr_t>(Qb) % (4 * sizeof(QT)) == 0;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  if (vec) {
+    for (int64_t i = 4 * ((int64_t)blockIdx.x * blockDim.x + threadIdx.x); i < max(pn, rn); i += 4 * stride) {
+      if (i < pn) {
+        float v[4];
+        if (keep) {
+          load4(Pb + i, v);
+          if (!(isfinite(v[0]) && isfinite(v[1]) && isfinite(v[2]) && isfinite(v[3]))) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) v[e] = nan0(v[e]);
+            store4(Pb + i, v);
+          }
+        } else {
+          v[0] = v[1] = v[2] = v[3] = 0.f;
+          store4(Pb + i, v);
+        }
+      }
+      if (i < rn) {
+        float v[4];
+        if (keep) {
+          load4(Rb + i, v);
+          if (!(isfinite(v[0]) && isfinite(v[1]) && isfinite(v[2]) && isfinite(v[3]))) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) v[e] = nan0(v[e]);
+            store4(Rb + i, v);
+          }
+        } else {
+          load4(Qb + i, v);
+          store4(Rb + i, v);
+        }
+      }
+    }
+    return;
+  }
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < max(pn, rn); i += stride) {
     if (i < pn) Pb[i] = keep ? nan0(Pb[i]) : 0.f;
     if (i < rn) Rb[i] = keep ? nan0(Rb[i]) : to_f<QT>(Qb[i]);
   }
@@ -228,6 +307,7 @@ void dion_fixup(at::Tensor& P, at::Tensor& R, const at::Tensor& Q0, const at::Te
               "dion_b200 fixup: contiguous fp32 P/R expected");
   c10::cuda::CUDAGuard guard(P.device());
   const int b = (int)P.size(0);
+  if (b == 0 || P.numel() == 0) return;  // nothing to do (e.g. a rank that holds no matrix of a batch)
   const int64_t pn = P.numel() / b, rn = R.numel() / b;
   dim3 grid((unsigned)std::min<int64_t>((std::max(pn, rn) + 255) / 256, 1024), b);
   auto s = at::cuda::getCurrentCUDAStream();
@@ -243,6 +323,7 @@ void col_sumsq(const at::Tensor& R, at::Tensor& out) {
   TORCH_CHECK(R.dim() == 3 && R.is_contiguous() && R.scalar_type() == at::kFloat, "dion_b200 col_sumsq: [b,rows,r] fp32");
   c10::cuda::CUDAGuard guard(R.device());
   const int b = (int)R.size(0), rows = (int)R.size(1), r = (int)R.size(2);
+  if (b == 0 || R.numel() == 0) return;  // nothing to do (e.g. a rank that holds no matrix of a batch)
   const bool vec4 = r % 4 == 0;
   const int rows_per_chunk = vec4 ? kRowsPerChunk4 : kRowsPerChunk;
   const int chunks = (rows + rows_per_chunk - 1) / rows_per_chunk;
@@ -271,6 +352,7 @@ void col_normalize(const at::Tensor& R, const at::Tensor& sumsq, double eps, at:
               "dion_b200 col_normalize: Q shape");
   c10::cuda::CUDAGuard guard(R.device());
   const int b = (int)R.size(0), rows = (int)R.size(1), r = (int)R.size(2);
+  if (b == 0 || R.numel() == 0) return;  // nothing to do (e.g. a rank that holds no matrix of a batch)
   const int64_t total = (int64_t)rows * r;
   auto s = at::cuda::getCurrentCUDAStream();
   const int qsz = (int)Q.element_size();

@@ -100,6 +100,7 @@ void gemm_ex(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10:
   const int64_t batch = A.size(0), M = A.size(1), K = A.size(2), N = B.size(2);
   TORCH_CHECK(B.size(0) == batch && B.size(1) == K, "dion_b200 gemm: shape mismatch");
   TORCH_CHECK(K > 0 && M > 0 && N > 0, "dion_b200 gemm: empty problem");
+  if (batch == 0) return;  // an empty batch (a rank that holds no matrix of a set)
   const bool use_ptrs = D_ptrs.has_value() && D_ptrs->defined();
   if (!use_ptrs) {
     TORCH_CHECK(D.is_cuda() && D.dim() == 3 && D.size(0) == batch && D.size(1) == M && D.size(2) == N &&

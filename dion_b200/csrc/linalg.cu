@@ -531,6 +531,7 @@ void cholesky_lower(at::Tensor& A, at::Tensor& info) {
   TORCH_CHECK(A.dim() == 3 && A.is_contiguous() && A.scalar_type() == at::kFloat && A.size(1) == A.size(2),
               "dion_b200 cholesky: contiguous [b, r, r] fp32");
   const int b = (int)A.size(0), r = (int)A.size(1);
+  if (b == 0 || A.numel() == 0) return;  // nothing to do (e.g. a rank that holds no matrix of a batch)
   const size_t smem = (size_t)(NB * LD + (size_t)r * LD) * sizeof(float);
   TORCH_CHECK(smem <= 227 * 1024, "dion_b200 cholesky: r too large for the single-CTA kernel");
   c10::cuda::CUDAGuard guard(A.device());
@@ -543,6 +544,7 @@ void tri_inv_lower(const at::Tensor& S, at::Tensor& Z, bool upper) {
   TORCH_CHECK(S.dim() == 3 && S.is_contiguous() && Z.is_contiguous() && S.scalar_type() == at::kFloat,
               "dion_b200 tri_inv: contiguous [b, r, r] fp32");
   const int b = (int)S.size(0), r = (int)S.size(1);
+  if (b == 0 || S.numel() == 0) return;  // nothing to do (e.g. a rank that holds no matrix of a batch)
   c10::cuda::CUDAGuard guard(S.device());
   auto stream = at::cuda::getCurrentCUDAStream();
   const int nblk = (r + NB - 1) / NB;
@@ -604,6 +606,7 @@ void qr_r(at::Tensor& A, at::Tensor& R) {
   TORCH_CHECK(A.dim() == 3 && A.is_contiguous() && A.scalar_type() == at::kFloat && A.size(1) >= A.size(2),
               "dion_b200 qr_r: contiguous [b, m, n] fp32 with m >= n");
   const int b = (int)A.size(0), m = (int)A.size(1), n = (int)A.size(2);
+  if (b == 0 || A.numel() == 0) return;  // nothing to do (e.g. a rank that holds no matrix of a batch)
   const size_t smem = ((size_t)m * QLD + NB * LD + 40 + 2 * NB) * sizeof(float);
   TORCH_CHECK(smem <= 227 * 1024, "dion_b200 qr_r: m too large for the panel kernel");
   c10::cuda::CUDAGuard guard(A.device());

@@ -33,7 +33,9 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <algorithm>
 #include <cstdlib>
+#include <string>
 
 #include "common.cuh"
 #include "host_utils.h"
@@ -251,13 +253,19 @@ __global__ void __launch_bounds__(QP_T, 1)
 // columns c and c + 32 of the tile.
 constexpr int QW_T = 256;
 constexpr int QW_COLS = 64;
+// With splits > 1 (grid.z = splits) each CTA takes one row range and writes
+// its partial V^T C to Wp [b, splits, PB, nt]; qr_w_finish_kernel sums them.
 __global__ void __launch_bounds__(QW_T) qr_w_kernel(const float* __restrict__ A_all, int n, int64_t bstride, int j0,
                                                   int rows, int nt, const float* __restrict__ Vg_all, int64_t vstride,
                                                   const float* __restrict__ Tg_all, float* __restrict__ Wc_all,
-                                                  int64_t wstride, int ldw) {
+                                                  int64_t wstride, int ldw, int splits, float* __restrict__ Wp_all) {
   const int mat = blockIdx.y;
   const int col0 = blockIdx.x * QW_COLS;
   const int w = threadIdx.x / 32, c = threadIdx.x % 32;
+  const int split = blockIdx.z;
+  const int rchunk = ((rows + splits - 1) / splits + 7) / 8 * 8;
+  const int r_lo = split * rchunk;
+  const int r_hi = min(rows, r_lo + rchunk);
   const float* Ct = A_all + (int64_t)mat * bstride + (int64_t)j0 * n + j0 + PB + col0;
   const float* V = Vg_all + (int64_t)mat * vstride;
   const bool ok0 = col0 + c < nt, ok1 = col0 + 32 + c < nt;
@@ -266,8 +274,8 @@ __global__ void __launch_bounds__(QW_T) qr_w_kernel(const float* __restrict__ A_
   for (int a = 0; a < PB; ++a) acc0[a] = acc1[a] = 0.f;
   // rows in batches of kRB per warp: all 2*kRB loads of the batch are issued before the FMAs
   constexpr int kRB = 8;
-  int i0 = w;
-  for (; i0 + 8 * (kRB - 1) < rows; i0 += 8 * kRB) {
+  int i0 = r_lo + w;
+  for (; i0 + 8 * (kRB - 1) < r_hi; i0 += 8 * kRB) {
     float x0[kRB], x1[kRB];
 #pragma unroll
     for (int u = 0; u < kRB; ++u) {
@@ -291,7 +299,7 @@ __global__ void __launch_bounds__(QW_T) qr_w_kernel(const float* __restrict__ A_
       }
     }
   }
-  for (int i = i0; i < rows; i += 8) {
+  for (int i = i0; i < r_hi; i += 8) {
     const float x0 = ok0 ? Ct[(int64_t)i * n + c] : 0.f;
     const float x1 = ok1 ? Ct[(int64_t)i * n + 32 + c] : 0.f;
     const float4* vr = reinterpret_cast<const float4*>(V + (int64_t)i * PB);
@@ -328,6 +336,14 @@ __global__ void __launch_bounds__(QW_T) qr_w_kernel(const float* __restrict__ A_
     for (int q = 0; q < 8; ++q) sacc += part[(q * PB + b) * PL + col];
     part[b * PL + col] = sacc;  // q = 0 slot: only this thread reads or writes (b, col)
   }
+  if (splits > 1) {
+    float* Wp = Wp_all + ((int64_t)mat * splits + split) * PB * nt;
+    for (int e = threadIdx.x; e < PB * QW_COLS; e += QW_T) {
+      const int b = e / QW_COLS, col = e % QW_COLS;
+      if (col0 + col < nt) Wp[(int64_t)b * nt + col0 + col] = part[b * PL + col];
+    }
+    return;
+  }
   __syncthreads();
   float* Wc = Wc_all + (int64_t)mat * wstride;
   for (int e = threadIdx.x; e < PB * QW_COLS; e += QW_T) {
@@ -344,6 +360,41 @@ __global__ void __launch_bounds__(QW_T) qr_w_kernel(const float* __restrict__ A_
   }
 }
 
+// W' = T^T sum_s Wp[s] for the row-split qr_w_kernel, written split like it.
+__global__ void __launch_bounds__(QW_T) qr_w_finish_kernel(const float* __restrict__ Wp_all, int splits, int nt,
+                                                         const float* __restrict__ Tg_all, float* __restrict__ Wc_all,
+                                                         int64_t wstride, int ldw) {
+  const int mat = blockIdx.y;
+  const int col0 = blockIdx.x * QW_COLS;
+  constexpr int PL = QW_COLS + 1;
+  __shared__ float sW[PB * PL];
+  __shared__ float sT[PB * PLD];
+  const float* Wp = Wp_all + (int64_t)mat * splits * PB * nt;
+  for (int e = threadIdx.x; e < PB * QW_COLS; e += QW_T) {
+    const int b = e / QW_COLS, col = e % QW_COLS;
+    float sacc = 0.f;
+    if (col0 + col < nt)
+      for (int q = 0; q < splits; ++q) sacc += Wp[((int64_t)q * PB + b) * nt + col0 + col];
+    sW[b * PL + col] = sacc;
+  }
+  const float* T = Tg_all + (int64_t)mat * PB * PB;
+  for (int e = threadIdx.x; e < PB * PB; e += QW_T) sT[(e / PB) * PLD + e % PB] = T[e];
+  __syncthreads();
+  float* Wc = Wc_all + (int64_t)mat * wstride;
+  for (int e = threadIdx.x; e < PB * QW_COLS; e += QW_T) {
+    const int a = e / QW_COLS, col = e % QW_COLS;
+    if (col0 + col >= nt) continue;
+    float sacc = 0.f;
+#pragma unroll
+    for (int b = 0; b < PB; ++b)
+      if (b <= a) sacc += sT[b * PLD + a] * sW[b * PL + col];
+    const float hi = tf32_hi(sacc);
+    Wc[(int64_t)a * ldw + col0 + col] = hi;
+    Wc[(int64_t)(PB + a) * ldw + col0 + col] = tf32_hi(sacc - hi);
+    Wc[(int64_t)(2 * PB + a) * ldw + col0 + col] = hi;
+  }
+}
+
 // R = upper triangle of A[:n, :n] (the R blocks of the panels plus the
 // trailing-update results left in rows that no later panel touches).
 __global__ void qr_extract_r_kernel(const float* __restrict__ A_all, int n, int64_t bstride,
@@ -353,6 +404,272 @@ __global__ void qr_extract_r_kernel(const float* __restrict__ A_all, int n, int6
   if (e >= (int64_t)n * n) return;
   const int i = (int)(e / n), j = (int)(e % n);
   R_all[(int64_t)mat * rstride + e] = j >= i ? A_all[(int64_t)mat * bstride + (int64_t)i * n + j] : 0.f;
+}
+
+// ------------------------------------------------------------ QR panel, register-resident
+// One CTA per matrix (no cluster), NW warps. Thread (w, lane) holds panel rows
+// gi(u) = (u * NW + w) * 32 + lane, u < R, with all 32 panel columns in
+// registers. Column step j:
+//   (1) each thread forms x_ij a_ic for its rows i > j and every column c; a
+//       warp transpose-reduction (32 shuffles) leaves lane c with the warp's
+//       sum of column c;
+//   (2) warp 0 adds the NW warp sums: D_c = sum_{i>j} x_ij a_ic. D_j is the
+//       squared norm below the diagonal, so the reflector needs no separate
+//       reduction; v_j^T a_c = a_jc + scale D_c is the update coefficient
+//       for c > j and the entry (V^T V)_{cj} of T's input for c < j;
+//   (3) each thread applies the reflector to its own rows.
+// Two CTA barriers per column and no shared-memory traffic proportional to
+// the panel (the shared-memory panel kernel above is bound by it). Rows:
+// R = 1 up to 512 rows, R = 2 up to 1024 (512 threads), R = 3 up to 1344
+// (448 threads: 144 registers for the 96 panel values).
+constexpr unsigned kFullMask = 0xffffffffu;
+
+// d[0..15] per lane -> column (lane & 15) summed over all 32 lanes
+__device__ __forceinline__ float warp_colsum16(float (&d)[16], int lane) {
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const bool hi = lane & 8;
+    const float send = hi ? d[k] : d[k + 8];
+    const float keep = hi ? d[k + 8] : d[k];
+    d[k] = keep + __shfl_xor_sync(kFullMask, send, 8);
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const bool hi = lane & 4;
+    const float send = hi ? d[k] : d[k + 4];
+    const float keep = hi ? d[k + 4] : d[k];
+    d[k] = keep + __shfl_xor_sync(kFullMask, send, 4);
+  }
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const bool hi = lane & 2;
+    const float send = hi ? d[k] : d[k + 2];
+    const float keep = hi ? d[k + 2] : d[k];
+    d[k] = keep + __shfl_xor_sync(kFullMask, send, 2);
+  }
+  {
+    const bool hi = lane & 1;
+    const float send = hi ? d[0] : d[1];
+    const float keep = hi ? d[1] : d[0];
+    d[0] = keep + __shfl_xor_sync(kFullMask, send, 1);
+  }
+  return d[0] + __shfl_xor_sync(kFullMask, d[0], 16);
+}
+
+// d[0..7] per lane -> column (lane & 7) summed over all 32 lanes
+__device__ __forceinline__ float warp_colsum8(float (&d)[8], int lane) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const bool hi = lane & 4;
+    const float send = hi ? d[k] : d[k + 4];
+    const float keep = hi ? d[k + 4] : d[k];
+    d[k] = keep + __shfl_xor_sync(kFullMask, send, 4);
+  }
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const bool hi = lane & 2;
+    const float send = hi ? d[k] : d[k + 2];
+    const float keep = hi ? d[k + 2] : d[k];
+    d[k] = keep + __shfl_xor_sync(kFullMask, send, 2);
+  }
+  {
+    const bool hi = lane & 1;
+    const float send = hi ? d[0] : d[1];
+    const float keep = hi ? d[1] : d[0];
+    d[0] = keep + __shfl_xor_sync(kFullMask, send, 1);
+  }
+  d[0] += __shfl_xor_sync(kFullMask, d[0], 8);
+  return d[0] + __shfl_xor_sync(kFullMask, d[0], 16);
+}
+
+template <int R>
+constexpr int qr_reg_threads() {
+  return R <= 2 ? 512 : 448;  // 128 / 144 registers a thread: the R x 32 panel values
+}
+
+template <int R>
+__global__ void __launch_bounds__(qr_reg_threads<R>(), 1)
+    qr_panel_reg_kernel(float* __restrict__ A_all, int m, int n, int64_t bstride, int j0, int kb,
+                        float* __restrict__ Vg_all, float* __restrict__ Vc_all, float* __restrict__ Tg_all,
+                        int64_t vstride, int64_t cstride) {
+  const int mat = blockIdx.x;
+  const int rows = m - j0;
+  const int NW = (int)(blockDim.x >> 5);
+  const int w = (int)(threadIdx.x >> 5), lane = (int)(threadIdx.x & 31);
+  float* A = A_all + (int64_t)mat * bstride + (int64_t)j0 * n + j0;  // panel origin, row stride n
+  __shared__ float red[32][PLD];
+  __shared__ float rowj[PB];
+  __shared__ float coef[PB];
+  __shared__ float fj[PB];
+  __shared__ float sG[PB][PLD];
+  __shared__ float sTau[PB], sBeta[PB];
+
+  float a[R][PB];
+  int gi[R];
+#pragma unroll
+  for (int u = 0; u < R; ++u) {
+    gi[u] = (u * NW + w) * 32 + lane;
+    const bool ok = gi[u] < rows;
+    const float4* src = reinterpret_cast<const float4*>(A + (int64_t)(ok ? gi[u] : 0) * n);
+#pragma unroll
+    for (int c4 = 0; c4 < PB / 4; ++c4) {
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (ok && 4 * c4 < kb) v = src[c4];
+      a[u][4 * c4 + 0] = v.x;
+      a[u][4 * c4 + 1] = v.y;
+      a[u][4 * c4 + 2] = v.z;
+      a[u][4 * c4 + 3] = v.w;
+    }
+  }
+
+  // The loop is rolled (a fully unrolled 32-step body overflows the
+  // instruction cache); the register window rotates by one column a step so
+  // that column j always sits in slot 0: slot k holds column (k + j) mod 32.
+#pragma unroll 1
+  for (int j = 0; j < kb; ++j) {
+    // ---- (1) x_ij a_ic over this thread's rows below j; warp sums per slot
+    float xj[R];
+#pragma unroll
+    for (int u = 0; u < R; ++u) xj[u] = gi[u] > j ? a[u][0] : 0.f;
+    if (w == 0 && lane == j) {
+#pragma unroll
+      for (int k = 0; k < PB; ++k) rowj[k] = a[0][k];
+    }
+    // slot groups of GW (a transpose-reduction each; 8 wide beside a 3-row window)
+    constexpr int GW = R >= 3 ? 8 : 16;
+    float mine = 0.f;
+#pragma unroll
+    for (int h = 0; h < PB / GW; ++h) {
+      float d[GW];
+#pragma unroll
+      for (int k = 0; k < GW; ++k) {
+        float sacc = 0.f;
+#pragma unroll
+        for (int u = 0; u < R; ++u) sacc = fmaf(xj[u], a[u][GW * h + k], sacc);
+        d[k] = sacc;
+      }
+      float t;
+      if constexpr (GW == 16) {
+        t = warp_colsum16(d, lane);
+      } else {
+        t = warp_colsum8(d, lane);
+      }
+      if (lane / GW == h) mine = t;
+    }
+    red[w][lane] = mine;
+    __syncthreads();
+    // ---- (2) reflector and coefficients (warp 0, lane = slot, column c = (lane + j) mod 32)
+    if (w == 0) {
+      float tot = 0.f;
+      for (int q = 0; q < NW; ++q) tot += red[q][lane];
+      const float sigma = __shfl_sync(kFullMask, tot, 0);
+      const float x0 = rowj[0];
+      float beta, tau, scale;
+      if (sigma == 0.f) {
+        beta = x0;
+        tau = 0.f;
+        scale = 0.f;
+      } else {
+        const float nrm = sqrtf(x0 * x0 + sigma);
+        beta = x0 >= 0.f ? -nrm : nrm;
+        tau = (beta - x0) / beta;
+        scale = 1.f / (x0 - beta);
+      }
+      const int c = lane + j;                  // column + 32 if it wrapped (a finished column c - 32 < j)
+      const bool later = lane > 0 && c < PB;   // c > j
+      const float dot = rowj[lane] + scale * tot;  // v_j^T a_c (c > j) or v_c^T v_j (c < j)
+      const float f = tau * dot;
+      if (c >= PB) sG[c - PB][j] = dot;
+      coef[lane] = later ? f * scale : (lane == 0 ? 1.f - scale : 0.f);
+      fj[lane] = later ? f : 0.f;
+      if (lane == 0) {
+        sTau[j] = tau;
+        sBeta[j] = beta;
+      }
+    }
+    __syncthreads();
+    // ---- (3) apply to this thread's rows (slot 0 becomes v_j below the diagonal), then rotate
+#pragma unroll
+    for (int u = 0; u < R; ++u) {
+      const float x = a[u][0];
+      if (gi[u] > j) {
+#pragma unroll
+        for (int k = 0; k < PB; ++k) a[u][k] = fmaf(-coef[k], x, a[u][k]);
+      } else if (gi[u] == j) {
+#pragma unroll
+        for (int k = 1; k < PB; ++k) a[u][k] -= fj[k];
+        a[u][0] = sBeta[j];
+      }
+      const float first = a[u][0];
+#pragma unroll
+      for (int k = 0; k < PB - 1; ++k) a[u][k] = a[u][k + 1];
+      a[u][PB - 1] = first;
+    }
+  }
+  // a narrow last panel (kb < 32): rotate the window back to column order
+#pragma unroll 1
+  for (int j = kb; j < PB; ++j) {
+#pragma unroll
+    for (int u = 0; u < R; ++u) {
+      const float first = a[u][0];
+#pragma unroll
+      for (int k = 0; k < PB - 1; ++k) a[u][k] = a[u][k + 1];
+      a[u][PB - 1] = first;
+    }
+  }
+  // ---- R block: panel rows 0..kb-1 are warp 0's first row set
+  if (w == 0 && lane < kb) {
+    float* Arow = A + (int64_t)lane * n;
+#pragma unroll
+    for (int c = 0; c < PB; ++c)
+      if (c >= lane && c < kb) Arow[c] = a[0][c];
+  }
+  // ---- V: fp32 (for V^T C) and split [Vhi | Vhi | Vlo] (A operand of the 3xTF32 update)
+  float* Vg = Vg_all + (int64_t)mat * vstride;
+  float* Vc = Vc_all + (int64_t)mat * cstride;
+#pragma unroll
+  for (int u = 0; u < R; ++u) {
+    if (gi[u] < rows) {
+      float4* vg = reinterpret_cast<float4*>(Vg + (int64_t)gi[u] * PB);
+      float4* vc = reinterpret_cast<float4*>(Vc + (int64_t)gi[u] * KC);
+#pragma unroll
+      for (int c4 = 0; c4 < PB / 4; ++c4) {
+        float v[4], hi[4], lo[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int c = 4 * c4 + e;
+          v[e] = c < kb ? (gi[u] > c ? a[u][c] : (gi[u] == c ? 1.f : 0.f)) : 0.f;
+          hi[e] = tf32_hi(v[e]);
+          lo[e] = tf32_hi(v[e] - hi[e]);
+        }
+        vg[c4] = make_float4(v[0], v[1], v[2], v[3]);
+        vc[c4] = make_float4(hi[0], hi[1], hi[2], hi[3]);
+        vc[PB / 4 + c4] = make_float4(hi[0], hi[1], hi[2], hi[3]);
+        vc[2 * PB / 4 + c4] = make_float4(lo[0], lo[1], lo[2], lo[3]);
+      }
+    }
+  }
+  // (after the row outputs: the panel registers are free for T's row)
+  // ---- T (upper): T[a][j] = -tau_j sum_{b=a}^{j-1} T[a][b] G[b][j]; lane a builds row a
+  if (w == 0) {
+    const int ar = lane;
+    float trow[PB];
+#pragma unroll
+    for (int b = 0; b < PB; ++b) trow[b] = (b == ar && ar < kb) ? sTau[ar] : 0.f;
+#pragma unroll
+    for (int jj = 1; jj < PB; ++jj) {
+      float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+      for (int b = 0; b < jj; ++b) {
+        if (b & 1) s1 = fmaf(trow[b], sG[b][jj], s1);
+        else s0 = fmaf(trow[b], sG[b][jj], s0);
+      }
+      if (ar < jj && jj < kb) trow[jj] = -sTau[jj] * (s0 + s1);
+    }
+    float* Tg = Tg_all + (int64_t)mat * PB * PB;
+#pragma unroll
+    for (int b = 0; b < PB; ++b) Tg[ar * PB + b] = trow[b];
+  }
 }
 
 // ------------------------------------------------------------ Cholesky panel
@@ -469,6 +786,7 @@ void qr_r_blocked(at::Tensor& A, at::Tensor& R) {
   TORCH_CHECK(R.is_contiguous() && R.size(0) == A.size(0) && R.size(1) == A.size(2) && R.size(2) == A.size(2),
               "dion_b200 qr_r_blocked: R must be a contiguous [b, n, n] tensor");
   const int b = (int)A.size(0), m = (int)A.size(1), n = (int)A.size(2);
+  if (b == 0 || A.numel() == 0) return;  // nothing to do (e.g. a rank that holds no matrix of a batch)
   TORCH_CHECK((int64_t)m <= 8LL * kQrMaxChunk, "dion_b200 qr_r_blocked: m too large (at most 8 x 1400 rows)");
   c10::cuda::CUDAGuard guard(A.device());
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
@@ -491,9 +809,38 @@ void qr_r_blocked(at::Tensor& A, at::Tensor& R) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(qr_w_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)w_smem));
     w_attr = true;
   }
+  // panels of up to 1536 rows: the register-resident kernel (one CTA per matrix);
+  // DION_B200_QR_PANEL=smem keeps the shared-memory / cluster kernel throughout
+  static const bool reg_panels = [] {
+    const char* e = std::getenv("DION_B200_QR_PANEL");
+    return !(e && std::string(e) == "smem");
+  }();
+  // W' row splits: about two CTAs per SM over the batch (decided per panel, at most splits_max)
+  const int splits_max = std::max(1, std::min(8, (2 * 148) / b + 1));
+  at::Tensor Wp = splits_max > 1 ? at::empty({b, splits_max, PB, n}, opt) : at::Tensor();
   for (int j0 = 0; j0 < n; j0 += PB) {
     const int kb = std::min(PB, n - j0);
     const int rows = m - j0;
+    const int R = !reg_panels ? 0 : rows <= 512 ? 1 : rows <= 1024 ? 2 : rows <= 1344 ? 3 : 0;
+    if (R > 0) {
+      const int nw = (rows + 32 * R - 1) / (32 * R);
+      const dim3 grid((unsigned)b), block((unsigned)(32 * nw));
+      float* Ap = A.data_ptr<float>();
+      if (R == 1)
+        qr_panel_reg_kernel<1><<<grid, block, 0, stream>>>(Ap, m, n, bs, j0, kb, Vg.data_ptr<float>(),
+                                                           Vc.data_ptr<float>(), Tg.data_ptr<float>(),
+                                                           (int64_t)m * PB, (int64_t)m * KC);
+      else if (R == 2)
+        qr_panel_reg_kernel<2><<<grid, block, 0, stream>>>(Ap, m, n, bs, j0, kb, Vg.data_ptr<float>(),
+                                                           Vc.data_ptr<float>(), Tg.data_ptr<float>(),
+                                                           (int64_t)m * PB, (int64_t)m * KC);
+      else
+        qr_panel_reg_kernel<3><<<grid, block, 0, stream>>>(Ap, m, n, bs, j0, kb, Vg.data_ptr<float>(),
+                                                           Vc.data_ptr<float>(), Tg.data_ptr<float>(),
+                                                           (int64_t)m * PB, (int64_t)m * KC);
+      C10_CUDA_KERNEL_LAUNCH_CHECK();
+      note_launch();
+    } else {
     int nclus = 1;
     while ((rows + nclus - 1) / nclus > max_chunk && nclus < 8) nclus *= 2;
     const int chunk = (rows + nclus - 1) / nclus;
@@ -515,13 +862,22 @@ void qr_r_blocked(at::Tensor& A, at::Tensor& R) {
                                       Vg.data_ptr<float>(), Vc.data_ptr<float>(), Tg.data_ptr<float>(),
                                       (int64_t)m * PB, (int64_t)m * KC, nclus));
     note_launch();
+    }
     const int nt = n - j0 - kb;
     if (nt <= 0) continue;
-    qr_w_kernel<<<dim3((unsigned)((nt + QW_COLS - 1) / QW_COLS), (unsigned)b), QW_T, w_smem, stream>>>(
+    const int ntiles = (nt + QW_COLS - 1) / QW_COLS;
+    const int splits = std::max(1, std::min({splits_max, (2 * 148) / (ntiles * b) + 1, rows / 256}));
+    qr_w_kernel<<<dim3((unsigned)ntiles, (unsigned)b, (unsigned)splits), QW_T, w_smem, stream>>>(
         A.data_ptr<float>(), n, bs, j0, rows, nt, Vg.data_ptr<float>(), (int64_t)m * PB, Tg.data_ptr<float>(),
-        Wc.data_ptr<float>(), (int64_t)KC * n, n);
+        Wc.data_ptr<float>(), (int64_t)KC * n, n, splits, splits > 1 ? Wp.data_ptr<float>() : nullptr);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     note_launch();
+    if (splits > 1) {
+      qr_w_finish_kernel<<<dim3((unsigned)ntiles, (unsigned)b), QW_T, 0, stream>>>(
+          Wp.data_ptr<float>(), splits, nt, Tg.data_ptr<float>(), Wc.data_ptr<float>(), (int64_t)KC * n, n);
+      C10_CUDA_KERNEL_LAUNCH_CHECK();
+      note_launch();
+    }
     // A[j0:, j0+32:] -= [Vhi|Vhi|Vlo] [W'hi;W'lo;W'hi]   (tcgen05, in place)
     at::Tensor Vsub = Vc.narrow(1, 0, rows);
     at::Tensor Wsub = Wc.narrow(2, 0, nt);
@@ -546,6 +902,7 @@ void cholesky_blocked(at::Tensor& A, at::Tensor& info) {
   TORCH_CHECK(info.scalar_type() == at::kInt && info.numel() >= A.size(0) && info.is_cuda(),
               "dion_b200 cholesky_blocked: info must be an int32 CUDA tensor of b entries");
   const int b = (int)A.size(0), r = (int)A.size(1);
+  if (b == 0 || A.numel() == 0) return;  // nothing to do (e.g. a rank that holds no matrix of a batch)
   c10::cuda::CUDAGuard guard(A.device());
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   C10_CUDA_CHECK(cudaMemsetAsync(info.data_ptr<int>(), 0, sizeof(int) * (size_t)b, stream));

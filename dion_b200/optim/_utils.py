@@ -8,6 +8,8 @@ Behavioural parity notes (reference files):
 """
 from __future__ import annotations
 
+import contextlib
+
 import math
 from collections import OrderedDict
 from typing import Any, Callable, Dict, Generator, Iterable, Iterator, List, Optional, Sequence, Tuple, Union
@@ -169,3 +171,48 @@ def scalar_update(
         )
     else:
         raise ValueError(f"Unknown scalar algorithm: {algo}")
+
+
+class StreamPool:
+    """A few CUDA side streams on which independent units of optimizer work
+    (same-shape groups) run concurrently, so that one group's kernels fill
+    the SMs another group's tail leaves idle. ``session(device, n)`` returns
+    a context for one step: ``use(i)`` enters unit i's stream (which first
+    waits for the work already queued on the current stream), ``join()``
+    makes the current stream wait for every stream used. Inactive (one
+    unit, CPU tensors, or disabled): ``use`` is a no-op."""
+
+    def __init__(self, size: int, enabled: bool = True):
+        self.size = size
+        self.enabled = enabled
+        self._pools: Dict[Any, List[Any]] = {}
+
+    def session(self, device, units: int) -> "_StreamSession":
+        if not (self.enabled and units > 1 and getattr(device, "type", None) == "cuda"):
+            return _StreamSession(None, None)
+        pool = self._pools.get(device)
+        if pool is None:
+            pool = [torch.cuda.Stream(device=device) for _ in range(self.size)]
+            self._pools[device] = pool
+        return _StreamSession(pool, torch.cuda.current_stream(device))
+
+
+class _StreamSession:
+    def __init__(self, pool, main):
+        self.pool, self.main = pool, main
+        self.active = pool is not None
+        self._used: List[Any] = []
+
+    def use(self, i: int):
+        if not self.active:
+            return contextlib.nullcontext()
+        st = self.pool[i % len(self.pool)]
+        if st not in self._used:
+            st.wait_stream(self.main)
+            self._used.append(st)
+        return torch.cuda.stream(st)
+
+    def join(self) -> None:
+        for st in self._used:
+            self.main.wait_stream(st)
+        self._used = []

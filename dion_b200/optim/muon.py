@@ -21,7 +21,9 @@ B200 design:
 """
 from __future__ import annotations
 
+import contextlib
 import math
+import os
 from typing import Any, Callable, Dict, List, Optional, Sequence, Tuple, Union
 
 import torch
@@ -34,7 +36,7 @@ from torch.optim.optimizer import Optimizer, ParamsT
 
 from .. import ops
 from ..utils.trace import phase
-from ._utils import group_by_signature, scalar_update, to_local
+from ._utils import StreamPool, group_by_signature, scalar_update, to_local
 
 __all__ = ["Muon", "adjust_lr_spectral_norm", "adjust_lr_rms_norm", "adjust_lr_keller_muon"]
 
@@ -56,6 +58,8 @@ def adjust_lr_keller_muon(lr: float, shape: Sequence[int]) -> float:
     fan_out, fan_in = shape[-2:]
     return lr * math.sqrt(max(1.0, fan_out / fan_in))
 
+
+_NUM_SMS = 148  # B200
 
 _ADJUST = {
     "spectral_norm": adjust_lr_spectral_norm,
@@ -154,7 +158,11 @@ class Muon(Optimizer):
         self._distributed_mesh = distributed_mesh
         self._ns_func = newton_schulz_func
         self._p2p_cache: Dict[Tuple, Any] = {}
-        self._ddp_parity = 1  # buffer half of the last replicated Newton-Schulz call
+        self._ddp_parity: Dict[int, int] = {}  # heap uid -> buffer half of its last replicated Newton-Schulz call
+        # shape groups run concurrently on a pool of side streams (their GEMMs fill each other's tail SMs);
+        # each group then has its own peer-memory heap
+        self._streams = StreamPool(3, os.environ.get("DION_B200_SIDE_STREAMS", "1") != "0")
+        self._heap_tag = ""
         self._coeffs = _resolve_coeffs(ns_coeffs)
         self.fsdp_mesh_dim = fsdp_mesh_dim
         self._world_mesh = world_mesh
@@ -213,21 +221,44 @@ class Muon(Optimizer):
         eps = float(group["epsilon"])
         nesterov = bool(group["nesterov"])
         adjust = _ADJUST[group["adjust_lr"]]
-        for same in group_by_signature(params).values():
+        sigs = list(group_by_signature(params).values())
+        # Only groups whose Newton-Schulz GEMMs leave most SMs idle go to side streams: the GEMM is a
+        # persistent kernel with a static tile schedule, and two full-size ones sharing the SMs
+        # stretch each other's tails (measured: 48 x 4096^2 + 48 x 4096 x 14336 ran 19 % slower).
+        small = [self._ns_tiles(same) < 2 * _NUM_SMS for same in sigs]
+        streams = self._streams.session(to_local(sigs[0][0]).device, sum(small) + (1 if not all(small) else 0))
+        side = 0
+        for gi, same in enumerate(sigs):
             p0 = same[0]
             adj_lr = adjust(lr, p0.shape)
             states = [self._state(p, "muon") for p in same]
             shard_dim = self._shard_dim(p0)
             shape = "x".join(str(d) for d in p0.shape)
-            if shard_dim is not None and self._world > 1:
-                with phase(f"muon/fsdp/{shape}"):
-                    self._muon_fsdp(same, states, shard_dim, mu, nesterov, eps, decay, adj_lr, group)
-            elif self._world > 1 and self._pg is not None:
-                with phase(f"muon/ddp/{shape}"):
-                    self._muon_ddp(same, states, mu, nesterov, eps, decay, adj_lr, group)
-            else:
-                with phase(f"muon/local/{shape}"):
-                    self._muon_local(same, states, mu, nesterov, eps, decay, adj_lr, group)
+            self._heap_tag = f":{shape}" if streams.active else ""
+            if small[gi]:
+                side += 1
+            with streams.use(side) if small[gi] else contextlib.nullcontext():
+                if shard_dim is not None and self._world > 1:
+                    with phase(f"muon/fsdp/{shape}"):
+                        self._muon_fsdp(same, states, shard_dim, mu, nesterov, eps, decay, adj_lr, group)
+                elif self._world > 1 and self._pg is not None:
+                    with phase(f"muon/ddp/{shape}"):
+                        self._muon_ddp(same, states, mu, nesterov, eps, decay, adj_lr, group)
+                else:
+                    with phase(f"muon/local/{shape}"):
+                        self._muon_local(same, states, mu, nesterov, eps, decay, adj_lr, group)
+        streams.join()
+
+    def _ns_tiles(self, same: List[Tensor]) -> int:
+        """256 x 256 output tiles of one Newton-Schulz GEMM over the matrices
+        this rank orthogonalises for a same-shape group."""
+        shape = to_local(same[0]).shape
+        m, k = shape[0], int(math.prod(shape[1:]))
+        mats = len(same) if self._world <= 1 else -(-len(same) // self._world)
+        s_, l_ = min(m, k), max(m, k)
+        if isinstance(same[0], DTensor) and self._world > 1:
+            s_, l_ = min(same[0].shape[0], k), max(same[0].shape[0], k)
+        return mats * (-(-s_ // 256)) * (-(-l_ // 256))
 
     def _shard_dim(self, p: Tensor) -> Optional[int]:
         if not isinstance(p, DTensor):
@@ -401,8 +432,8 @@ class Muon(Optimizer):
 
         W, me = self._world, self._rank
         half = sets * W * m * k * 2
-        heap = heap_for(self._pg, 2 * half, "muon_ddp", mine.device)
-        self._ddp_parity = par = 1 - self._ddp_parity
+        heap = heap_for(self._pg, 2 * half, "muon_ddp" + self._heap_tag, mine.device)
+        par = self._ddp_parity[heap.uid] = 1 - self._ddp_parity.get(heap.uid, 1)
         base = par * half
         key = ("ddp", heap.uid, par, sets, m, k)
         order = [(me + 1 + i) % W for i in range(W)]
@@ -431,7 +462,7 @@ class Muon(Optimizer):
         ms = m // W
         mat = m * k * 2
         gather_off, ret_off = 0, sets * mat
-        heap = heap_for(self._pg, 2 * sets * mat, "muon", X[0].device)
+        heap = heap_for(self._pg, 2 * sets * mat, "muon" + self._heap_tag, X[0].device)
         key = (heap.uid, sets, m, k)
 
         def build():

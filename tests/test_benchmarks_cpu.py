@@ -161,3 +161,35 @@ def test_optimizer_bench_cli_cases(capsys):
     ob.main(["--optimizer", "dion2", "--impl", "reference"])
     line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert line["impl"] == "reference" and "unavailable" in line
+
+
+def test_report_from_run_outputs(tmp_path):
+    """The measured report is built from parity JSON, bench and optimizer-bench lines."""
+    import json
+
+    from dion_b200.benchmarks import report
+
+    par = tmp_path / "p.json"
+    par.write_text(json.dumps({"config": {"preset": "tiny", "optimizer": "dion"},
+                               "ours": {"losses": [3.0, 2.5, 2.0], "seconds": 1.0},
+                               "reference": {"losses": [3.0, 2.6, 2.1], "seconds": 2.0},
+                               "comparison": {"final_ours": 2.0, "final_ref": 2.1, "mean_abs_diff": 0.07,
+                                              "tail_rel_diff": 0.05}}))
+    bench = tmp_path / "b.log"
+    bench.write_text("noise\n" + json.dumps({"metric": "m", "value": 100.0, "n_gpus": 1, "impl": "ours",
+                                             "config": {"model": "llama3-1B", "optimizer": "muon+adamw"},
+                                             "e2e": {"value": 99.0}}) + "\n" +
+                     json.dumps({"metric": "m", "value": 80.0, "n_gpus": 1, "impl": "reference",
+                                 "config": {"model": "llama3-1B", "optimizer": "muon+adamw"}}) + "\n")
+    ob = tmp_path / "o.log"
+    ob.write_text(json.dumps({"metric": "optimizer_step_ms", "optimizer": "dion", "impl": "ours", "n_gpus": 2,
+                              "ms": 50.0, "p2p": True, "matrices": "m"}) + "\n")
+    data = report.collect([str(par)], [str(bench)], [str(ob)])
+    assert len(data["parity"]) == 1 and len(data["bench"]) == 2 and len(data["optimizer"]) == 1
+    out = report.render(data, str(tmp_path / "rep"))
+    text = open(out).read()
+    assert "tiny dion" in text and "| ours | 1 |" in text and "| dion | ours | 2 |" in text
+    assert (tmp_path / "rep" / "loss_0.svg").exists() and (tmp_path / "rep" / "throughput.svg").exists()
+    # regenerating from the saved data gives the same report
+    report.main(["--data", str(tmp_path / "rep" / "data.json"), "--out", str(tmp_path / "rep2")])
+    assert open(tmp_path / "rep2" / "report.md").read() == text
