@@ -45,6 +45,10 @@ void lion(const std::vector<at::Tensor>& X, const std::vector<at::Tensor>& G, co
 void rms_norm_fwd(const at::Tensor& x, const at::Tensor& w, at::Tensor& y, at::Tensor& rstd, double eps);
 void rms_norm_bwd(const at::Tensor& gy, const at::Tensor& x, const at::Tensor& w, const at::Tensor& rstd,
                   at::Tensor& gx, at::Tensor& gw);
+void add_rms_norm_fwd(const at::Tensor& x, const at::Tensor& a, const at::Tensor& w, at::Tensor& h, at::Tensor& y,
+                      at::Tensor& rstd, double eps);
+void rms_norm_bwd_res(const at::Tensor& gy, const at::Tensor& h, const at::Tensor& w, const at::Tensor& rstd,
+                      const at::Tensor& gres, at::Tensor& gx, at::Tensor& gw);
 void rope_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& tab, at::Tensor& qo, at::Tensor& ko,
               bool inverse);
 void swiglu_fwd(const at::Tensor& a, const at::Tensor& b, at::Tensor& o);
@@ -106,6 +110,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("lion", &bdion::lion);
   m.def("rms_norm_fwd", &bdion::rms_norm_fwd);
   m.def("rms_norm_bwd", &bdion::rms_norm_bwd);
+  m.def("add_rms_norm_fwd", &bdion::add_rms_norm_fwd, "h = x + a, y = rms_norm(h) * w (one pass)");
+  m.def("rms_norm_bwd_res", &bdion::rms_norm_bwd_res, "RMSNorm backward plus a residual gradient");
   m.def("rope_fwd", &bdion::rope_fwd);
   m.def("swiglu_fwd", &bdion::swiglu_fwd);
   m.def("swiglu_bwd", &bdion::swiglu_bwd);

@@ -220,6 +220,109 @@ __global__ void __launch_bounds__(128) rms_bwd_reg_kernel(const __nv_bfloat16* _
     gw_part[(int64_t)blockIdx.x * D + col] = red[col] + red[D + col] + red[2 * D + col] + red[3 * D + col];
 }
 
+// One CTA per group of rows, D / 8 threads: thread t owns columns
+// [8t, 8t + 8) of every row, so the weight and its share of the weight
+// gradient stay in 16 registers whatever D is (the warp-per-row variant above
+// keeps 4 x D / 32 values per lane and runs out of registers at D = 2048).
+// The row's dot product is one block reduction per row; the per-warp
+// partials are double-buffered so one barrier per row suffices.
+// gres (optional): a gradient added to gx in the same pass (the residual
+// branch of a fused add + norm).
+template <typename WT>
+__global__ void __launch_bounds__(1024) rms_bwd_row_kernel(const __nv_bfloat16* __restrict__ gy,
+                                                           const __nv_bfloat16* __restrict__ x,
+                                                           const WT* __restrict__ w, const float* __restrict__ rstd,
+                                                           __nv_bfloat16* __restrict__ gx,
+                                                           float* __restrict__ gw_part, int R, int D,
+                                                           int rows_per_block,
+                                                           const __nv_bfloat16* __restrict__ gres) {
+  __shared__ float wsum[2][32];
+  const int t = threadIdx.x, lane = t & 31, wid = t >> 5, nw = blockDim.x >> 5;
+  const int col = t * 8;
+  float wv[8], acc[8];
+  load8(w + col, wv);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  const int r0 = blockIdx.x * rows_per_block;
+  const int r1 = min(R, r0 + rows_per_block);
+  int buf = 0;
+  for (int row = r0; row < r1; ++row) {
+    float xv[8], gv[8];
+    load8(x + (int64_t)row * D + col, xv);
+    load8(gy + (int64_t)row * D + col, gv);
+    const float r = rstd[row];
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      dot += gv[i] * wv[i] * xv[i];
+      acc[i] += gv[i] * xv[i] * r;
+    }
+    dot = warp_sum(dot);
+    if (lane == 0) wsum[buf][wid] = dot;
+    __syncthreads();
+    float tot = 0.f;
+    for (int q = 0; q < nw; ++q) tot += wsum[buf][q];
+    buf ^= 1;
+    const float k = r * r * r * tot / D;
+    float o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = r * wv[i] * gv[i] - xv[i] * k;
+    if (gres != nullptr) {
+      float rv[8];
+      load8(gres + (int64_t)row * D + col, rv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] += rv[i];
+    }
+    store8(gx + (int64_t)row * D + col, o);
+  }
+  float* gp = gw_part + (int64_t)blockIdx.x * D + col;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) gp[i] = acc[i];
+}
+
+// h = x + a (rounded to bf16, as the unfused add) and y = h * rstd(h) * w,
+// one CTA of D / 8 threads per group of rows (thread t: columns [8t, 8t+8)).
+template <typename WT>
+__global__ void __launch_bounds__(1024) add_rms_fwd_row_kernel(const __nv_bfloat16* __restrict__ x,
+                                                               const __nv_bfloat16* __restrict__ a,
+                                                               const WT* __restrict__ w,
+                                                               __nv_bfloat16* __restrict__ h,
+                                                               __nv_bfloat16* __restrict__ y,
+                                                               float* __restrict__ rstd, int R, int D,
+                                                               int rows_per_block, float eps) {
+  __shared__ float wsum[2][32];
+  const int t = threadIdx.x, lane = t & 31, wid = t >> 5, nw = blockDim.x >> 5;
+  const int col = t * 8;
+  float wv[8];
+  load8(w + col, wv);
+  const int r0 = blockIdx.x * rows_per_block;
+  const int r1 = min(R, r0 + rows_per_block);
+  int buf = 0;
+  for (int row = r0; row < r1; ++row) {
+    float xv[8], av[8];
+    load8(x + (int64_t)row * D + col, xv);
+    load8(a + (int64_t)row * D + col, av);
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      xv[i] = __bfloat162float(__float2bfloat16_rn(xv[i] + av[i]));
+      ss += xv[i] * xv[i];
+    }
+    store8(h + (int64_t)row * D + col, xv);
+    ss = warp_sum(ss);
+    if (lane == 0) wsum[buf][wid] = ss;
+    __syncthreads();
+    float tot = 0.f;
+    for (int q = 0; q < nw; ++q) tot += wsum[buf][q];
+    buf ^= 1;
+    const float r = rsqrtf(tot / D + eps);
+    if (t == 0) rstd[row] = r;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) xv[i] = xv[i] * r * wv[i];
+    store8(y + (int64_t)row * D + col, xv);
+  }
+}
+
 // RoPE over 8 consecutive elements (4 interleaved pairs) per thread; one
 // table row (cos, sin per pair) per position.
 __global__ void rope8_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
@@ -254,6 +357,42 @@ __global__ void rope8_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfl
     x[2 * p + 1] = a * s + b * c;
   }
   store8(dst + v * 8, x);
+}
+
+// RoPE with one CTA per (batch, position): the position and its table row
+// are fixed for the CTA, so no thread divides a 64-bit index (the per-element
+// variant above spends more time on index division than on memory). Thread
+// t handles 8-element groups t, t + blockDim, ... of the position's q heads
+// then k heads.
+__global__ void __launch_bounds__(128) rope_pos_kernel(const __nv_bfloat16* __restrict__ q,
+                                                       const __nv_bfloat16* __restrict__ k,
+                                                       const float2* __restrict__ tab, __nv_bfloat16* __restrict__ qo,
+                                                       __nv_bfloat16* __restrict__ ko, int S, int hq, int hk, int half,
+                                                       float sign) {
+  const int bs = blockIdx.x;  // b * S + s
+  const int pos = bs % S;
+  const int per_head = half / 4;  // 8-element groups per head
+  const int nq = hq * per_head, nk = hk * per_head;
+  const float2* trow = tab + (int64_t)pos * half;
+  const int64_t qbase = (int64_t)bs * hq * half * 2, kbase = (int64_t)bs * hk * half * 2;
+  for (int g = threadIdx.x; g < nq + nk; g += blockDim.x) {
+    const bool isq = g < nq;
+    const int gg = isq ? g : g - nq;
+    const int j0 = (gg % per_head) * 4;
+    const __nv_bfloat16* src = (isq ? q + qbase : k + kbase) + (int64_t)gg * 8;
+    __nv_bfloat16* dst = (isq ? qo + qbase : ko + kbase) + (int64_t)gg * 8;
+    float x[8];
+    load8(src, x);
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const float2 cs = trow[j0 + p];
+      const float c = cs.x, sn = sign * cs.y;
+      const float a = x[2 * p], b = x[2 * p + 1];
+      x[2 * p] = a * c - b * sn;
+      x[2 * p + 1] = a * sn + b * c;
+    }
+    store8(dst, x);
+  }
 }
 
 // ------------------------------------------------------------ SwiGLU
@@ -423,6 +562,28 @@ void rms_norm_bwd(const at::Tensor& gy, const at::Tensor& x, const at::Tensor& w
   const int warps = 4;
   const size_t smem = (size_t)warps * D * sizeof(float);
   TORCH_CHECK(smem <= 200 * 1024, "dion_b200 rms_norm_bwd: D too large");
+  if (D % 256 == 0 && D >= 1024 && D <= 8192) {
+    // row-per-CTA variant: D / 8 threads, a few CTAs per SM
+    const int threads = D / 8;
+    const int per_sm = std::max(1, 2048 / threads);
+    const int nblk = std::min(R, sms * per_sm);
+    const int rpb = (R + nblk - 1) / nblk;
+    auto part = at::empty({nblk, D}, x.options().dtype(at::kFloat));
+    auto gyp = reinterpret_cast<const __nv_bfloat16*>(gy.data_ptr());
+    auto xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+    auto gxp = reinterpret_cast<__nv_bfloat16*>(gx.data_ptr());
+    if (w.scalar_type() == at::kFloat)
+      rms_bwd_row_kernel<float><<<nblk, threads, 0, s>>>(gyp, xp, w.data_ptr<float>(), rstd.data_ptr<float>(), gxp,
+                                                         part.data_ptr<float>(), R, D, rpb, nullptr);
+    else
+      rms_bwd_row_kernel<__nv_bfloat16><<<nblk, threads, 0, s>>>(
+          gyp, xp, reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), rstd.data_ptr<float>(), gxp,
+          part.data_ptr<float>(), R, D, rpb, nullptr);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    note_launch();
+    at::sum_out(gw, part, 0);
+    return;
+  }
   if (D % 256 == 0 && (D / 256 == 1 || D / 256 == 2 || D / 256 == 3 || D / 256 == 4 || D / 256 == 8 ||
                        D / 256 == 16)) {
     const int nblk_r = std::min((R + 3) / 4, sms * 4);
@@ -481,11 +642,97 @@ void rms_norm_bwd(const at::Tensor& gy, const at::Tensor& x, const at::Tensor& w
   at::sum_out(gw, part, 0);
 }
 
+static void check_row_op(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.dim() == 2 && t.is_contiguous() && t.scalar_type() == at::kBFloat16, "dion_b200 ", name,
+              ": contiguous [rows, D] bf16 expected");
+}
+
+// h = x + a, y = rms_norm(h) * w (D % 256 == 0, 1024 <= D <= 8192)
+void add_rms_norm_fwd(const at::Tensor& x, const at::Tensor& a, const at::Tensor& w, at::Tensor& h, at::Tensor& y,
+                      at::Tensor& rstd, double eps) {
+  check_row_op(x, "add_rms_norm");
+  check_row_op(a, "add_rms_norm");
+  const int R = (int)x.size(0), D = (int)x.size(1);
+  TORCH_CHECK(a.sizes() == x.sizes() && h.sizes() == x.sizes() && y.sizes() == x.sizes() && w.numel() == D &&
+                  D % 256 == 0 && D >= 1024 && D <= 8192,
+              "dion_b200 add_rms_norm: shapes (D a multiple of 256 in [1024, 8192])");
+  if (R == 0) return;
+  c10::cuda::CUDAGuard guard(x.device());
+  auto s = at::cuda::getCurrentCUDAStream();
+  int dev, sms;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int threads = D / 8;
+  const int nblk = std::min(R, sms * std::max(1, 2048 / threads));
+  const int rpb = (R + nblk - 1) / nblk;
+  auto xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  auto ap = reinterpret_cast<const __nv_bfloat16*>(a.data_ptr());
+  auto hp = reinterpret_cast<__nv_bfloat16*>(h.data_ptr());
+  auto yp = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
+  if (w.scalar_type() == at::kFloat)
+    add_rms_fwd_row_kernel<float><<<nblk, threads, 0, s>>>(xp, ap, w.data_ptr<float>(), hp, yp,
+                                                           rstd.data_ptr<float>(), R, D, rpb, (float)eps);
+  else
+    add_rms_fwd_row_kernel<__nv_bfloat16><<<nblk, threads, 0, s>>>(
+        xp, ap, reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), hp, yp, rstd.data_ptr<float>(), R, D, rpb,
+        (float)eps);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  note_launch();
+}
+
+// gx = gres + d/dh rms_norm(h) . gy ; gw = sum_rows gy * h * rstd
+void rms_norm_bwd_res(const at::Tensor& gy, const at::Tensor& h, const at::Tensor& w, const at::Tensor& rstd,
+                      const at::Tensor& gres, at::Tensor& gx, at::Tensor& gw) {
+  check_row_op(gy, "rms_norm_bwd_res");
+  check_row_op(h, "rms_norm_bwd_res");
+  check_row_op(gres, "rms_norm_bwd_res");
+  const int R = (int)h.size(0), D = (int)h.size(1);
+  TORCH_CHECK(D % 256 == 0 && D >= 1024 && D <= 8192 && gres.sizes() == h.sizes() && gy.sizes() == h.sizes(),
+              "dion_b200 rms_norm_bwd_res: shapes");
+  c10::cuda::CUDAGuard guard(h.device());
+  auto s = at::cuda::getCurrentCUDAStream();
+  if (R == 0) {
+    gw.zero_();
+    return;
+  }
+  int dev, sms;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int threads = D / 8;
+  const int nblk = std::min(R, sms * std::max(1, 2048 / threads));
+  const int rpb = (R + nblk - 1) / nblk;
+  auto part = at::empty({nblk, D}, h.options().dtype(at::kFloat));
+  auto gyp = reinterpret_cast<const __nv_bfloat16*>(gy.data_ptr());
+  auto hp = reinterpret_cast<const __nv_bfloat16*>(h.data_ptr());
+  auto rp = reinterpret_cast<const __nv_bfloat16*>(gres.data_ptr());
+  auto gxp = reinterpret_cast<__nv_bfloat16*>(gx.data_ptr());
+  if (w.scalar_type() == at::kFloat)
+    rms_bwd_row_kernel<float><<<nblk, threads, 0, s>>>(gyp, hp, w.data_ptr<float>(), rstd.data_ptr<float>(), gxp,
+                                                       part.data_ptr<float>(), R, D, rpb, rp);
+  else
+    rms_bwd_row_kernel<__nv_bfloat16><<<nblk, threads, 0, s>>>(
+        gyp, hp, reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), rstd.data_ptr<float>(), gxp,
+        part.data_ptr<float>(), R, D, rpb, rp);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  note_launch();
+  at::sum_out(gw, part, 0);
+}
+
 void rope_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& tab, at::Tensor& qo, at::Tensor& ko,
               bool inverse) {
   TORCH_CHECK(q.dim() == 4 && q.is_contiguous() && k.is_contiguous(), "dion_b200 rope: [b,s,h,d] contiguous");
   c10::cuda::CUDAGuard guard(q.device());
   const int S = (int)q.size(1), hq = (int)q.size(2), hk = (int)k.size(2), d = (int)q.size(3);
+  if (d % 8 == 0 && k.size(0) == q.size(0) && k.size(1) == S) {
+    const int64_t rows = q.size(0) * (int64_t)S;
+    rope_pos_kernel<<<(unsigned)rows, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(k.data_ptr()),
+        reinterpret_cast<const float2*>(tab.data_ptr<float>()), reinterpret_cast<__nv_bfloat16*>(qo.data_ptr()),
+        reinterpret_cast<__nv_bfloat16*>(ko.data_ptr()), S, hq, hk, d / 2, inverse ? -1.f : 1.f);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    note_launch();
+    return;
+  }
   if (d % 8 == 0) {
     const int64_t nq8 = q.numel() / 8, nk8 = k.numel() / 8;
     const int64_t grid8 = (nq8 + nk8 + 255) / 256;

@@ -37,6 +37,13 @@ class RMSNorm(nn.Module):
             return _fused.rms_norm(x, self.weight, self.eps)
         return F.rms_norm(x.float(), (x.shape[-1],), self.weight.float(), self.eps).to(x.dtype)
 
+    def add_forward(self, x: torch.Tensor, a: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+        """(x + a, norm(x + a)): the residual add fused into the norm where the kernel applies."""
+        if _fused.add_rms_enabled(x) and a.dtype == x.dtype and a.shape == x.shape:
+            return _fused.add_rms_norm(x, a, self.weight, self.eps)
+        h = x + a
+        return h, self(h)
+
     def reset_parameters(self):
         nn.init.ones_(self.weight)
 

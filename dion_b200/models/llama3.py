@@ -163,8 +163,8 @@ class TransformerBlock(nn.Module):
         self.weight_init_std = 0.02 / (2 * (layer_id + 1)) ** 0.5 if cfg.depth_init else 0.02 / (2 * cfg.n_layers) ** 0.5
 
     def _block(self, x: torch.Tensor, rope: torch.Tensor) -> torch.Tensor:
-        h = x + self.attention(self.attention_norm(x), rope)
-        return h + self.feed_forward(self.ffn_norm(h))
+        h, n = self.ffn_norm.add_forward(x, self.attention(self.attention_norm(x), rope))
+        return h + self.feed_forward(n)
 
     def forward(self, x: torch.Tensor, rope: torch.Tensor) -> torch.Tensor:
         if self.ac_mode == "none" or not torch.is_grad_enabled():

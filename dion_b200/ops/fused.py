@@ -15,6 +15,7 @@ import torch.nn.functional as F
 from ._ext import ext, has_ext
 
 _DISABLED = os.environ.get("DION_B200_FUSED", "1") == "0"
+_ADDNORM_DISABLED = os.environ.get("DION_B200_FUSED_ADDNORM", "1") == "0"
 
 
 def enabled(x: torch.Tensor) -> bool:
@@ -45,6 +46,47 @@ class _RMSNorm(torch.autograd.Function):
 
 def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     return _RMSNorm.apply(x, w, eps)
+
+
+class _AddRMSNorm(torch.autograd.Function):
+    """h = x + a and y = rms_norm(h) * w in one pass (the residual add of a
+    transformer block fused into the next norm); the backward adds the
+    residual gradient into the norm's input gradient in the same pass."""
+
+    @staticmethod
+    def forward(ctx, x, a, w, eps):
+        x2 = x.reshape(-1, x.shape[-1]).contiguous()
+        a2 = a.reshape(-1, a.shape[-1]).contiguous()
+        h = torch.empty_like(x2)
+        y = torch.empty_like(x2)
+        rstd = torch.empty(x2.shape[0], device=x.device, dtype=torch.float32)
+        ext().add_rms_norm_fwd(x2, a2, w, h, y, rstd, float(eps))
+        ctx.save_for_backward(h, w, rstd)
+        ctx.shape = x.shape
+        return h.view(x.shape), y.view(x.shape)
+
+    @staticmethod
+    def backward(ctx, gh, gy):
+        h, w, rstd = ctx.saved_tensors
+        gy2 = gy.reshape(-1, gy.shape[-1]).contiguous()
+        gh2 = gh.reshape(-1, gh.shape[-1]).contiguous()
+        gx = torch.empty_like(h)
+        gw = torch.empty(w.shape, device=w.device, dtype=torch.float32)
+        ext().rms_norm_bwd_res(gy2, h, w, rstd, gh2, gx, gw)
+        g = gx.view(ctx.shape)
+        return g, g, gw.to(w.dtype), None
+
+
+def add_rms_enabled(x: torch.Tensor) -> bool:
+    """Fused add + RMSNorm: bf16 rows of 1024-8192 (multiple of 256) features."""
+    d = x.shape[-1]
+    return (not _ADDNORM_DISABLED and enabled(x) and hasattr(ext(), "add_rms_norm_fwd") and d % 256 == 0
+            and 1024 <= d <= 8192)
+
+
+def add_rms_norm(x: torch.Tensor, a: torch.Tensor, w: torch.Tensor, eps: float):
+    """Returns (x + a, rms_norm(x + a) * w)."""
+    return _AddRMSNorm.apply(x, a, w, eps)
 
 
 # ---------------------------------------------------------------- RoPE

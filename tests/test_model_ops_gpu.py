@@ -9,27 +9,30 @@ from dion_b200.ops import fused
 pytestmark = pytest.mark.gpu
 
 
-def test_rmsnorm_fwd_bwd():
+@pytest.mark.parametrize("rows,dim", [(37, 512), (3001, 2048), (700, 4096)])
+def test_rmsnorm_fwd_bwd(rows, dim):
+    """dim >= 1024 takes the row-per-CTA backward kernel (several rows per CTA)."""
     torch.manual_seed(0)
-    x = torch.randn(37, 512, device="cuda", dtype=torch.bfloat16, requires_grad=True)
-    w = torch.randn(512, device="cuda", dtype=torch.float32, requires_grad=True)
+    x = torch.randn(rows, dim, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    w = torch.randn(dim, device="cuda", dtype=torch.float32, requires_grad=True)
     y = fused.rms_norm(x, w, 1e-5)
     g = torch.randn_like(y)
     y.backward(g)
     xr = x.detach().float().requires_grad_()
     wr = w.detach().clone().requires_grad_()
-    yr = F.rms_norm(xr, (512,), wr, 1e-5)
+    yr = F.rms_norm(xr, (dim,), wr, 1e-5)
     yr.backward(g.float())
     torch.testing.assert_close(y.float(), yr, rtol=2e-2, atol=2e-2)
     torch.testing.assert_close(x.grad.float(), xr.grad, rtol=3e-2, atol=3e-2)
-    torch.testing.assert_close(w.grad, wr.grad, rtol=1e-2, atol=1e-1)
+    torch.testing.assert_close(w.grad, wr.grad, rtol=1e-2, atol=1e-1 * (rows / 37) ** 0.5)
 
 
-def test_rope_roundtrip_and_ref():
+@pytest.mark.parametrize("b,s,hq,hk,d", [(2, 64, 8, 2, 64), (3, 257, 32, 8, 128)])
+def test_rope_roundtrip_and_ref(b, s, hq, hk, d):
     torch.manual_seed(0)
-    q = torch.randn(2, 64, 8, 64, device="cuda", dtype=torch.bfloat16)
-    k = torch.randn(2, 64, 2, 64, device="cuda", dtype=torch.bfloat16)
-    tab = L.rope_table(64, 128, 10000.0).cuda()
+    q = torch.randn(b, s, hq, d, device="cuda", dtype=torch.bfloat16)
+    k = torch.randn(b, s, hk, d, device="cuda", dtype=torch.bfloat16)
+    tab = L.rope_table(d, 2 * s, 10000.0).cuda()
     qo, ko = fused.rope(q, k, tab)
     torch.testing.assert_close(qo.float(), L._rope_ref(q, tab).float(), rtol=2e-2, atol=2e-2)
     torch.testing.assert_close(ko.float(), L._rope_ref(k, tab).float(), rtol=2e-2, atol=2e-2)
@@ -73,3 +76,28 @@ def test_linear_cross_entropy():
     assert abs(loss.item() - lf.item()) < 1e-2
     torch.testing.assert_close(h.grad.float(), hf.grad, rtol=5e-2, atol=5e-3)
     torch.testing.assert_close(W.grad.float(), Wf.grad, rtol=5e-2, atol=5e-3)
+
+
+@pytest.mark.parametrize("rows,dim", [(513, 2048), (64, 1024)])
+def test_add_rmsnorm_fused(rows, dim):
+    """(x + a, rms_norm(x + a) * w) and its backward (the residual gradient added
+    to the norm's input gradient) against PyTorch fp32."""
+    torch.manual_seed(1)
+    x = torch.randn(rows, dim, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    a = torch.randn(rows, dim, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    w = torch.randn(dim, device="cuda", dtype=torch.float32, requires_grad=True)
+    assert fused.add_rms_enabled(x)
+    h, y = fused.add_rms_norm(x, a, w, 1e-5)
+    gh, gy = torch.randn_like(h), torch.randn_like(y)
+    torch.autograd.backward([h, y], [gh, gy])
+    xr = x.detach().float().requires_grad_()
+    ar = a.detach().float().requires_grad_()
+    wr = w.detach().clone().requires_grad_()
+    hr = (xr + ar).to(torch.bfloat16).float()  # the unfused add rounds to bf16
+    yr = F.rms_norm(hr, (dim,), wr, 1e-5)
+    torch.autograd.backward([hr, yr], [gh.float(), gy.float()])
+    torch.testing.assert_close(h.float(), hr, rtol=0, atol=0)
+    torch.testing.assert_close(y.float(), yr, rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(x.grad.float(), xr.grad, rtol=3e-2, atol=3e-2)
+    torch.testing.assert_close(a.grad.float(), ar.grad, rtol=3e-2, atol=3e-2)
+    torch.testing.assert_close(w.grad, wr.grad, rtol=1e-2, atol=1e-1 * (rows / 37) ** 0.5)
