@@ -52,6 +52,9 @@ class TrainerConfig:
     use_fsdp: bool = True
     ac_mode: str = "none"  # none | full | selective
     ac_option: str = "op"
+    # with tp > 1: token-sharded activations between sublayers and the TP
+    # collectives fused into the GEMMs (parallel/sp.py); False: plain TP
+    sequence_parallel: bool = True
     optimizer: HybridOptimizersContainer.Config = field(default_factory=HybridOptimizersContainer.Config)
     log_freq: int = 10
 
@@ -161,7 +164,7 @@ class Trainer:
             if self.mesh is None or "tp" not in self.mesh.mesh_dim_names:
                 raise ValueError("tensor parallelism needs use_fsdp=True (the mesh is built there)")
             tp_mesh = self.mesh["tp"]
-            apply_tp(model, tp_mesh)
+            apply_tp(model, tp_mesh, sequence_parallel=cfg.sequence_parallel and cfg.pp == 1)
         if cfg.use_fsdp and self.dp_mesh is not None:
             # pipeline stages keep their parameters gathered across micro-batches
             # (and the last stage's LM head stays gathered for the loss)
@@ -202,6 +205,15 @@ class Trainer:
     def forward_backward(self, tokens: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
         loss = self.model.loss(tokens, labels)
         loss.backward()
+        sp = getattr(self.model, "sp", None)
+        if sp is not None:
+            # each TP rank back-propagated its own tokens: sum the shared parameters'
+            # gradients, and report the whole batch's loss
+            from ..parallel.tp import sp_sync_replicated_grads
+
+            sp_sync_replicated_grads(self.model, sp.group)
+            loss = loss.detach().clone()
+            torch.distributed.all_reduce(loss, group=sp.group)
         return loss
 
     def train_step(self, tokens: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:

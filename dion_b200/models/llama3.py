@@ -23,6 +23,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from . import layers as L
+from ..parallel.sp import sp_column_linears, sp_row_linear
 
 __all__ = ["Llama3Config", "Transformer", "LLAMA3_CONFIGS", "llama3_config"]
 
@@ -107,8 +108,19 @@ class Attention(nn.Module):
         self.wk = nn.Linear(cfg.dim, self.n_kv_heads * self.head_dim, bias=False)
         self.wv = nn.Linear(cfg.dim, self.n_kv_heads * self.head_dim, bias=False)
         self.wo = nn.Linear(cfg.n_heads * self.head_dim, cfg.dim, bias=False)
+        self.sp = None  # sequence-parallel TP group (parallel/sp.py), set by apply_tp
 
     def forward(self, x: torch.Tensor, rope: torch.Tensor) -> torch.Tensor:
+        if self.sp is not None:
+            # x: this rank's [N / T, D] token shard; q/k/v cover all tokens, this rank's heads
+            bs, seqlen = self.sp.batch_shape
+            q, k, v = sp_column_linears(self.sp, x, [self.wq.weight, self.wk.weight, self.wv.weight])
+            q = q.view(bs, seqlen, -1, self.head_dim)
+            k = k.view(bs, seqlen, -1, self.head_dim)
+            v = v.view(bs, seqlen, -1, self.head_dim)
+            q, k = L.apply_rope(q, k, rope)
+            o = L.causal_attention(q, k, v)
+            return sp_row_linear(self.sp, o.reshape(bs * seqlen, -1), self.wo.weight)
         bs, seqlen, _ = x.shape
         # -1 heads: under tensor parallelism each rank holds n_heads / tp of them
         q = self.wq(x).view(bs, seqlen, -1, self.head_dim)
@@ -125,8 +137,12 @@ class FeedForward(nn.Module):
         self.w1 = nn.Linear(dim, hidden, bias=False)
         self.w2 = nn.Linear(hidden, dim, bias=False)
         self.w3 = nn.Linear(dim, hidden, bias=False)
+        self.sp = None  # sequence-parallel TP group (parallel/sp.py), set by apply_tp
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.sp is not None:
+            a, b = sp_column_linears(self.sp, x, [self.w1.weight, self.w3.weight])
+            return sp_row_linear(self.sp, L.swiglu(a, b), self.w2.weight)
         return self.w2(L.swiglu(self.w1(x), self.w3(x)))
 
 
@@ -183,6 +199,7 @@ class Transformer(nn.Module):
         self.tok_embeddings = nn.Embedding(cfg.vocab_size, cfg.dim)
         self.layers = nn.ModuleDict({str(i): TransformerBlock(i, cfg) for i in range(cfg.n_layers)})
         self.norm = L.RMSNorm(cfg.dim, cfg.norm_eps)
+        self.sp = None  # sequence-parallel TP group (parallel/sp.py), set by apply_tp
         self.output = nn.Linear(cfg.dim, cfg.vocab_size, bias=False)
         self.register_buffer("rope_cache", L.rope_table(cfg.head_dim, cfg.max_seq_len, cfg.rope_theta), persistent=False)
 
@@ -241,12 +258,23 @@ class Transformer(nn.Module):
         chunk-wise without materialising fp32 logits. (The loss lives in
         ``forward`` so FSDP's root hooks unshard the LM head for it.)"""
         seqlen = tokens.shape[1]
-        h = self.tok_embeddings(tokens)
+        sp = self.sp
+        if sp is not None:
+            # sequence parallelism: this rank embeds and carries its shard of the flattened tokens
+            sp.batch_shape = (tokens.shape[0], seqlen)
+            h = self.tok_embeddings(sp.shard_rows(tokens.reshape(-1)))
+        else:
+            h = self.tok_embeddings(tokens)
         rope = self.rope_cache[:seqlen].float()
         for layer in self.layers.values():
             h = layer(h, rope)
         h = self.norm(h)
         if labels is not None:
+            if sp is not None:
+                # this rank's share of the mean loss over all N tokens (the TP
+                # ranks' shares sum to it; replicated-parameter gradients are
+                # summed over TP after backward)
+                return L.linear_cross_entropy(h, self.output.weight, sp.shard_rows(labels.reshape(-1))) / sp.T
             return L.linear_cross_entropy(h, self.output.weight, labels)
         if return_hidden:
             return h

@@ -63,16 +63,20 @@ def init_distributed(backend: Optional[str] = None, timeout_s: float = 300.0) ->
 
 def build_mesh(dims: ParallelDims, device_type: Optional[str] = None) -> Optional[DeviceMesh]:
     """Mesh with named dims ("dp_replicate", "dp_shard", "tp", "pp"), size-1 dims
-    dropped -- except ``dp_shard`` beside a replicate dim: replicas without
-    sharding are HSDP with a shard dim of 1 (FSDP2 then all-reduces the
-    gradients over the replicas and every replica holds whole matrices)."""
+    dropped -- except ``dp_shard`` beside a replicate or TP dim: replicas
+    without sharding are HSDP with a shard dim of 1 (FSDP2 then all-reduces
+    the gradients over the replicas and every replica holds whole matrices),
+    and TP without data parallelism still gets FSDP2's mixed precision."""
     world = dist.get_world_size() if dist.is_initialized() else 1
     d = dims.resolve(world)
     if device_type is None:
         device_type = "cuda" if torch.cuda.is_available() else "cpu"
     names, sizes = [], []
     for name, size in (("pp", d.pp), ("dp_replicate", d.dp_replicate), ("dp_shard", d.dp_shard), ("tp", d.tp)):
-        if size > 1 or (name == "dp_shard" and d.dp_replicate > 1):
+        # dp_shard stays (size 1) beside a replicate or TP dim: FSDP2 then still
+        # applies (mixed precision: bf16 compute, fp32 master weights) when every
+        # rank of a TP group holds the whole data-parallel shard
+        if size > 1 or (name == "dp_shard" and (d.dp_replicate > 1 or d.tp > 1)):
             names.append(name)
             sizes.append(size)
     if not names:

@@ -193,3 +193,17 @@ def test_report_from_run_outputs(tmp_path):
     # regenerating from the saved data gives the same report
     report.main(["--data", str(tmp_path / "rep" / "data.json"), "--out", str(tmp_path / "rep2")])
     assert open(tmp_path / "rep2" / "report.md").read() == text
+
+
+def test_step_trace_summary():
+    """Device time by owner and idle gaps from a chrome trace."""
+    from dion_b200.benchmarks.step_trace import summarize
+
+    ev = [{"cat": "kernel", "name": "nvjet_tst_256x256", "ts": 0, "dur": 100},
+          {"cat": "kernel", "name": "void bdion::gemm_tc2_kernel<...>", "ts": 150, "dur": 50},
+          {"cat": "kernel", "name": "cudnn_generated_fort_native_sdpa", "ts": 180, "dur": 40},
+          {"cat": "cpu_op", "name": "aten::mm", "ts": 0, "dur": 5}]
+    s = summarize({"traceEvents": ev})
+    assert s["kernels"] == 3
+    assert abs(s["span_ms"] - 0.22) < 1e-9 and abs(s["idle_ms"] - 0.05) < 1e-9
+    assert s["by_owner_ms"] == {"cuBLAS": 0.1, "dion_b200": 0.05, "cuDNN": 0.04}
