@@ -129,10 +129,6 @@ class AdaDionV2(Dion):
                 st.update({"r": init_r, "r_cap": r_cap, "transpose": cfg.is_transposed, "erank_ema": None,
                            "aerr_ema": None, "ada_step": 0})
 
-    def _arena(self, params, group, order, slots):
-        Mb, Qb = super()._arena(params, group, order, slots)
-        return Mb, Qb
-
     # ------------------------------------------------------------------ hooks
     def _active_q(self, params, order, Qb):
         if not self._adaptive_rank:

@@ -795,8 +795,13 @@ class Dion(Optimizer):
 
     # ---- FSDP x TP (inner-sharded) parameters
     def _dion_fsdp_tp(self, group: dict, params: List[Tensor], cfg: DionParamConfig) -> None:
-        """Inner-sharded update: P = M Q reduced over the outer mesh, orthogonalised
-        across the inner mesh with a distributed randomised Cholesky QR."""
+        """Inner-sharded update of one same-signature set, batched: P = M Q
+        reduced over the mesh dims that shard the contracted dimension (one
+        collective for the whole set), orthogonalised across the inner mesh
+        with a distributed randomised Cholesky QR, R = M^T P likewise; the
+        all-zero guard, error feedback, column norms and weight update run as
+        batched kernels on the local shards (adadion_v2.py:1298-1448 does the
+        same per matrix)."""
         from .linalg import distributed_orthogonalize
 
         for p in params:
@@ -805,51 +810,52 @@ class Dion(Optimizer):
         lr, mu = float(group["lr"]), float(group["mu"])
         wd, eps = float(group["weight_decay"]), float(group["epsilon"])
         rm = self._replicate_mesh
-        for p in params:
-            st = self.state[p]
-            G = p.grad
-            if self._replicate_mesh_grad_sync and not cfg.compressed_all_reduce and rm is not None:
-                G = DTensor.from_local(self._all_reduce_replicate([to_local(G)])[0], G.device_mesh, G.placements,
-                                       run_check=False, shape=G.shape, stride=G.stride())
-            M = st["momentum"]
-            M.add_(G.to(M.dtype))
-            Qd = st["Q"]
-            if cfg.Q_inner_unsharded_placements is not None:
-                Qd = Qd.redistribute(placements=cfg.Q_inner_unsharded_placements)
-            Mt = M.mT if cfg.is_transposed else M
-            P = (Mt @ Qd.to(M.dtype)).redistribute(
-                placements=[Replicate() if pl.is_partial() else pl for pl in (Mt @ Qd.to(M.dtype)).placements]
-            )
-            P = distributed_orthogonalize(P.unsqueeze(0) if P.ndim == 2 else P, float(group["oversample"]),
-                                          cfg.inner_shard_mesh_dim).squeeze(0)
-            R = Mt.mT @ P
-            R = R.redistribute(placements=[Replicate() if pl.is_partial() else pl for pl in R.placements])
-            Pl, Rl = to_local(P).float().unsqueeze(0), to_local(R).float().unsqueeze(0).contiguous()
-            Pl = Pl.contiguous()
-            # all-zero flag on the device (no host read per parameter)
-            nz = (to_local(M) != 0).any().to(torch.float32).view(1)
-            Q0 = to_local(Qd).float().unsqueeze(0).contiguous()
-            ops.dion_fixup_(Pl, Rl, Q0, nz)
-            Ml = to_local(M)
-            dt = self._op_dtype(Ml.dtype)
-            # M -= (1 - mu) P R^T (R P^T when transposed), in place on the tcgen05 GEMM
-            if cfg.is_transposed:
-                ops.matmul_update_([Ml], Rl.to(dt), Pl.to(dt).transpose(1, 2), gamma=1.0, delta=-(1.0 - mu))
-            else:
-                ops.matmul_update_([Ml], Pl.to(dt), Rl.to(dt).transpose(1, 2), gamma=1.0, delta=-(1.0 - mu))
-            sumsq = ops.col_sumsq(Rl)
-            if cfg.outer_shard_mesh_dim is not None:
-                dist.all_reduce(sumsq, group=R.device_mesh.get_group(cfg.outer_shard_mesh_dim))
-            Qn = torch.empty_like(Rl)
-            ops.col_normalize(Rl, sumsq, eps, Qn)
-            s_lr = self._scaled_lr(p.shape, lr)
-            Xl = to_local(p)
-            xdt = self._op_dtype(Xl.dtype)
-            # X = (1 - lr wd) X - s_lr P Q^T (Q P^T when transposed), in place
-            if cfg.is_transposed:
-                ops.matmul_update_([Xl], Qn.to(xdt), Pl.to(xdt).transpose(1, 2), gamma=1.0 - lr * wd, delta=-s_lr)
-            else:
-                ops.matmul_update_([Xl], Pl.to(xdt), Qn.to(xdt).transpose(1, 2), gamma=1.0 - lr * wd, delta=-s_lr)
-            Qfull = DTensor.from_local(Qn[0].to(to_local(Qd).dtype), Qd.device_mesh, Qd.placements, run_check=False,
-                                       shape=Qd.shape, stride=Qd.stride())
-            to_local(st["Q"]).copy_(to_local(Qfull.redistribute(placements=cfg.Q_sharded_placements)))
+        states = [self.state[p] for p in params]
+        Ms = [st["momentum"] for st in states]
+        G_loc = [to_local(p.grad) for p in params]
+        if self._replicate_mesh_grad_sync and not cfg.compressed_all_reduce and rm is not None:
+            G_loc = self._all_reduce_replicate(G_loc)
+        M_loc = [to_local(M) for M in Ms]
+        nz = ops.dion_momentum_add_(M_loc, G_loc)  # also: 1 per matrix whose momentum is not all zero
+        Qds = [st["Q"] for st in states]
+        if cfg.Q_inner_unsharded_placements is not None:
+            Qds = [Qd.redistribute(placements=cfg.Q_inner_unsharded_placements) for Qd in Qds]
+        Mb = torch.stack([M.mT if cfg.is_transposed else M for M in Ms])  # [n, d, k] DTensor
+        Qb = torch.stack(Qds).to(Mb.dtype)
+        P = Mb @ Qb
+        P = P.redistribute(placements=[Replicate() if pl.is_partial() else pl for pl in P.placements])
+        P = distributed_orthogonalize(P, float(group["oversample"]), cfg.inner_shard_mesh_dim)
+        R = Mb.mT @ P
+        R = R.redistribute(placements=[Replicate() if pl.is_partial() else pl for pl in R.placements])
+        Pl = to_local(P).float().contiguous()
+        Rl = to_local(R).float().contiguous()
+        Q0 = to_local(torch.stack(Qds)).float().contiguous()
+        ops.dion_fixup_(Pl, Rl, Q0, nz.to(Pl.device))
+        dt = self._op_dtype(M_loc[0].dtype)
+        # M -= (1 - mu) P R^T (R P^T when transposed), in place on the tcgen05 GEMM, one launch
+        if cfg.is_transposed:
+            ops.matmul_update_(M_loc, Rl.to(dt), Pl.to(dt).transpose(1, 2), gamma=1.0, delta=-(1.0 - mu))
+        else:
+            ops.matmul_update_(M_loc, Pl.to(dt), Rl.to(dt).transpose(1, 2), gamma=1.0, delta=-(1.0 - mu))
+        sumsq = ops.col_sumsq(Rl)
+        if cfg.outer_shard_mesh_dim is not None:
+            dist.all_reduce(sumsq, group=R.device_mesh.get_group(cfg.outer_shard_mesh_dim))
+        Qn = torch.empty_like(Rl)
+        ops.col_normalize(Rl, sumsq, eps, Qn)
+        s_lr = self._scaled_lr(params[0].shape, lr)
+        X_loc = [to_local(p) for p in params]
+        xdt = self._op_dtype(X_loc[0].dtype)
+        # X = (1 - lr wd) X - s_lr P Q^T (Q P^T when transposed), in place
+        if cfg.is_transposed:
+            ops.matmul_update_(X_loc, Qn.to(xdt), Pl.to(xdt).transpose(1, 2), gamma=1.0 - lr * wd, delta=-s_lr)
+        else:
+            ops.matmul_update_(X_loc, Pl.to(xdt), Qn.to(xdt).transpose(1, 2), gamma=1.0 - lr * wd, delta=-s_lr)
+        Qs = Qds[0]
+        stacked = [Shard(pl.dim + 1) if pl.is_shard() else pl for pl in Qs.placements]
+        target = [Shard(pl.dim + 1) if pl.is_shard() else pl for pl in cfg.Q_sharded_placements]
+        Qfull = DTensor.from_local(Qn.to(to_local(Qs).dtype), Qs.device_mesh, stacked, run_check=False,
+                                   shape=(len(params),) + tuple(Qs.shape),
+                                   stride=(Qs.numel(),) + tuple(Qs.stride()))
+        Qnew = to_local(Qfull.redistribute(placements=target))
+        for st, q in zip(states, Qnew.unbind(0)):
+            to_local(st["Q"]).copy_(q)
