@@ -53,6 +53,9 @@ def parse(argv=None):
     p.add_argument("--rank-fraction", type=float, default=0.25)
     p.add_argument("--replicated", action="store_true",
                    help="plain replicated tensors (DDP layout) instead of Shard(0) DTensors")
+    p.add_argument("--trace", default=None,
+                   help="after timing, profile one more step and write rank 0's kernel timeline (.json.gz)"
+                        " plus a device-time summary line")
     return p.parse_args(argv)
 
 
@@ -159,6 +162,27 @@ def main(argv=None):
             "p2p": os.environ.get("DION_B200_P2P", "1") != "0",
             "rank_fraction": args.rank_fraction if args.optimizer != "muon" else None,
         }))
+    if args.trace:
+        from torch.profiler import ProfilerActivity, profile
+
+        from .step_trace import summarize
+
+        dist.barrier()
+        with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
+            opt.step()
+            torch.cuda.synchronize()
+        if rank == 0:
+            import gzip
+            import tempfile
+
+            with tempfile.TemporaryDirectory() as d:
+                path = os.path.join(d, "t.json")
+                prof.export_chrome_trace(path)
+                with open(path) as f:
+                    trace = json.load(f)
+            with gzip.open(args.trace, "wt") as f:
+                json.dump(trace, f)
+            print(json.dumps({"trace_summary": summarize(trace, top=15)}))
     dist.barrier()
     dist.destroy_process_group()
 

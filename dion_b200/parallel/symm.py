@@ -70,7 +70,16 @@ class SymmetricHeap:
         self._flag_off = 0
         self.data_off = _round(E.symm_flag_bytes())
         self.nbytes = _round(nbytes)
-        ptr, handle = E.symm_create(self.data_off + self.nbytes + _GUARD)
+        try:
+            ptr, handle = E.symm_create(self.data_off + self.nbytes + _GUARD)
+        except RuntimeError as e:
+            # the region is allocated outside PyTorch's caching allocator: give back
+            # the allocator's cached, unused blocks (activations of the step that just
+            # ran) and try once more
+            if "out of memory" not in str(e).lower():
+                raise
+            torch.cuda.empty_cache()
+            ptr, handle = E.symm_create(self.data_off + self.nbytes + _GUARD)
         hd = handle.to(self.device)
         allh = torch.empty(self.world * hd.numel(), dtype=torch.uint8, device=self.device)
         dist.all_gather_into_tensor(allh, hd, group=group)
