@@ -400,7 +400,10 @@ def scaled_update_(X: List[Tensor], U: List[Tensor], decay: float, lrs: Sequence
             x.copy_((decay * x.float() - lr * u.float()).to(x.dtype))
         return
     if not isinstance(lrs, Tensor):
-        lrs = torch.tensor([float(v) for v in lrs], dtype=torch.float32).to(X[0].device, non_blocking=True)
+        # staged through pinned memory: an asynchronous copy (a pageable one
+        # would make the host wait for the stream's queued work)
+        lrs = torch.tensor([float(v) for v in lrs], dtype=torch.float32).pin_memory().to(X[0].device,
+                                                                                         non_blocking=True)
     ext().scaled_update(X, [u.contiguous() for u in U], float(decay), lrs.float())
 
 

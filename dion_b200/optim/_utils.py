@@ -216,3 +216,25 @@ class _StreamSession:
         for st in self._used:
             self.main.wait_stream(st)
         self._used = []
+
+
+_DEV_LISTS: Dict[Any, Tensor] = {}
+
+
+def device_list(values: Sequence, dtype: torch.dtype, device) -> Tensor:
+    """A small Python list as a device tensor, cached by value and copied
+    from pinned memory: a pageable host-to-device copy blocks the host until
+    the current stream drains, which keeps work queued on other streams from
+    overlapping it."""
+    key = (str(device), dtype, tuple(values))
+    t = _DEV_LISTS.get(key)
+    if t is None:
+        if len(_DEV_LISTS) > 1024:
+            _DEV_LISTS.clear()
+        t = torch.tensor(list(values), dtype=dtype)
+        if getattr(device, "type", str(device)) == "cuda" or str(device).startswith("cuda"):
+            t = t.pin_memory().to(device, non_blocking=True)  # asynchronous: pinned source
+        else:
+            t = t.to(device)
+        _DEV_LISTS[key] = t
+    return t

@@ -32,7 +32,7 @@ from torch.distributed import ProcessGroup
 from torch.distributed.device_mesh import DeviceMesh
 
 from .. import ops
-from ._utils import to_local
+from ._utils import device_list, to_local
 from .dion import Dion, DionMixedPrecisionConfig
 from .linalg import orthogonalize
 
@@ -141,7 +141,7 @@ class AdaDionV2(Dion):
         r_max = min(width, ((max(ranks) + 7) // 8) * 8)
         Qw = Qb[:, :, :r_max]
         mask = (torch.arange(r_max, device=Qb.device).unsqueeze(0)
-                < torch.tensor(ranks, device=Qb.device).unsqueeze(1)).to(Qb.dtype)
+                < device_list(ranks, torch.int64, Qb.device).unsqueeze(1)).to(Qb.dtype)
         Qw.mul_(mask.unsqueeze(1))
         return Qw, ranks
 
@@ -154,7 +154,7 @@ class AdaDionV2(Dion):
             if r > 0:
                 by_rank.setdefault(int(r), []).append(i)
         for r, idx in by_rank.items():
-            it = torch.tensor(idx, device=P.device)
+            it = device_list(idx, torch.int64, P.device)
             sub = P.index_select(0, it)[:, :, :r].contiguous()
             out[it, :, :r] = orthogonalize(sub, float(group["oversample"]))
         return out
@@ -163,10 +163,8 @@ class AdaDionV2(Dion):
         if ranks is None:
             return
         c = self._ada_config
-        slots = torch.tensor([order[i] for i in range(len(params))], dtype=torch.int64).to(sumsq.device,
-                                                                                            non_blocking=True)
-        rs = torch.tensor([ranks[order[i]] for i in range(len(params))], dtype=torch.int32).to(sumsq.device,
-                                                                                               non_blocking=True)
+        slots = device_list([order[i] for i in range(len(params))], torch.int64, sumsq.device)
+        rs = device_list([ranks[order[i]] for i in range(len(params))], torch.int32, sumsq.device)
         # entropy effective rank of the active column norms (one kernel), one
         # device->host copy per shape group for the host-side rank schedule
         eranks = ops.effective_rank(sumsq, slots, rs).cpu().tolist()

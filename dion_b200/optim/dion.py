@@ -46,7 +46,7 @@ from torch.distributed.tensor import DTensor, Partial, Placement, Replicate, Sha
 from torch.optim.optimizer import Optimizer, ParamsT
 
 from .. import ops
-from ._utils import AsyncRuntime, AsyncTask, group_by_signature, scalar_update, to_local
+from ._utils import AsyncRuntime, AsyncTask, device_list, group_by_signature, scalar_update, to_local
 from ..utils.trace import phase
 from .linalg import orthogonalize
 
@@ -566,7 +566,7 @@ class Dion(Optimizer):
         # X = (1 - lr*wd) X - sqrt(fan_out/fan_in) lr * P Q^T   (Q P^T when transposed)
         X = to_local(params)
         xdt = self._op_dtype(X[0].dtype)
-        idx = torch.tensor(order, device=Mb.device)
+        idx = device_list(order, torch.int64, Mb.device)
         Qn = Qb.index_select(0, idx).to(xdt)
         Px = P.index_select(0, idx).to(xdt)
         s_lr = self._scaled_lr(params[0].shape, lr)
@@ -663,7 +663,7 @@ class Dion(Optimizer):
         with phase(name):
             nz_p = ops.dion_momentum_add_([Mb[o] for o in order], G)
             nz = torch.zeros(sets * W, device=Mb.device, dtype=torch.float32)
-            nz[torch.tensor(order, device=Mb.device)] = nz_p
+            nz[device_list(order, torch.int64, Mb.device)] = nz_p
         t = cfg.is_transposed
         me = mesh.get_local_rank()
         my_ranks = None if ranks is None else ranks[me * sets:(me + 1) * sets]
