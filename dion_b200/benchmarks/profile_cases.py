@@ -66,6 +66,13 @@ def newton_schulz():
 
 
 @case
+def newton_schulz_2048():
+    """The 1B model's 2048 x 2048 group: 32 matrices (short K: the shape that runs furthest below peak)."""
+    U = torch.randn(32, 2048, 2048, device="cuda", dtype=torch.bfloat16)
+    return lambda: ops.newton_schulz(U, ops.KELLER_NS_COEFFS)
+
+
+@case
 def qr_r():
     A = torch.randn(8, 1280, 1024, device="cuda")
     return lambda: LA.qr_r(A)
