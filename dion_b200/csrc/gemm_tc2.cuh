@@ -362,6 +362,7 @@ __global__ void __launch_bounds__(192, 1)
               for (int j = 0; j < 8; ++j) v[i + j] += beta * cv[j];
             }
           } else {
+#pragma unroll
             for (int i = 0; i < 32; ++i)
               if (col0 + i < args.N) v[i] += beta * to_f<CT>(crow[i]);
           }
@@ -378,12 +379,14 @@ __global__ void __launch_bounds__(192, 1)
               store8(drow + i, pv);
             }
           } else {
+#pragma unroll
             for (int i = 0; i < 32; ++i)
               if (col0 + i < args.N) drow[i] = from_f<OutT>(args.gamma * to_f<OutT>(drow[i]) + args.delta * v[i]);
           }
         } else if (!args.sym) {
           for (int rep = 0; rep < args.nrep; ++rep) {
             if (rep > 0) drow = reinterpret_cast<OutT*>(dps[rep]) + (int64_t)lrow * args.ldd + col0;
+#pragma unroll
             for (int i = 0; i < 32; ++i)
               if (col0 + i < args.N) drow[i] = from_f<OutT>(v[i]);
           }
@@ -391,9 +394,10 @@ __global__ void __launch_bounds__(192, 1)
           if (col0 > row && full) {
 #pragma unroll
             for (int i = 0; i < 32; i += 8) store8(drow + i, v + i);
-#pragma unroll 4
+#pragma unroll
             for (int i = 0; i < 32; ++i) Db[(int64_t)(col0 + i) * args.ldd + row] = from_f<OutT>(v[i]);
           } else if (col0 + 31 >= row) {
+#pragma unroll
             for (int i = 0; i < 32; ++i) {
               const int j = col0 + i;
               if (j >= args.N || j < row) continue;
