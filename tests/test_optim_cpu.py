@@ -154,3 +154,36 @@ def test_philox_known_answers_and_statistics():
     assert not torch.equal(x, philox_normal((200, 500), 123, 10, 1.0, "cpu"))
     # element i does not depend on the requested size
     assert torch.equal(philox_normal((7,), 5, 1, 2.0, "cpu"), philox_normal((10,), 5, 1, 2.0, "cpu")[:7])
+
+
+def test_stream_pool_is_inactive_without_cuda_or_with_one_unit():
+    """Side streams only for several units on a CUDA device; otherwise use() is a no-op."""
+    from dion_b200.optim._utils import StreamPool
+
+    pool = StreamPool(3)
+    for dev, units in ((torch.device("cpu"), 4), (torch.device("cpu"), 1)):
+        s = pool.session(dev, units)
+        assert not s.active
+        with s.use(0):
+            pass
+        s.join()
+    assert not StreamPool(3, enabled=False).session(torch.device("cuda", 0), 4).active
+
+
+def test_device_list_is_cached_by_value():
+    from dion_b200.optim._utils import device_list
+
+    a = device_list([3, 1, 2], torch.int64, torch.device("cpu"))
+    b = device_list([3, 1, 2], torch.int64, torch.device("cpu"))
+    c = device_list([3, 1, 4], torch.int64, torch.device("cpu"))
+    assert a is b and a.tolist() == [3, 1, 2] and c.tolist() == [3, 1, 4]
+    assert device_list((1, 2), torch.int32, "cpu").dtype == torch.int32
+
+
+def test_muon_side_stream_size_classes():
+    """Groups whose Newton-Schulz GEMMs fill the GPU stay on the main stream."""
+    params = [torch.nn.Parameter(torch.zeros(512, 2048)) for _ in range(4)]
+    opt = Muon(params, lr=0.02)
+    assert opt._ns_tiles(params) == 4 * 2 * 8  # 4 matrices x (512/256) x (2048/256) tiles
+    big = [torch.nn.Parameter(torch.zeros(4096, 4096)) for _ in range(8)]
+    assert opt._ns_tiles(big) == 8 * 16 * 16
