@@ -37,14 +37,22 @@ _OPT = re.compile(r"(?:Optimizer:\s*|--config\s+\S*?_)(adamw|muon|dion2|dion|ada
 
 
 def parse_log_text(text: str, name: Optional[str] = None) -> dict:
-    """{"optimizer", "step", "loss", ..., "time_s"} lists (one entry per logged step)."""
+    """{"optimizer", "step", "loss", ..., "time_s"} lists (one entry per logged
+    step), plus "val_step" / "val_loss" from validation lines."""
     m = _OPT.search(text)
     out: Dict[str, list] = {k: [] for k in _FIELDS}
     out["time_s"] = []
+    out["val_step"], out["val_loss"] = [], []
     seen = set()
     t0 = None
     for line in text.splitlines():
         if "step:" not in line or "loss:" not in line:
+            continue
+        if "validate" in line:  # validation pass: "validate step: N  loss: X"
+            vm, lm = _FIELDS["step"][0].search(line), _FIELDS["loss"][0].search(line)
+            if vm and lm and int(vm.group(1)) not in out["val_step"]:
+                out["val_step"].append(int(vm.group(1)))
+                out["val_loss"].append(float(lm.group(1)))
             continue
         sm = _FIELDS["step"][0].search(line)
         if not sm:

@@ -30,40 +30,55 @@ def _sync_for_checkpoint(optimizers) -> None:
             fn()
 
 
-def save(folder: str, model, optimizers, step: int, model_only: bool = False) -> str:
+def save(folder: str, model, optimizers, step: int, model_only: bool = False, data=None) -> str:
     """Write a DCP checkpoint. Full checkpoints go to ``step-<N>``; a
     model-only save goes to ``step-<N>-model``, a name that resuming never
-    picks (it holds no optimizer state to resume from)."""
+    picks (it holds no optimizer state to resume from). ``data``: a loader
+    with ``state_dict()`` (the global samples consumed), stored beside the
+    step so a resumed job continues at the same sample."""
     path = os.path.join(folder, f"step-{step}-model" if model_only else f"step-{step}")
     _sync_for_checkpoint(optimizers)
     sd: Dict[str, Any] = {"model": get_model_state_dict(model)}
     if not model_only:
         sd["optimizer"] = optimizers.state_dict()
         sd["train_state"] = {"step": torch.tensor(step)}
+        if data is not None and hasattr(data, "state_dict"):
+            sd["train_state"]["data_samples"] = torch.tensor(int(data.state_dict()["samples"]))
     dcp.save(sd, checkpoint_id=path)
     return path
+
+
+def _metadata_keys(path: str):
+    return dcp.FileSystemReader(path).read_metadata().state_dict_metadata.keys()
 
 
 def _has_optimizer_state(path: str) -> bool:
     """Whether the checkpoint at ``path`` holds optimizer entries (a
     model-only save does not); read from the DCP metadata only."""
-    md = dcp.FileSystemReader(path).read_metadata()
-    return any(k.startswith("optimizer.") for k in md.state_dict_metadata)
+    return any(k.startswith("optimizer.") for k in _metadata_keys(path))
 
 
-def load(path: str, model, optimizers=None) -> int:
-    """Load model (and, when the checkpoint has them, optimizer and step)
-    state; returns the saved step, 0 for a model-only checkpoint. Errors in
-    loading the optimizer state are raised, never skipped."""
+def load(path: str, model, optimizers=None, data=None) -> int:
+    """Load model (and, when the checkpoint has them, optimizer, step and
+    data position) state; returns the saved step, 0 for a model-only
+    checkpoint. Errors in loading the optimizer state are raised, never
+    skipped. ``data``: a loader with ``load_state_dict``; checkpoints written
+    without a data position leave it where it is."""
     sd: Dict[str, Any] = {"model": get_model_state_dict(model)}
-    has_opt = optimizers is not None and _has_optimizer_state(path)
+    keys = set(_metadata_keys(path))
+    has_opt = optimizers is not None and any(k.startswith("optimizer.") for k in keys)
+    has_data = has_opt and data is not None and "train_state.data_samples" in keys
     if has_opt:
         sd["optimizer"] = optimizers.state_dict()
         sd["train_state"] = {"step": torch.tensor(0)}
+        if has_data:
+            sd["train_state"]["data_samples"] = torch.tensor(0)
     dcp.load(sd, checkpoint_id=path)
     set_model_state_dict(model, sd["model"])
     if has_opt:
         optimizers.load_state_dict(sd["optimizer"])
+        if has_data:
+            data.load_state_dict({"samples": int(sd["train_state"]["data_samples"])})
         return int(sd["train_state"]["step"])
     return 0
 
@@ -87,7 +102,7 @@ class CheckpointManager:
     def maybe_load(self, trainer) -> None:
         p = self.latest()
         if p is not None:
-            trainer.step_idx = load(p, self.model, self.optimizers)
+            trainer.step_idx = load(p, self.model, self.optimizers, data=getattr(trainer, "data", None))
 
     def maybe_save(self, trainer, step: int, final: bool = False) -> Optional[str]:
         """Full checkpoint every ``interval`` steps (the final step included);
@@ -95,11 +110,12 @@ class CheckpointManager:
         ``model_only_last``, or a full checkpoint when that step is off the
         interval and ``model_only_last`` is False."""
         path = None
+        data = getattr(trainer, "data", None)
         if self.interval > 0 and step % self.interval == 0:
-            path = save(self.folder, self.model, self.optimizers, step)
+            path = save(self.folder, self.model, self.optimizers, step, data=data)
         if final:
             if self.model_only_last:
                 path = save(self.folder, self.model, self.optimizers, step, model_only=True)
             elif path is None:
-                path = save(self.folder, self.model, self.optimizers, step)
+                path = save(self.folder, self.model, self.optimizers, step, data=data)
         return path

@@ -94,8 +94,13 @@ class MetricsConfig:
 
 @dataclass
 class DataConfig:
+    # "synthetic" or token files: comma-separated files, directories of *.bin or
+    # glob patterns (written by `python -m dion_b200.data.tokenize`)
     dataset: str = "synthetic"
     seed: int = 0
+    shuffle: bool = True
+    prefetch: int = 4
+    bytes_per_token: int = 0  # raw token files without a header: 2 or 4
 
 
 @dataclass
@@ -103,6 +108,7 @@ class ValidatorConfig:
     enable: bool = False
     freq: int = 100
     steps: int = 20
+    dataset: str = ""  # held-out token files (same forms as dataloader.dataset)
 
 
 @dataclass

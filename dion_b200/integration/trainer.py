@@ -3,7 +3,9 @@
 One process per GPU; FSDP2/HSDP over the data-parallel mesh; the hybrid
 optimizer container; warmup + cosine LR schedule with a floor (as in
 ada_dion/integration/config_registry.py:161-184: warmup 200, cosine decay
-to 10 %, grad-norm clip 1.0); synthetic uniform tokens.
+to 10 %, grad-norm clip 1.0); synthetic uniform tokens or token files read
+by the native loader (:mod:`dion_b200.data`), with an optional validation
+pass over held-out token files.
 
 ``train_step`` is the public per-step API: it takes the step's host batch
 (pinned int64 tokens / labels), copies it to the device, runs forward,
@@ -12,15 +14,15 @@ backward, clipping and the optimizer, and returns the loss tensor.
 from __future__ import annotations
 
 import math
-import os
 import time
 from dataclasses import dataclass, field
-from typing import Any, Dict, Iterator, List, Optional, Tuple
+from typing import Any, Dict, List, Optional
 
 import torch
 import torch.distributed as dist
 import torch.nn as nn
 
+from ..data import SyntheticTokens, TokenFileLoader, build_loader
 from ..models.llama3 import Llama3Config, Transformer, llama3_config
 from ..parallel.fsdp import apply_fsdp
 from ..parallel.tp import apply_tp
@@ -57,6 +59,13 @@ class TrainerConfig:
     sequence_parallel: bool = True
     optimizer: HybridOptimizersContainer.Config = field(default_factory=HybridOptimizersContainer.Config)
     log_freq: int = 10
+    # "synthetic", or token files (comma-separated files, directories of *.bin, globs)
+    dataset: str = "synthetic"
+    data_shuffle: bool = True
+    data_prefetch: int = 4
+    data_bytes_per_token: int = 0  # raw token files only (files with a header carry it)
+    # held-out token files for ``validate`` ("" = none)
+    val_dataset: str = ""
 
 
 def lr_lambda(step: int, warmup: int, total: int, min_factor: float) -> float:
@@ -67,28 +76,6 @@ def lr_lambda(step: int, warmup: int, total: int, min_factor: float) -> float:
         return 1.0
     prog = min(1.0, (step - warmup) / max(1, total - warmup))
     return min_factor + (1 - min_factor) * 0.5 * (1 + math.cos(math.pi * prog))
-
-
-class SyntheticTokens:
-    """Uniform random tokens over the vocabulary from a fixed seed, produced
-    on the host in pinned memory (one [global_batch, seq+1] draw per step;
-    each rank keeps its slice)."""
-
-    def __init__(self, vocab: int, seq_len: int, local_batch: int, seed: int, rank: int = 0, world: int = 1):
-        self.vocab, self.seq, self.lb = vocab, seq_len, local_batch
-        self.rank, self.world = rank, world
-        self.gen = torch.Generator().manual_seed(seed)
-
-    def next(self) -> Tuple[torch.Tensor, torch.Tensor]:
-        full = torch.randint(0, self.vocab, (self.lb * self.world, self.seq + 1), generator=self.gen)
-        mine = full[self.rank * self.lb : (self.rank + 1) * self.lb]
-        t = mine[:, :-1].contiguous().pin_memory() if torch.cuda.is_available() else mine[:, :-1].contiguous()
-        l = mine[:, 1:].contiguous().pin_memory() if torch.cuda.is_available() else mine[:, 1:].contiguous()
-        return t, l
-
-    def __iter__(self) -> Iterator[Tuple[torch.Tensor, torch.Tensor]]:
-        while True:
-            yield self.next()
 
 
 def clip_grad_norm_multi_mesh_(params: List[torch.nn.Parameter], max_norm: float,
@@ -183,8 +170,16 @@ class Trainer:
         # and of one pipeline share a batch
         tp, pp = max(1, cfg.tp), max(1, cfg.pp)
         per_stage = self.world // pp
-        self.data = SyntheticTokens(mcfg.vocab_size, cfg.seq_len, cfg.local_batch_size, cfg.seed,
-                                    (self.rank % per_stage) // tp, per_stage // tp)
+        self.data_rank, self.data_world = (self.rank % per_stage) // tp, per_stage // tp
+        self.data = build_loader(cfg.dataset, vocab=mcfg.vocab_size, seq_len=cfg.seq_len,
+                                 local_batch=cfg.local_batch_size, seed=cfg.seed, rank=self.data_rank,
+                                 world=self.data_world, shuffle=cfg.data_shuffle, prefetch=cfg.data_prefetch,
+                                 bytes_per_token=cfg.data_bytes_per_token)
+        self.val_data = None
+        if cfg.val_dataset:
+            self.val_data = TokenFileLoader(cfg.val_dataset, cfg.seq_len, cfg.local_batch_size, rank=self.data_rank,
+                                            world=self.data_world, shuffle=False, prefetch=cfg.data_prefetch,
+                                            vocab=mcfg.vocab_size, bytes_per_token=cfg.data_bytes_per_token)
 
     @property
     def last_grad_norm(self) -> float:
@@ -236,6 +231,32 @@ class Trainer:
         self.optimizers.zero_grad(set_to_none=True)
         self.step_idx += 1
         return loss.detach()
+
+    @torch.no_grad()
+    def validate(self, steps: int) -> float:
+        """Mean loss over the first ``steps`` batches of the validation files
+        (read from their start on every call, in file order), averaged over
+        the data-parallel ranks; the same value is returned on every rank."""
+        if self.val_data is None:
+            raise ValueError("no validation dataset configured (TrainerConfig.val_dataset)")
+        if self.pp_runner is not None:
+            raise NotImplementedError("validation with pipeline parallelism is not supported")
+        self.val_data.load_state_dict({"samples": 0})
+        total = torch.zeros((), device=self.device, dtype=torch.float32)
+        for _ in range(steps):
+            t, l = self.val_data.next()
+            loss = self.model.loss(t.to(self.device, non_blocking=True), l.to(self.device, non_blocking=True))
+            sp = getattr(self.model, "sp", None)
+            if sp is not None:  # each TP rank holds its tokens' share of the batch loss
+                loss = loss.detach().clone()
+                dist.all_reduce(loss, group=sp.group)
+            total += loss.float()
+        total /= max(1, steps)
+        if dist.is_initialized() and dist.get_world_size() > 1:
+            # TP ranks hold equal values: the sum over all ranks / world = mean over DP ranks
+            dist.all_reduce(total)
+            total /= dist.get_world_size()
+        return float(total)
 
     def train(self, steps: Optional[int] = None, log=print) -> List[float]:
         steps = steps or self.cfg.steps

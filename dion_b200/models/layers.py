@@ -121,4 +121,13 @@ def linear_cross_entropy(h: torch.Tensor, W: torch.Tensor, labels: torch.Tensor,
     lab = labels.reshape(-1)
     if not h.is_cuda:
         return F.cross_entropy((h2 @ W.t()).float(), lab)
+    if not (torch.is_grad_enabled() and (h.requires_grad or W.requires_grad)):
+        # evaluation: the same chunked loss without the gradient products
+        T = h2.shape[0]
+        total = torch.zeros((), device=h.device, dtype=torch.float32)
+        for s in range(0, T, chunk):
+            e = min(T, s + chunk)
+            loss_c, _ = _fused.cross_entropy_fwd_bwd(h2[s:e] @ W.t(), lab[s:e], 1.0 / T)
+            total += loss_c
+        return total / T
     return _LinearCE.apply(h2, W, lab, chunk)

@@ -5,9 +5,11 @@
 
 Builds the model, FSDP2/HSDP mesh, hybrid optimizer and LR schedule from a
 registered :class:`~dion_b200.integration.config.JobConfig`, trains on
-synthetic uniform tokens, logs torchtitan-style lines (step, loss,
-grad_norm, memory, tps, tflops, mfu) and optionally writes JSONL metrics and
-DCP checkpoints.
+synthetic uniform tokens or token files (``--dataloader.dataset``), logs
+torchtitan-style lines (step, loss, grad_norm, memory, tps, tflops, mfu),
+runs a validation pass every ``--validator.freq`` steps when enabled, and
+optionally writes JSONL metrics and DCP checkpoints (with the data
+position).
 """
 from __future__ import annotations
 
@@ -54,6 +56,11 @@ def trainer_config_from_job(job: JobConfig) -> TrainerConfig:
         log_freq=job.metrics.log_freq,
         ac_mode=job.activation_checkpoint.mode,
         ac_option=job.activation_checkpoint.selective_ac_option,
+        dataset=job.dataloader.dataset,
+        data_shuffle=job.dataloader.shuffle,
+        data_prefetch=job.dataloader.prefetch,
+        data_bytes_per_token=job.dataloader.bytes_per_token,
+        val_dataset=job.validator.dataset if job.validator.enable else "",
     )
 
 
@@ -84,6 +91,8 @@ def main(argv: Optional[List[str]] = None) -> List[float]:
     leftover = apply_overrides(job, rest)
     if leftover:
         raise SystemExit(f"unrecognised arguments: {leftover}")
+    if job.validator.enable and not job.validator.dataset:
+        raise SystemExit("--validator.enable needs held-out token files: --validator.dataset PATH")
     tc = trainer_config_from_job(job)
     tr = Trainer(tc)
     from .benchmarks.metrics_collector import OptimizerMetricsCollector
@@ -123,6 +132,12 @@ def main(argv: Optional[List[str]] = None) -> List[float]:
                       f"tps: {tps:,.0f}  tflops: {tflops:,.2f}  mfu: {mfu:.2f}%", flush=True)
             if collector is not None:
                 collector.collect(s, loss=v, grad_norm=gn, tps=tps)
+        if job.validator.enable and (s % job.validator.freq == 0 or s == tc.steps):
+            vloss = tr.validate(job.validator.steps)
+            if tr.rank == 0:
+                print(f"validate step: {s:5d}  loss: {vloss:8.4f}", flush=True)
+            if collector is not None:
+                collector.collect(s, val_loss=vloss)
         if ckpt is not None:
             ckpt.maybe_save(tr, s, final=(s == tc.steps))
     if dist.is_initialized():

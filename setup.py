@@ -2,13 +2,14 @@
 
     python setup.py build_ext --inplace
 
-produces dion_b200/_C.*.so next to the Python sources.
+produces dion_b200/_C.*.so (the sm_100a kernels) and dion_b200/_io.*.so
+(host-side data loading, plain C++) next to the Python sources.
 """
 import glob
 import os
 
 from setuptools import setup
-from torch.utils.cpp_extension import BuildExtension, CUDAExtension
+from torch.utils.cpp_extension import BuildExtension, CppExtension, CUDAExtension
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join("dion_b200", "csrc")
@@ -37,7 +38,15 @@ setup(
             sources=sources,
             include_dirs=[os.path.join(HERE, CSRC)],
             extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
-        )
+        ),
+        CppExtension(
+            name="dion_b200._io",
+            sources=[os.path.join(CSRC, "io", "token_loader.cpp")],
+            extra_compile_args=["-O3", "-std=c++17", "-pthread"],
+            # the C++ runtime torch itself loads (a compiler whose libstdc++.so link is
+            # missing would otherwise embed the static archive)
+            extra_link_args=["-pthread", "-l:libstdc++.so.6"],
+        ),
     ],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
 )

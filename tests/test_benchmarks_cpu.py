@@ -106,7 +106,10 @@ def test_logparse(tmp_path):
     assert d["tps"] == [1234.0] * 3 and d["mfu"][0] == 12.34 and d["time_s"] == [0.0, 10.0, 20.0]
     ours = tmp_path / "muon_run.log"
     ours.write_text("step:    10  loss:   7.1234  grad_norm:  0.5000  memory:  3.00GiB  tps: 98,765  "
-                    "tflops: 400.50  mfu: 20.00%\n")
+                    "tflops: 400.50  mfu: 20.00%\nvalidate step:    10  loss:   7.5000\n"
+                    "validate step:    15  loss:   7.2500\n")
+    mine = logparse.parse_log(str(ours))
+    assert mine["step"] == [10] and mine["val_step"] == [10, 15] and mine["val_loss"] == [7.5, 7.25]
     out = logparse.generate_plots([str(log), str(ours)], str(tmp_path / "plots"), tokens_per_step=4096)
     assert any(p.endswith(".svg") for p in out)
     with open(out[-1]) as fh:
