@@ -76,6 +76,11 @@ def test_linear_cross_entropy():
     assert abs(loss.item() - lf.item()) < 1e-2
     torch.testing.assert_close(h.grad.float(), hf.grad, rtol=5e-2, atol=5e-3)
     torch.testing.assert_close(W.grad.float(), Wf.grad, rtol=5e-2, atol=5e-3)
+    # evaluation (no autograd): the same chunked loss without the gradient products
+    W.grad = None
+    with torch.no_grad():
+        ev = L.linear_cross_entropy(h, W, lab, chunk=128)
+    assert W.grad is None and abs(ev.item() - lf.item()) < 1e-2 and abs(ev.item() - loss.item()) < 1e-5
 
 
 @pytest.mark.parametrize("rows,dim", [(513, 2048), (64, 1024)])
