@@ -22,6 +22,9 @@ __all__ = [
     "matmul_to_ptrs",
     "matmul_precise",
     "philox_normal",
+    "random_unit_columns_",
+    "keyed_unit_columns_",
+    "keyed_stream",
     "newton_schulz",
     "muon_momentum_",
     "scaled_update_",
@@ -603,6 +606,46 @@ def random_unit_columns_(Q: Tensor, key: Optional[int] = None, stream: Optional[
     if Q.stride(1) == 1 and Q.dtype in (torch.float32, torch.bfloat16):
         return col_normalize(z, col_sumsq(z), 1e-12, Q.unsqueeze(0))[0]
     Q.copy_(col_normalize(z, col_sumsq(z), 1e-12, torch.empty_like(z))[0])
+    return Q
+
+
+_KEYED_STREAM_TAG = 0x4B59 << 48  # keyed refills: apart from the counter-keyed streams
+
+
+def _mix64(x: int) -> int:
+    """splitmix64 finaliser (Steele, Lea and Flood, OOPSLA 2014)."""
+    m = (1 << 64) - 1
+    x = (x + 0x9E3779B97F4A7C15) & m
+    x = ((x ^ (x >> 30)) * 0xBF58476D1CE4E5B9) & m
+    x = ((x ^ (x >> 27)) * 0x94D049BB133111EB) & m
+    return x ^ (x >> 31)
+
+
+def keyed_stream(*parts: int) -> int:
+    """A 48-bit stream id that is a pure function of ``parts`` (tagged so it
+    never meets the call-counter streams)."""
+    h = 0
+    for v in parts:
+        h = _mix64(h ^ (int(v) & ((1 << 64) - 1)))
+    return _KEYED_STREAM_TAG | (h & ((1 << 48) - 1))
+
+
+def keyed_unit_columns_(Q: Tensor, *parts: int) -> Tensor:
+    """Unit-norm Gaussian columns in the 2-D view ``Q`` that are a pure
+    function of the process seed and ``parts`` (e.g. a step counter and the
+    column range): a run resumed from a checkpoint, and every rank, draws the
+    same columns as an uninterrupted run. CUDA: the Philox and column
+    kernels; CPU: torch's generator seeded from the same key."""
+    rows, cols = Q.shape
+    if rows == 0 or cols == 0:
+        return Q
+    stream = keyed_stream(*parts)
+    if Q.is_cuda and has_ext():
+        return random_unit_columns_(Q, stream=stream)
+    gen = torch.Generator(device=Q.device)
+    gen.manual_seed(_mix64(torch.initial_seed() ^ stream) & ((1 << 63) - 1))
+    z = torch.randn(rows, cols, device=Q.device, dtype=torch.float32, generator=gen)
+    Q.copy_((z / z.norm(dim=0, keepdim=True).clamp_min(1e-12)).to(Q.dtype))
     return Q
 
 

@@ -334,15 +334,19 @@ class LowRankOptimizer(Optimizer):
         st["tr"] = tr
         st["step"] = 0
 
-    @staticmethod
-    def _refill(Qbuf: Tensor, lo: int, hi: int, gen: Optional[torch.Generator] = None) -> None:
-        """Fresh unit-norm Gaussian columns [lo, hi) of Qbuf (on CUDA without
-        an explicit generator: the Philox + column-normalise kernels)."""
-        if hi > lo and gen is None and _col_kernels(Qbuf):
-            ops.random_unit_columns_(Qbuf[:, lo:hi])
-        elif hi > lo:
-            Qbuf[:, lo:hi].copy_(F.normalize(
-                torch.randn(Qbuf.shape[0], hi - lo, device=Qbuf.device, dtype=Qbuf.dtype, generator=gen), dim=0))
+    def _refill(self, Qbuf: Tensor, lo: int, hi: int, step: int, gen: Optional[torch.Generator] = None) -> None:
+        """Fresh unit-norm Gaussian columns [lo, hi) of Qbuf. Without an
+        explicit generator the draws are a pure function of (process seed,
+        optimizer tag, Qbuf's shape, step, lo, hi), like the initial Qbuf
+        (keyed by shape), so every rank and a run resumed from a checkpoint
+        draw the same columns (CUDA: the Philox + column-normalise kernels)."""
+        if hi <= lo:
+            return
+        if gen is None:
+            ops.keyed_unit_columns_(Qbuf[:, lo:hi], self.SEED_TAG, Qbuf.shape[0], Qbuf.shape[1], step, lo, hi)
+            return
+        Qbuf[:, lo:hi].copy_(F.normalize(
+            torch.randn(Qbuf.shape[0], hi - lo, device=Qbuf.device, dtype=Qbuf.dtype, generator=gen), dim=0))
 
     @staticmethod
     def _write_q(st: Dict[str, Any], Qn: Tensor, r: int) -> None:

@@ -126,7 +126,7 @@ class AdaDion(LowRankOptimizer):
         if st["step"] <= g["rank_warmup_steps"]:
             des = max(re, int(min(g["warmup_rank"], rc, cap)))
             if des > r:
-                self._refill(Qbuf, r, des)
+                self._refill(Qbuf, r, des, st["step"])
             st["r"] = des
             return
         sig = torch.linalg.vector_norm(R.float(), dim=0)
@@ -158,7 +158,7 @@ class AdaDion(LowRankOptimizer):
             rn = r
         rn = int(min(max(re, rn), rc, cap))
         if rn > r:
-            self._refill(Qbuf, r, rn)
+            self._refill(Qbuf, r, rn, st["step"])
         st["r"] = rn
 
     def get_effective_rank(self) -> Dict[str, float]:

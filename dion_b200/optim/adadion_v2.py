@@ -26,7 +26,6 @@ import math
 from typing import Any, Dict, List, Optional, Tuple, Union
 
 import torch
-import torch.nn.functional as F
 from torch import Tensor
 from torch.distributed import ProcessGroup
 from torch.distributed.device_mesh import DeviceMesh
@@ -191,11 +190,10 @@ class AdaDionV2(Dion):
             r_next = int(min(max(c["rank_min"], r_next), r_cap))
             if r_next > r:
                 Q = self._q_full[id(p)]
-                if Q.is_cuda and ops.has_ext():
-                    ops.random_unit_columns_(Q[:, r:r_next])  # Philox + column-normalise kernels
-                else:
-                    Q[:, r:r_next].copy_(F.normalize(
-                        torch.randn(Q.shape[0], r_next - r, device=Q.device, dtype=Q.dtype), dim=0))
+                # keyed by (shape, adaptation step, column range): identical on every
+                # rank and after a resume (CUDA: Philox + column-normalise kernels)
+                ops.keyed_unit_columns_(Q[:, r:r_next], 0x41445632, Q.shape[0], Q.shape[1], st["ada_step"], r,
+                                        r_next)
             st["r"] = r_next
 
     # ------------------------------------------------------------------ diagnostics

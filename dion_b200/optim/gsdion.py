@@ -164,7 +164,7 @@ class GSDion(LowRankOptimizer):
         if ((st["step"] % g["refresh_period"] == 0) or (q_t > g["refresh_spike"])) and st["step"] > warm:
             gen = torch.Generator(device=pl.device)
             gen.manual_seed(0x5246 + st["step"])
-            self._refill(Qbuf, 0, r, gen)
+            self._refill(Qbuf, 0, r, st["step"], gen)
         if g["use_residual_rank"] and st["step"] > warm:
             if q_t > g["tau_up"]:
                 st["good_streak"] = 0
@@ -180,12 +180,12 @@ class GSDion(LowRankOptimizer):
             rn = quantize_int(min(max(re, rn), rc, cap), g["rank_quantize"])
             rn = int(min(max(re, rn), rc, cap))
             if rn > r:
-                self._refill(Qbuf, r, rn)
+                self._refill(Qbuf, r, rn, st["step"])
             st["r"] = rn
         elif st["step"] <= warm:
             des = max(re, int(min(g["warmup_rank"], rc, cap)))
             if des > r:
-                self._refill(Qbuf, r, des)
+                self._refill(Qbuf, r, des, st["step"])
             st["r"] = des
         st.update({"_q_t": q_t, "_s_t": s_t, "_s_raw": s_raw, "_c_t": c_t, "_alpha_t": alpha_t, "_m_t": m_t,
                    "_dw_fro": dw_fro, "_dw_rms": dw_rms, "_grad_rms": grad_rms, "_update_rms": _rms(D).item()})

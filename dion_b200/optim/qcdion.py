@@ -114,7 +114,7 @@ class QCDion(LowRankOptimizer):
                 if st["bad_streak"] >= g["boost_k"]:
                     rn = min(r * 2, rc, Qbuf.shape[1])
                     if rn > r:
-                        self._refill(Qbuf, r, rn)
+                        self._refill(Qbuf, r, rn, st["step"])
                     st["r"] = rn
                     st["bad_streak"] = 0
             else:

@@ -28,6 +28,12 @@ NVCC_FLAGS = ARCH + [
 if os.environ.get("BDION_PTXAS_VERBOSE"):
     NVCC_FLAGS.append("-Xptxas=-v")
 
+# Link the shared C++ runtime that torch itself loads. A toolchain whose
+# libstdc++.so development link is missing silently embeds the static archive
+# instead, and torch's error checks (which format their messages with
+# iostreams) then crash inside the extension rather than raising.
+LINK_CXX_RUNTIME = ["-l:libstdc++.so.6"]
+
 sources = sorted(glob.glob(os.path.join(CSRC, "*.cu"))) + sorted(glob.glob(os.path.join(CSRC, "*.cpp")))
 
 setup(
@@ -38,14 +44,13 @@ setup(
             sources=sources,
             include_dirs=[os.path.join(HERE, CSRC)],
             extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
+            extra_link_args=LINK_CXX_RUNTIME,
         ),
         CppExtension(
             name="dion_b200._io",
             sources=[os.path.join(CSRC, "io", "token_loader.cpp")],
             extra_compile_args=["-O3", "-std=c++17", "-pthread"],
-            # the C++ runtime torch itself loads (a compiler whose libstdc++.so link is
-            # missing would otherwise embed the static archive)
-            extra_link_args=["-pthread", "-l:libstdc++.so.6"],
+            extra_link_args=["-pthread"] + LINK_CXX_RUNTIME,
         ),
     ],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},

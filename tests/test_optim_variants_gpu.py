@@ -106,6 +106,58 @@ def test_random_unit_columns_kernel_matches_oracle():
     assert torch.allclose(n, torch.ones_like(n), atol=1e-2)
 
 
+def test_keyed_unit_columns_are_a_function_of_their_key():
+    """Keyed refills (used so resumed runs and every rank draw the same
+    columns): same key -> same columns, another key -> other columns, and
+    the kernel result equals the Philox oracle for that key's stream."""
+    Q1 = torch.zeros(200, 16, device="cuda")
+    Q2 = torch.zeros(200, 16, device="cuda")
+    ops.keyed_unit_columns_(Q1[:, 2:10], 7, 200, 16, 5, 2, 10)
+    ops.keyed_unit_columns_(Q2[:, 2:10], 7, 200, 16, 5, 2, 10)
+    assert torch.equal(Q1, Q2)
+    ops.keyed_unit_columns_(Q2[:, 2:10], 7, 200, 16, 6, 2, 10)
+    assert not torch.equal(Q1, Q2)
+    z = ops.philox_normal((200, 8), torch.initial_seed(), ops.keyed_stream(7, 200, 16, 5, 2, 10), 1.0, "cpu")
+    ref = (z / z.norm(dim=0, keepdim=True)).double()
+    assert torch.allclose(Q1[:, 2:10].double().cpu(), ref, atol=1e-5, rtol=1e-4)
+
+
+LOWRANK_ADAPTIVE = [(c, kw) for c, kw in ADAPTIVE if c is not AdaDionV2]
+
+
+@pytest.mark.parametrize("cls,kw", LOWRANK_ADAPTIVE, ids=[c.__name__ for c, _ in LOWRANK_ADAPTIVE])
+def test_cuda_resume_matches_uninterrupted(cls, kw):
+    """Adaptive-rank runs refill Q columns; with keyed refills a run resumed
+    from a state dict reproduces the uninterrupted run. (AdaDionV2 is left
+    out: its randomised orthogonaliser draws a fresh sketch per call, which
+    changes the result only by rounding and column signs.)"""
+    torch.manual_seed(1)
+    x0 = torch.randn(256, 128, device="cuda")
+
+    def grads(i):
+        return torch.randn(256, 128, device="cuda", generator=torch.Generator("cuda").manual_seed(100 + i)) * 0.1
+
+    ref = nn.Parameter(x0.clone())
+    R = cls([ref], **kw)
+    for i in range(6):
+        ref.grad = grads(i)
+        R.step()
+    a = nn.Parameter(x0.clone())
+    A = cls([a], **kw)
+    for i in range(3):
+        a.grad = grads(i)
+        A.step()
+    b = nn.Parameter(a.detach().clone())
+    B = cls([b], **kw)
+    B.load_state_dict(copy.deepcopy(A.state_dict()))
+    for i in range(3, 6):
+        b.grad = grads(i)
+        B.step()
+    torch.cuda.synchronize()
+    ops.check_status()
+    assert torch.allclose(b.detach(), ref.detach(), rtol=1e-4, atol=1e-5)
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_col_normalize_2d_matches_fp32(dtype):
     torch.manual_seed(3)
