@@ -359,19 +359,53 @@ class LowRankOptimizer(Optimizer):
         return D, False
 
     # ---- checkpoint
+    # Per-matrix state entries that hold None until first set (EMAs, anchors).
+    # A flattened DCP checkpoint (the container's format) stores only tensors
+    # and numbers, so state_dict() leaves out entries that are None (put back
+    # by load_state_dict()) and text diagnostics such as SDion's last mode.
+    NULLABLE_STATE: Tuple[str, ...] = ()
+    # Under FSDP the state is kept as plain local tensors. Entries whose rows
+    # follow the parameter's row shard ("always", or "tr" when the matrix is
+    # handled transposed so the basis lives on its rows) are checkpointed as
+    # DTensors with the parameter's placements, so DCP stores every rank's
+    # rows (a plain tensor would be saved once, as if replicated).
+    ROW_SHARDED_STATE: Dict[str, str] = {"M": "always", "Dr_ema": "always", "Qbuf": "tr", "Q_anchor": "tr",
+                                         "Q_prev_proj": "tr"}
+
+    def _checkpoint_entry(self, p: Tensor, st: Dict[str, Any], k: str, v: Any) -> Any:
+        mode = self.ROW_SHARDED_STATE.get(k)
+        if not (isinstance(v, Tensor) and isinstance(p, DTensor)) or mode is None or (mode == "tr" and not st.get("tr")):
+            return v
+        shape = torch.Size((p.shape[0],) + tuple(v.shape[1:]))
+        stride = tuple(int(math.prod(shape[i + 1:])) for i in range(len(shape)))
+        return DTensor.from_local(v.contiguous(), p.device_mesh, p.placements, run_check=False, shape=shape,
+                                  stride=stride)
+
     def state_dict(self):
         sd = super().state_dict()
+        params = [p for g in self.param_groups for p in g["params"]]
+        sd["state"] = {k: {n: (self._checkpoint_entry(params[k], st, n, v) if isinstance(k, int) and k < len(params)
+                               else v)
+                           for n, v in st.items() if v is not None and not isinstance(v, str)}
+                       for k, st in sd["state"].items()}
         ws = self._ws()
         if ws > 1:
             sd[self.WS_KEY] = ws
         return sd
 
-    def load_state_dict(self, sd):
-        sd = dict(sd)
+    def load_state_dict(self, state_dict):
+        sd = dict(state_dict)
         saved = sd.pop(self.WS_KEY, None)
         if saved is not None and saved != self._ws():
             raise RuntimeError(f"Checkpoint world_size={saved} != current {self._ws()}")
         super().load_state_dict(sd)
+        for st in self.state.values():
+            for k, v in list(st.items()):
+                if isinstance(v, DTensor):  # back to this rank's rows
+                    st[k] = v.to_local()
+            if "M" in st:
+                for k in self.NULLABLE_STATE:
+                    st.setdefault(k, None)
 
     # ---- diagnostics
     def get_rank(self) -> Dict[str, int]:

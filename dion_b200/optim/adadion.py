@@ -27,6 +27,7 @@ __all__ = ["AdaDion"]
 class AdaDion(LowRankOptimizer):
     WS_KEY = "_adadion_ws"
     SEED_TAG = 0x4469_6F6E
+    NULLABLE_STATE = ("erank_ema", "aerr_ema", "Q_anchor")
     DIAG_KEYS = ("r", "erank_ema", "aerr_ema")
 
     def __init__(

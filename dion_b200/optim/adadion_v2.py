@@ -29,6 +29,7 @@ import torch
 from torch import Tensor
 from torch.distributed import ProcessGroup
 from torch.distributed.device_mesh import DeviceMesh
+from torch.distributed.tensor import DTensor
 
 from .. import ops
 from ._utils import device_list, to_local
@@ -157,6 +158,47 @@ class AdaDionV2(Dion):
             sub = P.index_select(0, it)[:, :, :r].contiguous()
             out[it, :, :r] = orthogonalize(sub, float(group["oversample"]))
         return out
+
+    # ------------------------------------------------------------------ checkpoint
+    # In adaptive mode ``momentum`` and ``Q`` are plain local tensors (shards of
+    # a sharded parameter's state). The checkpoint view wraps them as DTensors
+    # of the parameter's mesh (momentum with the parameter's placements, Q with
+    # Dion's Q placements), so DCP stores every shard and reshards on load;
+    # loading re-packs them into a local arena on the next step, as for Dion.
+    # erank_ema / aerr_ema are None until first set; a flattened DCP checkpoint
+    # (the container's format) cannot hold None, so they are left out while
+    # None and put back on load.
+    def _checkpoint_view(self, p: Tensor, st: Dict[str, Any]) -> Dict[str, Any]:
+        out = {n: v for n, v in st.items() if v is not None}
+        cfg = self._param_config.get(p)
+        if not (self._adaptive_rank and isinstance(p, DTensor) and "r_cap" in st) or (
+                cfg is not None and cfg.inner_shard_mesh_dim is not None):
+            return out  # (with an inner shard the local tensors stay as they are)
+        mom, Q = st.get("momentum"), st.get("Q")
+        if mom is not None and not isinstance(mom, DTensor):
+            out["momentum"] = DTensor.from_local(mom.contiguous(), p.device_mesh, p.placements, run_check=False,
+                                                 shape=p.shape, stride=p.stride())
+        if Q is not None and not isinstance(Q, DTensor) and cfg is not None:
+            if cfg.Q_sharded_placements is None:
+                self._q_placements(p, cfg)
+            rows = p.shape[0] if st["transpose"] else p.shape[1]
+            out["Q"] = DTensor.from_local(Q.contiguous(), p.device_mesh, cfg.Q_sharded_placements, run_check=False,
+                                          shape=torch.Size((rows, Q.shape[1])), stride=(Q.shape[1], 1))
+        return out
+
+    def state_dict(self):
+        sd = super().state_dict()
+        params = [p for g in self.param_groups for p in g["params"]]
+        sd["state"] = {k: self._checkpoint_view(params[k], st) if isinstance(k, int) and k < len(params)
+                       else {n: v for n, v in st.items() if v is not None} for k, st in sd["state"].items()}
+        return sd
+
+    def load_state_dict(self, state_dict) -> None:
+        super().load_state_dict(state_dict)
+        for st in self.state.values():
+            if "r_cap" in st:
+                st.setdefault("erank_ema", None)
+                st.setdefault("aerr_ema", None)
 
     def _after_update(self, group, params, order, sumsq, ranks) -> None:
         if ranks is None:

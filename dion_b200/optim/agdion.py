@@ -21,6 +21,7 @@ __all__ = ["AGDion"]
 class AGDion(LowRankOptimizer):
     WS_KEY = "_agdion_ws"
     SEED_TAG = 0x4147_4469
+    NULLABLE_STATE = ("Q_anchor",)
     DIAG_KEYS = ("r", "_drift", "_tail", "_did_extra", "_did_refresh", "_steps_since_refresh")
 
     def __init__(

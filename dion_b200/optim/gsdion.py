@@ -32,6 +32,7 @@ def _rms(X) -> torch.Tensor:
 class GSDion(LowRankOptimizer):
     WS_KEY = "_gsdion_ws"
     SEED_TAG = 0x4753_4469
+    NULLABLE_STATE = ("log_rms_ema", "Q_anchor")
     DIAG_KEYS = ("r", "_q_t", "_s_t", "_s_raw", "_c_t", "_alpha_t", "_m_t", "_dw_fro", "_dw_rms", "_grad_rms",
                  "_update_rms", "q_ema")
 

@@ -24,6 +24,7 @@ __all__ = ["QCDion"]
 class QCDion(LowRankOptimizer):
     WS_KEY = "_qcdion_ws"
     SEED_TAG = 0x5143_4469
+    NULLABLE_STATE = ("Q_prev_proj",)
     DIAG_KEYS = ("r", "_q_t", "_d_t", "_e_t", "_z_t", "_g_t", "_D_fro", "z_ema", "_extra_step", "bad_streak")
 
     def __init__(

@@ -26,6 +26,7 @@ __all__ = ["SDion"]
 class SDion(LowRankOptimizer):
     WS_KEY = "_sdion_ws"
     SEED_TAG = 0x5344_696F
+    NULLABLE_STATE = ("Q_anchor",)
     DIAG_KEYS = ("r", "_drift", "_tail", "_mode", "steps_skipped", "total_skips", "total_full", "total_consensus",
                  "total_recovery")
 

@@ -253,3 +253,58 @@ def test_checkpoint_load_model_only_and_full(tmp_path):
 
     with pytest.raises((CheckpointException, RuntimeError, KeyError)):
         ckpt.load(str(tmp_path / "step-5"), _MockLlama(), c3)
+
+
+def _reshard_body(folder, phase, optimizer, rank, world):
+    """phase "save": FSDP over `world` ranks, 2 steps, checkpoint, then 2 more
+    steps; phase "load": resume the checkpoint and take the same 2 steps."""
+    import torch.distributed as dist
+
+    from dion_b200.checkpoint import CheckpointManager
+    from dion_b200.integration.hybrid_optimizer import HybridOptimizersContainer
+    from dion_b200.integration.trainer import Trainer, TrainerConfig
+
+    cfg = TrainerConfig(model="tiny", model_overrides=dict(n_layers=2, vocab_size=512, max_seq_len=64), seq_len=32,
+                        local_batch_size=4 // world, steps=4, warmup_steps=0, dp_shard=world,
+                        optimizer=HybridOptimizersContainer.Config(name=optimizer, lr=0.02, scalar_lr=3e-3), seed=5)
+    torch.manual_seed(0)
+    tr = Trainer(cfg, device=torch.device("cpu"))
+    ck = CheckpointManager(folder, tr.model, tr.optimizers, interval=2, model_only_last=False)
+    if phase == "save":
+        for s in (1, 2):
+            tr.train_step(*tr.data.next())
+            ck.maybe_save(tr, s)
+    else:
+        ck.maybe_load(tr)
+        assert tr.step_idx == 2
+    losses = []
+    for _ in range(2):
+        loss = tr.train_step(*tr.data.next()).detach().clone()
+        if world > 1:  # mean over the data-parallel ranks = the global batch's loss
+            dist.all_reduce(loss)
+            loss /= world
+        losses.append(float(loss))
+    return losses
+
+
+# Dion2 under FSDP selects rows per shard, so its update depends on the world
+# size by definition: its checkpoint is resumed at the same size.
+@pytest.mark.parametrize("optimizer,load_world", [("Dion", 1), ("Muon", 1), ("AdaDionV2", 1), ("Dion2", 2),
+                                                  ("AdaDion", 2)])
+def test_fsdp_checkpoint_reshards_across_world_sizes(tmp_path, optimizer, load_world):
+    """A checkpoint (matrix optimizer + AdamW) written by 2 FSDP ranks (gloo)
+    resumes on ``load_world`` ranks: the same global batches give the losses
+    the uninterrupted 2-rank run reached (AdaDionV2 in adaptive-rank mode,
+    whose local state is checkpointed as DTensors)."""
+    import functools
+
+    from test_distributed_cpu import spawn
+
+    folder = str(tmp_path / "ck")
+    saved = spawn(functools.partial(_reshard_body, folder, "save", optimizer), world=2)
+    for r, (status, res) in saved.items():
+        assert status == "ok", res
+    loaded = spawn(functools.partial(_reshard_body, folder, "load", optimizer), world=load_world)
+    assert loaded[0][0] == "ok", loaded[0][1]
+    a, b = torch.tensor(saved[0][1]), torch.tensor(loaded[0][1])
+    assert torch.allclose(a, b, rtol=1e-4, atol=1e-4), (a, b)
