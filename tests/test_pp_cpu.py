@@ -46,3 +46,40 @@ def test_pipeline_with_fsdp():
     ref, _ = _run(1, 2)
     got, _ = _run(2, 2)
     assert torch.allclose(ref, got, rtol=2e-3, atol=2e-3), (ref, got)
+
+
+def _ckpt_body(folder, phase, pp, rank, world):
+    """phase "save": 2 steps, checkpoint, 2 more steps; "load": resume, 2 steps."""
+    from dion_b200.checkpoint import CheckpointManager
+    from dion_b200.integration.hybrid_optimizer import HybridOptimizersContainer
+    from dion_b200.integration.trainer import Trainer, TrainerConfig
+
+    opt = HybridOptimizersContainer.Config(name="Muon", lr=0.02, scalar_lr=3e-3)
+    cfg = TrainerConfig(model="tiny", model_overrides=dict(n_layers=4, vocab_size=512, max_seq_len=64), seq_len=32,
+                        local_batch_size=4, steps=4, warmup_steps=0, dp_shard=1, pp=pp, pp_microbatches=2,
+                        optimizer=opt, seed=7, use_fsdp=False)
+    torch.manual_seed(0)
+    tr = Trainer(cfg, device=torch.device("cpu"))
+    ck = CheckpointManager(folder, tr.model, tr.optimizers, interval=2, model_only_last=False)
+    if phase == "save":
+        for s in (1, 2):
+            tr.train_step(*tr.data.next())
+            ck.maybe_save(tr, s)
+    else:
+        ck.maybe_load(tr)
+        assert tr.step_idx == 2
+    return [float(tr.train_step(*tr.data.next())) for _ in range(2)]
+
+
+def test_pipeline_checkpoint_resumes_without_pipeline(tmp_path):
+    """Stages keep the full model's parameter names, so a checkpoint written by
+    a 2-stage pipeline loads into the unpipelined model (and optimizer) and
+    continues with the pipeline's losses."""
+    folder = str(tmp_path / "ck")
+    saved = spawn(functools.partial(_ckpt_body, folder, "save", 2), world=2)
+    for r in saved.values():
+        assert r[0] == "ok", r[1]
+    loaded = spawn(functools.partial(_ckpt_body, folder, "load", 1), world=1)
+    assert loaded[0][0] == "ok", loaded[0][1]
+    a, b = torch.tensor(saved[0][1]), torch.tensor(loaded[0][1])
+    assert torch.allclose(a, b, rtol=2e-3, atol=2e-3), (a, b)
