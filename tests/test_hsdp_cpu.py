@@ -45,3 +45,47 @@ def test_hsdp_matches_fsdp(optimizer):
 def test_hsdp_trains(optimizer):
     got = _run(optimizer, 2, 2)
     assert torch.isfinite(got).all()
+
+
+def _ckpt_body(folder, phase, optimizer, rank, world):
+    import torch.distributed as dist
+
+    from dion_b200.checkpoint import CheckpointManager
+    from dion_b200.integration.hybrid_optimizer import HybridOptimizersContainer
+    from dion_b200.integration.trainer import Trainer, TrainerConfig
+
+    opt = HybridOptimizersContainer.Config(name=optimizer, lr=0.02, scalar_lr=3e-3)
+    cfg = TrainerConfig(model="tiny", model_overrides=dict(n_layers=2, vocab_size=512, max_seq_len=64), seq_len=32,
+                        local_batch_size=2, steps=4, warmup_steps=0, dp_replicate=2, dp_shard=2, optimizer=opt,
+                        seed=11)
+    torch.manual_seed(0)
+    tr = Trainer(cfg, device=torch.device("cpu"))
+    ck = CheckpointManager(folder, tr.model, tr.optimizers, interval=2, model_only_last=False)
+    if phase == "save":
+        for s in (1, 2):
+            tr.train_step(*tr.data.next())
+            ck.maybe_save(tr, s)
+    else:
+        ck.maybe_load(tr)
+        assert tr.step_idx == 2
+    out = []
+    for _ in range(2):
+        loss = tr.train_step(*tr.data.next()).detach().clone()
+        dist.all_reduce(loss)
+        out.append(float(loss / world))
+    return out
+
+
+@pytest.mark.parametrize("optimizer", ["Dion", "Muon"])
+def test_hsdp_checkpoint_resume(tmp_path, optimizer):
+    """HSDP 2 x 2: replicas synchronise their state before the save
+    (Dion's ``synchronize_for_checkpoint``), and the resumed run continues
+    with the uninterrupted run's losses."""
+    folder = str(tmp_path / "ck")
+    saved = spawn(functools.partial(_ckpt_body, folder, "save", optimizer), world=4)
+    loaded = spawn(functools.partial(_ckpt_body, folder, "load", optimizer), world=4)
+    for out in (saved, loaded):
+        for r in out.values():
+            assert r[0] == "ok", r[1]
+    a, b = torch.tensor(saved[0][1]), torch.tensor(loaded[0][1])
+    assert torch.allclose(a, b, rtol=1e-4, atol=1e-4), (a, b)
