@@ -2,6 +2,7 @@
 file format, window contents, rank sharding, keyed per-epoch shuffling,
 resume by position, host-side vocabulary check, tokenization of text files,
 and the trainer / checkpoint / validation wiring (CPU)."""
+import functools
 import json
 import math
 import os
@@ -226,3 +227,31 @@ def test_loader_rejects_bad_output_buffers(tmp_path):
         ld._impl.next(torch.empty(2, 7, dtype=torch.int64), torch.empty(2, 8, dtype=torch.int64))
     with pytest.raises(ValueError, match="int64"):
         ld._impl.next(torch.empty(2, 8, dtype=torch.int32), torch.empty(2, 8, dtype=torch.int64))
+
+
+def _validate_body(train_dir, val, rank, world):
+    from dion_b200.integration.hybrid_optimizer import HybridOptimizersContainer
+    from dion_b200.integration.trainer import Trainer, TrainerConfig
+
+    cfg = TrainerConfig(model="debug", model_overrides=dict(vocab_size=256), seq_len=32, local_batch_size=4 // world,
+                        steps=4, warmup_steps=0, optimizer=HybridOptimizersContainer.Config(name="Muon"),
+                        dataset=train_dir, val_dataset=val, dp_shard=world)
+    torch.manual_seed(0)
+    tr = Trainer(cfg, device=torch.device("cpu"))
+    return [tr.validate(3)]
+
+
+def test_validation_is_split_over_data_parallel_ranks(tmp_path):
+    """FSDP over 2 ranks: each rank evaluates its half of every validation
+    batch and all ranks return the global mean, equal to one process
+    evaluating the whole batches."""
+    from test_distributed_cpu import spawn
+
+    train_dir, val = _corpus(tmp_path)
+    two = spawn(functools.partial(_validate_body, train_dir, val), world=2)
+    one = spawn(functools.partial(_validate_body, train_dir, val), world=1)
+    for out in (two, one):
+        for r, (status, res) in out.items():
+            assert status == "ok", res
+    assert two[0][1] == two[1][1]
+    assert abs(two[0][1][0] - one[0][1][0]) < 1e-4, (two[0][1], one[0][1])
