@@ -230,6 +230,12 @@ def device_list(values: Sequence, dtype: torch.dtype, device) -> Tensor:
     t = _DEV_LISTS.get(key)
     if t is None:
         if len(_DEV_LISTS) > 1024:
+            # a cached tensor may last have been read by a kernel still queued on
+            # another stream than the one that allocated it: let the device
+            # drain before its memory can be handed out again (rare: once per
+            # 1024 distinct lists)
+            if torch.cuda.is_available() and torch.cuda.is_initialized():
+                torch.cuda.synchronize()
             _DEV_LISTS.clear()
         t = torch.tensor(list(values), dtype=dtype)
         if getattr(device, "type", str(device)) == "cuda" or str(device).startswith("cuda"):
