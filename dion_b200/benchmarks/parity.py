@@ -145,19 +145,26 @@ def _build_optimizer(impl: str, optimizer: str, model, matrix_names, a, mesh=Non
     named = list(model.named_parameters())
     groups = _groups(named, set(matrix_names), a.scalar_lr, a.scalar_wd)
     if impl == "ours":
-        from ..optim import Dion, Muon
+        from ..optim import AdaDionV2, Dion, Muon
 
         if optimizer == "dion":
             return Dion(groups, outer_shard_mesh=mesh, lr=a.lr, mu=a.mu, rank_fraction=a.rank_fraction,
                         weight_decay=a.wd)
+        if optimizer == "adadion_v2":
+            return AdaDionV2(groups, outer_shard_mesh=mesh, lr=a.lr, mu=a.mu, rank_fraction_max=a.rank_fraction,
+                             weight_decay=a.wd, adaptive_rank=True, init_rank_fraction=a.init_rank_fraction,
+                             rank_min=a.rank_min)
         return Muon(groups, distributed_mesh=mesh, lr=a.lr, mu=a.mu, weight_decay=a.wd, nesterov=False,
                     adjust_lr="spectral_norm")
     if REF_PATH not in sys.path:
         sys.path.insert(0, REF_PATH)
-    if optimizer == "dion":
+    if optimizer in ("dion", "adadion_v2"):
         from ada_dion.optim.adadion_v2 import AdaDionV2
 
         # one rank: no outer shard mesh (the same call the benchmark's reference arm makes)
+        if optimizer == "adadion_v2":
+            return AdaDionV2(groups, lr=a.lr, mu=a.mu, rank_fraction_max=a.rank_fraction, weight_decay=a.wd,
+                             adaptive_rank=True, init_rank_fraction=a.init_rank_fraction, rank_min=a.rank_min)
         return AdaDionV2(groups, lr=a.lr, mu=a.mu, rank_fraction_max=a.rank_fraction, weight_decay=a.wd)
     from dion import Muon as RefMuon
 
@@ -240,7 +247,7 @@ def run_arm(impl: str, a, init_state=None, opt_seed: int = 0) -> Dict:
     opt = _build_optimizer(impl, a.optimizer, model, matrix_names, a, mesh)
     base = [g["lr"] for g in opt.param_groups]
     get = make_data(a.data, a.steps, a.batch, a.seq_len, cfg.vocab_size, a.data_seed)
-    losses = []
+    losses, ranks = [], []
     t0 = time.time()
     for s in range(a.steps):
         f = lr_factor(s, a.steps, a.warmup)
@@ -253,8 +260,14 @@ def run_arm(impl: str, a, init_state=None, opt_seed: int = 0) -> Dict:
         opt.step()
         opt.zero_grad(set_to_none=True)
         losses.append(float(loss.detach().float().item()))
-    return {"impl": impl, "losses": losses, "seconds": time.time() - t0, "opt_seed": opt_seed,
-            "state_layout": state_layout(opt, model), "init_state": init_state}
+        rk = opt.get_rank() if hasattr(opt, "get_rank") else {}
+        if rk:  # adaptive rank: the mean active rank over the matrices after this step
+            ranks.append(sum(rk.values()) / len(rk))
+    out = {"impl": impl, "losses": losses, "seconds": time.time() - t0, "opt_seed": opt_seed,
+           "state_layout": state_layout(opt, model), "init_state": init_state}
+    if ranks:
+        out["mean_ranks"] = ranks
+    return out
 
 
 def compare(ours: List[float], ref: List[float], spread: List[float] = None) -> Dict:
@@ -273,7 +286,8 @@ def compare(ours: List[float], ref: List[float], spread: List[float] = None) -> 
 def parse(argv=None):
     p = argparse.ArgumentParser()
     p.add_argument("--preset", default="tiny")
-    p.add_argument("--optimizer", choices=["dion", "muon"], default="dion")
+    p.add_argument("--optimizer", choices=["dion", "muon", "adadion_v2"], default="dion",
+                   help="adadion_v2: adaptive rank, Q at --rank-fraction, starting at --init-rank-fraction")
     p.add_argument("--impl", choices=["ours", "reference", "both"], default="both")
     p.add_argument("--device", default="cpu")
     p.add_argument("--dtype", choices=["fp32", "bf16", "mixed"], default="fp32")
@@ -289,6 +303,8 @@ def parse(argv=None):
     p.add_argument("--mu", type=float, default=0.95)
     p.add_argument("--wd", type=float, default=0.0)
     p.add_argument("--rank-fraction", type=float, default=0.25)
+    p.add_argument("--init-rank-fraction", type=float, default=0.125)
+    p.add_argument("--rank-min", type=int, default=8)
     p.add_argument("--scalar-lr", type=float, default=3e-4)
     p.add_argument("--scalar-wd", type=float, default=0.1)
     p.add_argument("--ref-seeds", type=int, default=1, help="reference runs with optimizer seeds 0..n-1")
@@ -307,6 +323,10 @@ def golden_record(res: Dict) -> Dict:
            "ours_losses": res["ours"]["losses"],
            "reference_state_layout": ref["state_layout"],
            "comparison": res.get("comparison")}
+    if "mean_ranks" in ref:
+        rec["reference_mean_ranks"] = [ref["mean_ranks"]] + [o["mean_ranks"]
+                                                              for o in res.get("reference_other_seeds", [])]
+        rec["ours_mean_ranks"] = res["ours"].get("mean_ranks")
     rec["config"].pop("golden", None)
     return rec
 

@@ -7,9 +7,10 @@ Builds the model, FSDP2/HSDP mesh, hybrid optimizer and LR schedule from a
 registered :class:`~dion_b200.integration.config.JobConfig`, trains on
 synthetic uniform tokens or token files (``--dataloader.dataset``), logs
 torchtitan-style lines (step, loss, grad_norm, memory, tps, tflops, mfu),
-runs a validation pass every ``--validator.freq`` steps when enabled, and
-optionally writes JSONL metrics and DCP checkpoints (with the data
-position).
+runs a validation pass every ``--validator.freq`` steps when enabled,
+records profiler traces every ``--profiling.profile_freq`` steps when
+enabled, and optionally writes JSONL metrics and DCP checkpoints (with the
+data position).
 """
 from __future__ import annotations
 
@@ -64,6 +65,31 @@ def trainer_config_from_job(job: JobConfig) -> TrainerConfig:
     )
 
 
+def _profiler(job: JobConfig, tr: Trainer):
+    """torch.profiler over the training loop when ``--profiling.enable_profiling``:
+    every ``profile_freq`` steps the last step is recorded (one warm-up step
+    before it) and written as a Chrome trace to
+    ``<save_traces_folder>/iteration_<step>/rank<r>_trace.json``, the layout
+    torchtitan uses and ``benchmarks.tiers.parse_profiler_trace`` reads."""
+    pc = job.profiling
+    if not pc.enable_profiling:
+        return None
+    freq = max(2, int(pc.profile_freq))
+    acts = [torch.profiler.ProfilerActivity.CPU]
+    if torch.cuda.is_available():
+        acts.append(torch.profiler.ProfilerActivity.CUDA)
+
+    def on_ready(p):
+        d = os.path.join(pc.save_traces_folder, f"iteration_{tr.step_idx}")
+        os.makedirs(d, exist_ok=True)
+        p.export_chrome_trace(os.path.join(d, f"rank{tr.rank}_trace.json"))
+
+    prof = torch.profiler.profile(activities=acts, schedule=torch.profiler.schedule(wait=freq - 2, warmup=1, active=1),
+                                  on_trace_ready=on_ready)
+    prof.__enter__()
+    return prof
+
+
 def _load_config(module: Optional[str], name: str) -> JobConfig:
     """Config ``name`` from this package's registry, or from ``module``'s
     function of that name (so experiment modules can add configs)."""
@@ -107,6 +133,7 @@ def main(argv: Optional[List[str]] = None) -> List[float]:
         ckpt = CheckpointManager(job.checkpoint.folder, tr.model, tr.optimizers, interval=job.checkpoint.interval,
                                  model_only_last=job.checkpoint.last_save_model_only)
         ckpt.maybe_load(tr)
+    prof = _profiler(job, tr)
     flops_tok = tr.model_cfg.flops_per_token(tc.seq_len)
     tokens_step = tc.local_batch_size * tc.seq_len
     losses: List[float] = []
@@ -140,6 +167,10 @@ def main(argv: Optional[List[str]] = None) -> List[float]:
                 collector.collect(s, val_loss=vloss)
         if ckpt is not None:
             ckpt.maybe_save(tr, s, final=(s == tc.steps))
+        if prof is not None:
+            prof.step()
+    if prof is not None:
+        prof.__exit__(None, None, None)
     if dist.is_initialized():
         dist.barrier()
     return losses

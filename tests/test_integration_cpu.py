@@ -308,3 +308,20 @@ def test_fsdp_checkpoint_reshards_across_world_sizes(tmp_path, optimizer, load_w
     assert loaded[0][0] == "ok", loaded[0][1]
     a, b = torch.tensor(saved[0][1]), torch.tensor(loaded[0][1])
     assert torch.allclose(a, b, rtol=1e-4, atol=1e-4), (a, b)
+
+
+def test_train_entry_writes_profiler_traces(tmp_path):
+    """--profiling.enable_profiling records one step every profile_freq steps
+    as a Chrome trace per rank (torchtitan's folder layout), which the trace
+    parser reads."""
+    from dion_b200 import train
+    from dion_b200.benchmarks.tiers import parse_profiler_trace
+
+    folder = tmp_path / "traces"
+    train.main(["--config", "llama3_debug_muon", "--training.steps", "4", "--training.seq_len", "32",
+                "--training.local_batch_size", "2", "--profiling.enable_profiling", "--profiling.profile_freq", "2",
+                "--profiling.save_traces_folder", str(folder)])
+    got = sorted(p.name for p in folder.iterdir())
+    assert got == ["iteration_2", "iteration_4"], got
+    res = parse_profiler_trace(str(folder / "iteration_4" / "rank0_trace.json"))
+    assert isinstance(res, dict) and res

@@ -1,7 +1,8 @@
 """Loss parity with the reference implementation on the CPU configuration
 (4-layer Llama, d=256, 4 heads, SwiGLU 1024, vocab 4096, seq 256, batch 8,
 fp32, N(0, 0.02) init from seed 0; Dion rank d/4, mu 0.95, lr 0.01 on the
-matrices, AdamW lr 3e-4 / betas 0.9, 0.95 / wd 0.1 on the rest; 50 steps).
+matrices, AdamW lr 3e-4 / betas 0.9, 0.95 / wd 0.1 on the rest; 50 steps;
+AdaDionV2 with adaptive rank between 1/8 and 1/4 of the matrix side).
 
 The golden files under tests/golden/ were written by
 ``python -m dion_b200.benchmarks.parity ... --golden`` from runs of the
@@ -28,7 +29,8 @@ def _load(name):
         return json.load(fh)
 
 
-@pytest.mark.parametrize("name", ["parity_tiny_dion.json", "parity_tiny_muon.json"])
+@pytest.mark.parametrize("name", ["parity_tiny_dion.json", "parity_tiny_muon.json",
+                                  "parity_tiny_adadion_v2.json"])
 def test_loss_curve_matches_reference(name):
     from dion_b200.benchmarks import parity
 
@@ -53,3 +55,12 @@ def test_loss_curve_matches_reference(name):
     assert max(abs(x - y) for x, y in zip(ours, g["ours_losses"])) < 5e-3
     # optimizer state: same parameters, same state keys, same shapes as the reference
     assert res["state_layout"] == g["reference_state_layout"]
+    if "reference_mean_ranks" in g:
+        # adaptive rank: the mean active rank follows the reference's schedule
+        # (within the spread of the reference's own seeds, and at most one
+        # rank step of 16 apart at the end)
+        refs_r = g["reference_mean_ranks"]
+        ours_r = res["mean_ranks"]
+        r_spread = max((max(abs(x - y) for x, y in zip(refs_r[0], r)) for r in refs_r[1:]), default=0.0)
+        r_dev = min(max(abs(x - y) for x, y in zip(ours_r, r)) for r in refs_r)
+        assert r_dev <= max(3.0 * r_spread, 16.0), (r_dev, r_spread)
