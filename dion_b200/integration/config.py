@@ -30,6 +30,7 @@ __all__ = [
     "DataConfig",
     "ValidatorConfig",
     "ProfilingConfig",
+    "DebugConfig",
     "JobConfig",
     "apply_overrides",
 ]
@@ -46,6 +47,7 @@ class ModelConfig:
 @dataclass
 class TrainingConfig:
     local_batch_size: int = 8
+    global_batch_size: int = -1  # > local x data-parallel degree: gradient accumulation
     seq_len: int = 2048
     steps: int = 10000
     dtype: str = "bfloat16"
@@ -119,6 +121,14 @@ class ProfilingConfig:
 
 
 @dataclass
+class DebugConfig:
+    # torchtitan's [debug] section: ``--debug.seed`` (taking precedence over
+    # training.seed) and ``--debug.deterministic``
+    seed: int = 0
+    deterministic: bool = False
+
+
+@dataclass
 class JobConfig:
     model: ModelConfig = field(default_factory=ModelConfig)
     optimizer: HybridOptimizersContainer.Config = field(default_factory=HybridOptimizersContainer.Config)
@@ -131,6 +141,7 @@ class JobConfig:
     dataloader: DataConfig = field(default_factory=DataConfig)
     validator: ValidatorConfig = field(default_factory=ValidatorConfig)
     profiling: ProfilingConfig = field(default_factory=ProfilingConfig)
+    debug: DebugConfig = field(default_factory=DebugConfig)
 
     def to_dict(self) -> Dict[str, Any]:
         return dataclasses.asdict(self)

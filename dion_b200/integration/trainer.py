@@ -66,6 +66,10 @@ class TrainerConfig:
     data_bytes_per_token: int = 0  # raw token files only (files with a header carry it)
     # held-out token files for ``validate`` ("" = none)
     val_dataset: str = ""
+    # sequences per optimizer step over all data-parallel ranks; a multiple of
+    # local_batch_size x the data-parallel degree, the quotient being the number
+    # of accumulated micro-batches (-1: no accumulation)
+    global_batch_size: int = -1
 
 
 def lr_lambda(step: int, warmup: int, total: int, min_factor: float) -> float:
@@ -171,8 +175,18 @@ class Trainer:
         tp, pp = max(1, cfg.tp), max(1, cfg.pp)
         per_stage = self.world // pp
         self.data_rank, self.data_world = (self.rank % per_stage) // tp, per_stage // tp
+        self.grad_accum = 1
+        if cfg.global_batch_size and cfg.global_batch_size > 0:
+            per_pass = cfg.local_batch_size * self.data_world
+            if cfg.global_batch_size % per_pass:
+                raise ValueError(f"global_batch_size {cfg.global_batch_size} is not a multiple of local_batch_size x "
+                                 f"data-parallel degree = {per_pass}")
+            self.grad_accum = cfg.global_batch_size // per_pass
+            if self.grad_accum > 1 and cfg.pp > 1:
+                raise ValueError("with pipeline parallelism set pp_microbatches instead of gradient accumulation")
+        # each step reads grad_accum micro-batches of local_batch_size sequences
         self.data = build_loader(cfg.dataset, vocab=mcfg.vocab_size, seq_len=cfg.seq_len,
-                                 local_batch=cfg.local_batch_size, seed=cfg.seed, rank=self.data_rank,
+                                 local_batch=cfg.local_batch_size * self.grad_accum, seed=cfg.seed, rank=self.data_rank,
                                  world=self.data_world, shuffle=cfg.data_shuffle, prefetch=cfg.data_prefetch,
                                  bytes_per_token=cfg.data_bytes_per_token)
         self.val_data = None
@@ -211,6 +225,28 @@ class Trainer:
             torch.distributed.all_reduce(loss, group=sp.group)
         return loss
 
+    def _accumulate(self, tokens: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
+        """Gradient accumulation: the step's rows as ``grad_accum`` micro-batches
+        (FSDP reduce-scatters each micro-batch's gradients into the sharded
+        accumulators), each loss scaled by 1 / grad_accum; the TP sum of
+        replicated parameters' gradients runs once, after the last. Returns
+        the step's mean loss."""
+        n = self.grad_accum
+        total = None
+        for t, l in zip(tokens.chunk(n), labels.chunk(n)):
+            loss = self.model.loss(t, l)
+            (loss / n).backward()
+            d = loss.detach() / n
+            total = d if total is None else total + d
+        sp = getattr(self.model, "sp", None)
+        if sp is not None:
+            from ..parallel.tp import sp_sync_replicated_grads
+
+            sp_sync_replicated_grads(self.model, sp.group)
+            total = total.clone()
+            torch.distributed.all_reduce(total, group=sp.group)
+        return total
+
     def train_step(self, tokens: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
         """One optimisation step on a host (or device) batch; returns the device loss."""
         tokens = tokens.to(self.device, non_blocking=True)
@@ -218,6 +254,8 @@ class Trainer:
         self._set_lr()
         if self.pp_runner is not None:
             loss = self.pp_runner.step(tokens, labels)
+        elif self.grad_accum > 1:
+            loss = self._accumulate(tokens, labels)
         else:
             loss = self.forward_backward(tokens, labels)
         if self.cfg.max_norm and self.cfg.max_norm > 0:

@@ -45,7 +45,7 @@ def trainer_config_from_job(job: JobConfig) -> TrainerConfig:
         warmup_steps=job.lr_scheduler.warmup_steps,
         min_lr_factor=job.lr_scheduler.min_lr_factor,
         max_norm=job.training.max_norm,
-        seed=job.training.seed if job.training.seed else job.dataloader.seed,
+        seed=job.debug.seed or job.training.seed or job.dataloader.seed,
         init_mode=job.model.init,
         dp_replicate=par.data_parallel_replicate_degree,
         dp_shard=par.data_parallel_shard_degree,
@@ -62,6 +62,7 @@ def trainer_config_from_job(job: JobConfig) -> TrainerConfig:
         data_prefetch=job.dataloader.prefetch,
         data_bytes_per_token=job.dataloader.bytes_per_token,
         val_dataset=job.validator.dataset if job.validator.enable else "",
+        global_batch_size=job.training.global_batch_size,
     )
 
 
@@ -119,6 +120,9 @@ def main(argv: Optional[List[str]] = None) -> List[float]:
         raise SystemExit(f"unrecognised arguments: {leftover}")
     if job.validator.enable and not job.validator.dataset:
         raise SystemExit("--validator.enable needs held-out token files: --validator.dataset PATH")
+    if job.debug.deterministic:
+        torch.use_deterministic_algorithms(True, warn_only=True)
+        torch.backends.cudnn.benchmark = False
     tc = trainer_config_from_job(job)
     tr = Trainer(tc)
     from .benchmarks.metrics_collector import OptimizerMetricsCollector
@@ -135,7 +139,7 @@ def main(argv: Optional[List[str]] = None) -> List[float]:
         ckpt.maybe_load(tr)
     prof = _profiler(job, tr)
     flops_tok = tr.model_cfg.flops_per_token(tc.seq_len)
-    tokens_step = tc.local_batch_size * tc.seq_len
+    tokens_step = tc.local_batch_size * tr.grad_accum * tc.seq_len
     losses: List[float] = []
     t_last = time.perf_counter()
     for step in range(tr.step_idx, tc.steps):

@@ -325,3 +325,62 @@ def test_train_entry_writes_profiler_traces(tmp_path):
     assert got == ["iteration_2", "iteration_4"], got
     res = parse_profiler_trace(str(folder / "iteration_4" / "rank0_trace.json"))
     assert isinstance(res, dict) and res
+
+
+def _accum_body(local, global_batch, rank, world):
+    from dion_b200.integration.hybrid_optimizer import HybridOptimizersContainer
+    from dion_b200.integration.trainer import Trainer, TrainerConfig
+
+    cfg = TrainerConfig(model="tiny", model_overrides=dict(n_layers=2, vocab_size=512, max_seq_len=64), seq_len=32,
+                        local_batch_size=local, global_batch_size=global_batch, steps=3, warmup_steps=0,
+                        dp_shard=world, optimizer=HybridOptimizersContainer.Config(name="Muon", lr=0.02), seed=3)
+    torch.manual_seed(0)
+    tr = Trainer(cfg, device=torch.device("cpu"))
+    assert tr.grad_accum == global_batch // (local * world)
+    out = []
+    for _ in range(3):
+        loss = tr.train_step(*tr.data.next()).detach().clone()
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(loss)
+            loss /= world
+        out.append(float(loss))
+    return out
+
+
+@pytest.mark.parametrize("world", [1, 2])
+def test_gradient_accumulation_matches_full_batch(world):
+    """global_batch_size = 2 x local x data-parallel degree accumulates two
+    micro-batches per step and trains like one step on the whole batch."""
+    import functools
+
+    from test_distributed_cpu import spawn
+
+    full = spawn(functools.partial(_accum_body, 4 // world, 4), world=world)
+    acc = spawn(functools.partial(_accum_body, 2 // world, 4), world=world)
+    for out in (full, acc):
+        for r, (status, res) in out.items():
+            assert status == "ok", res
+    a, b = torch.tensor(full[0][1]), torch.tensor(acc[0][1])
+    assert torch.allclose(a, b, rtol=1e-4, atol=1e-4), (a, b)
+
+
+def test_global_batch_must_divide():
+    from dion_b200.integration.trainer import Trainer, TrainerConfig
+
+    with pytest.raises(ValueError, match="multiple"):
+        Trainer(TrainerConfig(model="tiny", seq_len=16, local_batch_size=3, global_batch_size=4, steps=1),
+                device=torch.device("cpu"))
+
+
+def test_debug_seed_and_global_batch_flags():
+    """The reference's command lines use --debug.seed and
+    --training.global-batch-size; both map onto the trainer."""
+    from dion_b200.integration.config_registry import get_config
+    from dion_b200.train import trainer_config_from_job
+
+    job = get_config("llama3_debug_muon")
+    assert apply_overrides(job, ["--debug.seed", "42", "--training.global-batch-size", "64"]) == []
+    tc = trainer_config_from_job(job)
+    assert tc.seed == 42 and tc.global_batch_size == 64
