@@ -90,6 +90,8 @@ class CheckpointConfig:
 class MetricsConfig:
     log_freq: int = 10
     enable_tensorboard: bool = False
+    save_tb_folder: str = "tb"
+    # W&B: project / run name / mode from WANDB_PROJECT, WANDB_RUN_NAME, WANDB_MODE
     enable_wandb: bool = False
     save_jsonl: Optional[str] = None
 

@@ -128,8 +128,21 @@ def main(argv: Optional[List[str]] = None) -> List[float]:
     from .benchmarks.metrics_collector import OptimizerMetricsCollector
 
     collector = None
-    if job.metrics.save_jsonl and tr.rank == 0:
-        collector = OptimizerMetricsCollector(tr.optimizers, output_dir=job.metrics.save_jsonl)
+    tb = wb = None
+    if tr.rank == 0:
+        mc = job.metrics
+        if mc.enable_tensorboard:
+            from torch.utils.tensorboard import SummaryWriter
+
+            tb = SummaryWriter(log_dir=mc.save_tb_folder)
+        if mc.enable_wandb:
+            import wandb
+
+            wb = wandb.init(project=os.environ.get("WANDB_PROJECT", "dion_b200"), name=os.environ.get("WANDB_RUN_NAME"),
+                            config=job.to_dict())
+        if mc.save_jsonl or tb is not None or wb is not None:
+            collector = OptimizerMetricsCollector(tr.optimizers, output_dir=mc.save_jsonl or mc.save_tb_folder,
+                                                  tb_writer=tb, wandb_run=wb)
     ckpt = None
     if job.checkpoint.enable:
         from .checkpoint import CheckpointManager
@@ -175,6 +188,12 @@ def main(argv: Optional[List[str]] = None) -> List[float]:
             prof.step()
     if prof is not None:
         prof.__exit__(None, None, None)
+    if collector is not None:
+        collector.close()
+    if tb is not None:
+        tb.close()
+    if wb is not None:
+        wb.finish()
     if dist.is_initialized():
         dist.barrier()
     return losses

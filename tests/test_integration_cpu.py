@@ -384,3 +384,22 @@ def test_debug_seed_and_global_batch_flags():
     assert apply_overrides(job, ["--debug.seed", "42", "--training.global-batch-size", "64"]) == []
     tc = trainer_config_from_job(job)
     assert tc.seed == 42 and tc.global_batch_size == 64
+
+
+def test_train_entry_tensorboard(tmp_path):
+    """--metrics.enable_tensorboard writes the step metrics as TensorBoard events."""
+    pytest.importorskip("tensorboard")
+    from dion_b200 import train
+
+    tb = tmp_path / "tb"
+    train.main(["--config", "llama3_debug_muon", "--training.steps", "2", "--training.seq_len", "32",
+                "--training.local_batch_size", "2", "--metrics.log_freq", "1", "--metrics.enable_tensorboard",
+                "--metrics.save_tb_folder", str(tb)])
+    events = [p for p in tb.iterdir() if p.name.startswith("events.out.tfevents")]
+    assert events and events[0].stat().st_size > 0
+    from tensorboard.backend.event_processing.event_accumulator import EventAccumulator
+
+    acc = EventAccumulator(str(tb))
+    acc.Reload()
+    assert "optimizer/loss" in acc.Tags()["scalars"]
+    assert [e.step for e in acc.Scalars("optimizer/loss")] == [1, 2]
