@@ -403,3 +403,24 @@ def test_train_entry_tensorboard(tmp_path):
     acc.Reload()
     assert "optimizer/loss" in acc.Tags()["scalars"]
     assert [e.step for e in acc.Scalars("optimizer/loss")] == [1, 2]
+
+
+@pytest.mark.parametrize("experiment,count", [("perf", 5), ("convergence", 15), ("dion2", 3), ("adadion", 48),
+                                              ("anchor", 6), ("sdion", 8)])
+def test_experiment_launcher_runs_parse(experiment, count):
+    """Every run the experiment launcher would start names a registered
+    config and only overrides that the CLI accepts."""
+    import shlex
+    import subprocess
+
+    script = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "dion_b200", "launch",
+                          "run_experiments.sh")
+    env = dict(os.environ, DRY_RUN="1", VAL_DATA="val.bin", TRAIN_DATA="train/")
+    out = subprocess.run(["bash", script, experiment], capture_output=True, text=True, env=env, check=True).stdout
+    runs = [l for l in out.splitlines() if l.startswith("DRY_RUN")]
+    assert len(runs) == count
+    for line in runs:
+        head, _, args = line.partition(" args=")
+        fields = dict(kv.split("=", 1) for kv in head.split()[1:])
+        job = get_config(f"llama3_{fields['model']}_{fields['optimizer']}")
+        assert apply_overrides(job, shlex.split(args)) == [], line
