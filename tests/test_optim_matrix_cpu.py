@@ -120,3 +120,30 @@ def test_mixed_groups_route_scalars_to_adamw_and_lion(cls, kw):
     assert not torch.equal(bias, b0) and not torch.equal(norm, n0)
     # Lion's sign update moves each coordinate by at most lr per step (plus decoupled decay)
     assert float((norm - n0).detach().abs().max()) <= 2 * 1e-3 * 1.1
+
+
+def _state_bytes(opt):
+    n = 0
+    for st in opt.state.values():
+        for v in st.values():
+            if isinstance(v, torch.Tensor):
+                n += v.numel() * v.element_size()
+    return n
+
+
+@pytest.mark.parametrize("cls,kw", ALL, ids=IDS)
+def test_state_does_not_grow_over_steps(cls, kw):
+    """Stress check: after warm-up the optimizer state (and the optimizer's
+    own caches) stay the same size however many steps run."""
+    torch.manual_seed(6)
+    params = [nn.Parameter(torch.randn(s)) for s in [(32, 16), (16, 32), (24, 24), (24, 24)]]
+    opt = cls(params, **kw)
+    for i in range(12):
+        _step(opt, params, i)
+    size = _state_bytes(opt)
+    caches = {k: len(v) for k, v in vars(opt).items() if isinstance(v, (dict, list)) and k != "param_groups"}
+    for i in range(12, 60):
+        _step(opt, params, i)
+    assert _state_bytes(opt) <= size
+    later = {k: len(v) for k, v in vars(opt).items() if isinstance(v, (dict, list)) and k != "param_groups"}
+    assert later == caches, (caches, later)
