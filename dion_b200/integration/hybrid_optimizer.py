@@ -166,7 +166,29 @@ class HybridOptimizersContainer(Optimizer):
             return optim.SDion(groups, device_mesh=shard_mesh, lr=cfg.lr, mu=cfg.mu, init_rank=cfg.init_rank,
                          rank_min=cfg.rank_min, rank_max=cfg.rank_max, qbuf_max_cols=cfg.qbuf_max_cols,
                          weight_decay=cfg.weight_decay, **mode_kw)
-        raise ValueError(f"Unknown matrix optimizer: {name!r}. Supported: 'AdamW', 'Muon', 'Dion', 'Dion2', 'AdaDion', 'AdaDionV2'")
+        # the research variants by class name (the reference container reaches only SDion, as "AdaDion")
+        lowrank = dict(device_mesh=shard_mesh, lr=cfg.lr, mu=cfg.mu, init_rank=cfg.init_rank, rank_min=cfg.rank_min,
+                       rank_max=cfg.rank_max, qbuf_max_cols=cfg.qbuf_max_cols, weight_decay=cfg.weight_decay)
+        if name == "AdaDionAnchor":  # the plain AdaDion class (ANCHOR-MBP)
+            return optim.AdaDion(groups, adaptive_rank=cfg.adaptive_rank, erank_ema_beta=cfg.erank_ema_beta,
+                                 rho=cfg.rho, rank_quantize=cfg.rank_quantize, rank_warmup_steps=cfg.rank_warmup_steps,
+                                 warmup_rank=cfg.warmup_rank, rank_step_up=cfg.rank_step_up,
+                                 rank_step_down=cfg.rank_step_down, use_quality_control=cfg.use_quality_control,
+                                 aerr_ema_beta=cfg.aerr_ema_beta, aerr_target=cfg.aerr_target,
+                                 aerr_up_margin=cfg.aerr_up_margin, aerr_down_margin=cfg.aerr_down_margin,
+                                 use_anchor=cfg.use_anchor, anchor_alpha=cfg.anchor_alpha,
+                                 anchor_period=cfg.anchor_period, **lowrank)
+        if name == "SDion":
+            return optim.SDion(groups, **lowrank)
+        if name == "GSDion":
+            return optim.GSDion(groups, use_anchor=cfg.use_anchor, anchor_alpha=cfg.anchor_alpha,
+                                anchor_period=cfg.anchor_period, **lowrank)
+        if name == "AGDion":
+            return optim.AGDion(groups, use_anchor=cfg.use_anchor, anchor_alpha=cfg.anchor_alpha, **lowrank)
+        if name == "QCDion":
+            return optim.QCDion(groups, **lowrank)
+        raise ValueError(f"Unknown matrix optimizer: {name!r}. Supported: 'AdamW', 'Muon', 'Dion', 'Dion2', 'AdaDion', "
+                         "'AdaDionV2', 'AdaDionAnchor', 'SDion', 'GSDion', 'AGDion', 'QCDion'")
 
     def __iter__(self) -> Iterator[Optimizer]:
         return iter(self.optimizers)

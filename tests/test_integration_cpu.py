@@ -424,3 +424,31 @@ def test_experiment_launcher_runs_parse(experiment, count):
         fields = dict(kv.split("=", 1) for kv in head.split()[1:])
         job = get_config(f"llama3_{fields['model']}_{fields['optimizer']}")
         assert apply_overrides(job, shlex.split(args)) == [], line
+
+
+def _variant_body(name, rank, world):
+    from dion_b200.integration.hybrid_optimizer import HybridOptimizersContainer
+    from dion_b200.integration.trainer import Trainer, TrainerConfig
+
+    cfg = TrainerConfig(model="tiny", model_overrides=dict(n_layers=2, vocab_size=512, max_seq_len=64), seq_len=32,
+                        local_batch_size=2, steps=3, warmup_steps=0, dp_shard=world,
+                        optimizer=HybridOptimizersContainer.Config(name=name, lr=0.02, init_rank=8, rank_min=4,
+                                                                   rank_max=32, warmup_rank=16), seed=1)
+    torch.manual_seed(0)
+    tr = Trainer(cfg, device=torch.device("cpu"))
+    assert type(tr.optimizers.optimizers[0]).__name__ == {"AdaDionAnchor": "AdaDion"}.get(name, name)
+    return [float(tr.train_step(*tr.data.next())) for _ in range(3)]
+
+
+@pytest.mark.parametrize("name", ["AdaDionAnchor", "SDion", "GSDion", "AGDion", "QCDion"])
+def test_container_trains_research_variants(name):
+    """The research variants are selectable by name (--optimizer.name) and
+    train under FSDP over 2 ranks."""
+    import functools
+
+    from test_distributed_cpu import spawn
+
+    out = spawn(functools.partial(_variant_body, name), world=2)
+    for r, (status, res) in out.items():
+        assert status == "ok", res
+        assert all(math.isfinite(v) for v in res)
