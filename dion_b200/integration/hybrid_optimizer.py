@@ -157,6 +157,9 @@ class HybridOptimizersContainer(Optimizer):
                              rank_quantize=cfg.rank_quantize, rank_step_up=cfg.rank_step_up,
                              rank_step_down=cfg.rank_step_down, erank_ema_beta=cfg.erank_ema_beta)
         if name == "AdaDion":
+            if tp_mesh is not None:
+                raise ValueError("AdaDion (SDion) supports data-parallel layouts (DDP / FSDP); it has no "
+                                 "tensor-parallel path")
             mode_kw = {
                 "baseline": dict(enable_skip=False, enable_consensus=False, enable_anchor=False, enable_recovery=False),
                 "skip": dict(enable_skip=True, enable_consensus=False, enable_anchor=False, enable_recovery=True),
@@ -167,6 +170,8 @@ class HybridOptimizersContainer(Optimizer):
                          rank_min=cfg.rank_min, rank_max=cfg.rank_max, qbuf_max_cols=cfg.qbuf_max_cols,
                          weight_decay=cfg.weight_decay, **mode_kw)
         # the research variants by class name (the reference container reaches only SDion, as "AdaDion")
+        if tp_mesh is not None and name in ("AdaDionAnchor", "SDion", "GSDion", "AGDion", "QCDion"):
+            raise ValueError(f"{name} supports data-parallel layouts (DDP / FSDP); it has no tensor-parallel path")
         lowrank = dict(device_mesh=shard_mesh, lr=cfg.lr, mu=cfg.mu, init_rank=cfg.init_rank, rank_min=cfg.rank_min,
                        rank_max=cfg.rank_max, qbuf_max_cols=cfg.qbuf_max_cols, weight_decay=cfg.weight_decay)
         if name == "AdaDionAnchor":  # the plain AdaDion class (ANCHOR-MBP)

@@ -103,7 +103,10 @@ class AdaDionV2(Dion):
 
     # ------------------------------------------------------------------ state
     def _bind_arena(self, params, order, mom_arena, q_arena, cfg, q_shape) -> None:
-        if not self._adaptive_rank:
+        if not self._adaptive_rank or cfg.inner_shard_mesh_dim is not None:
+            # matrices sharded over an inner (TP) mesh keep the fixed rank r_cap: the
+            # FSDP x TP update takes no active rank (nor does the reference's,
+            # ada_dion/optim/adadion_v2.py:1298-1448, which ignores r_list)
             return super()._bind_arena(params, order, mom_arena, q_arena, cfg, q_shape)
         key = tuple(id(p) for p in params)
         r_cap = q_shape[1]

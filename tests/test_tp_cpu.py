@@ -46,7 +46,7 @@ def test_fsdp_tp_matches_dp(optimizer):
     assert torch.allclose(a, b, rtol=2e-3, atol=2e-3), (a, b)
 
 
-@pytest.mark.parametrize("optimizer", ["AdamW", "Dion"])
+@pytest.mark.parametrize("optimizer", ["AdamW", "Dion", "AdaDionV2"])
 def test_fsdp_tp_trains(optimizer):
     got = spawn(_train(optimizer, 2, 2), world=4)
     for r in got.values():
@@ -104,3 +104,18 @@ def test_fsdp_tp_checkpoint_resume(tmp_path, optimizer, load_layout):
     assert loaded[0][0] == "ok", loaded[0][1]
     a, b = torch.tensor(saved[0][1]), torch.tensor(loaded[0][1])
     assert torch.allclose(a, b, rtol=2e-3, atol=2e-3), (a, b)
+
+
+def _lowrank_tp_body(rank, world):
+    try:
+        _train_body("SDion", 1, 2, rank, world)
+    except ValueError as e:
+        return [str(e)]
+    return ["no error"]
+
+
+def test_adadion_family_rejects_tensor_parallelism():
+    out = spawn(_lowrank_tp_body, world=2)
+    for r in out.values():
+        assert r[0] == "ok", r[1]
+        assert "tensor-parallel" in r[1][0], r[1]
