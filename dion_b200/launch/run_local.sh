@@ -16,7 +16,7 @@ run_test() {
     echo "--- $1: OK ---"
 }
 if [ "$WHICH" = "all" ]; then
-    for o in muon dion dion2 adamw adadion; do run_test "llama3_debug_$o"; done
+    for o in muon dion dion2 adamw adadion adadion_v2; do run_test "llama3_debug_$o"; done
 else
     run_test "llama3_debug_$WHICH"
 fi
