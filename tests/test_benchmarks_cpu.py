@@ -210,3 +210,15 @@ def test_step_trace_summary():
     assert s["kernels"] == 3
     assert abs(s["span_ms"] - 0.22) < 1e-9 and abs(s["idle_ms"] - 0.05) < 1e-9
     assert s["by_owner_ms"] == {"cuBLAS": 0.1, "dion_b200": 0.05, "cuDNN": 0.04}
+
+
+def test_layout_check_reports_each_combination():
+    """The layout checker trains an optimizer on a 2-rank layout (gloo) and
+    reports combinations an optimizer declines as unsupported."""
+    from dion_b200.benchmarks import layout_check
+
+    rows = layout_check.main(["--layouts", "1x2x1x1,1x1x2x1", "--optimizers", "Muon,SDion", "--steps", "2"])
+    got = {(r["layout"], r["optimizer"]): r["status"] for r in rows}
+    assert got == {("1x2x1x1", "Muon"): "ok", ("1x2x1x1", "SDion"): "ok",
+                   ("1x1x2x1", "Muon"): "ok", ("1x1x2x1", "SDion"): "unsupported"}, got
+    assert all(len(r["losses"]) == 2 for r in rows if r["status"] == "ok")
