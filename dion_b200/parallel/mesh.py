@@ -57,6 +57,16 @@ def init_distributed(backend: Optional[str] = None, timeout_s: float = 300.0) ->
             kw["store"] = dist.HashStore()
             kw["rank"] = 0
             kw["world_size"] = 1
+        restart = int(os.environ.get("TORCHELASTIC_RESTART_COUNT", "0") or 0)
+        if world > 1 and restart > 0 and "MASTER_ADDR" in os.environ:
+            # an elastic restart: the launcher's store still holds the failed attempt's
+            # process-group keys (peer addresses, communicator ids), which a rank could
+            # read before its new peer overwrites them; key this attempt apart
+            agent_store = os.environ.get("TORCHELASTIC_USE_AGENT_STORE") == "True"
+            base = dist.TCPStore(os.environ["MASTER_ADDR"], int(os.environ["MASTER_PORT"]), world,
+                                 is_master=not agent_store and rank == 0,
+                                 timeout=datetime.timedelta(seconds=timeout_s))
+            kw.update(store=dist.PrefixStore(f"dion_b200/attempt_{restart}", base), rank=rank, world_size=world)
         dist.init_process_group(backend=backend, timeout=datetime.timedelta(seconds=timeout_s), **kw)
     return rank, world, local
 

@@ -2,6 +2,7 @@
 all-zero gradients, checkpoint world-size mismatches, and ranks that stall
 or leave between steps. (A rank that raises is covered in
 test_distributed_cpu.py.)"""
+import os
 import time
 
 import pytest
@@ -111,3 +112,33 @@ def test_rank_leaving_between_steps_times_out():
     out = spawn(_leaver)
     assert out[1] == ("ok", "left")
     assert out[0][0] == "err" and "peer left" in out[0][1]
+
+
+def test_elastic_restart_resumes_from_checkpoint(tmp_path):
+    """A rank that raises mid-run (host-side) ends the attempt; torchrun's
+    elastic agent restarts every rank and the job resumes from its last
+    checkpoint and finishes (gloo, 2 ranks)."""
+    import socket
+    import subprocess
+    import sys
+
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    here = os.path.dirname(os.path.abspath(__file__))
+    ck = tmp_path / "ck"
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2", "--max-restarts=1",
+           "--master-addr", "127.0.0.1", "--master-port", str(port), os.path.join(here, "elastic_worker.py"),
+           "--config", "llama3_debug_muon", "--training.steps", "4", "--training.seq_len", "32",
+           "--training.local_batch_size", "2", "--metrics.log_freq", "1", "--checkpoint.enable",
+           "--checkpoint.folder", str(ck), "--checkpoint.interval", "2", "--checkpoint.no-last_save_model_only"]
+    env = dict(os.environ, PYTHONPATH=os.path.dirname(here), CUDA_VISIBLE_DEVICES="")
+    res = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=300)
+    log = res.stdout + res.stderr
+    assert res.returncode == 0, log[-3000:]
+    assert "injected host-side failure" in log
+    steps = [int(l.split()[1]) for l in res.stdout.splitlines() if l.startswith("step:")]
+    # attempt 1 logs steps 1-2 (then rank 1 fails); attempt 2 resumes at step 2 and logs 3-4
+    assert steps == [1, 2, 3, 4], steps
+    assert (ck / "step-2").exists() and (ck / "step-4").exists()
