@@ -125,6 +125,10 @@ class Trainer:
         shard_mesh = replicate_mesh = None
         dims = ParallelDims(cfg.dp_replicate, cfg.dp_shard, cfg.tp, cfg.pp)
         self.dp_mesh = None
+        if not cfg.use_fsdp and self.world // (max(1, cfg.tp) * max(1, cfg.pp)) > 1:
+            # without FSDP nothing would reduce gradients across data-parallel ranks
+            raise ValueError("use_fsdp=False needs a single data-parallel rank; for replicated data "
+                             "parallelism keep FSDP and set dp_replicate (HSDP with dp_shard=1)")
         if cfg.use_fsdp or cfg.pp > 1:
             self.mesh = build_mesh(dims, device.type)
             names = self.mesh.mesh_dim_names

@@ -83,3 +83,23 @@ def test_pipeline_checkpoint_resumes_without_pipeline(tmp_path):
     assert loaded[0][0] == "ok", loaded[0][1]
     a, b = torch.tensor(saved[0][1]), torch.tensor(loaded[0][1])
     assert torch.allclose(a, b, rtol=2e-3, atol=2e-3), (a, b)
+
+
+def _no_fsdp_dp_body(rank, world):
+    from dion_b200.integration.trainer import Trainer, TrainerConfig
+
+    try:
+        Trainer(TrainerConfig(model="tiny", seq_len=16, local_batch_size=2, steps=1, pp=1, use_fsdp=False),
+                device=torch.device("cpu"))
+    except ValueError as e:
+        return [str(e)]
+    return ["no error"]
+
+
+def test_data_parallel_without_fsdp_is_rejected():
+    """Two data-parallel ranks with use_fsdp=False would train unsynchronised
+    replicas; the trainer refuses the layout."""
+    out = spawn(_no_fsdp_dp_body, world=2)
+    for r in out.values():
+        assert r[0] == "ok", r[1]
+        assert "dp_replicate" in r[1][0], r[1]
