@@ -13,12 +13,13 @@ from __future__ import annotations
 
 import os
 import re
-from typing import Any, Dict, Optional
+from typing import Any, Dict, List, Optional, Tuple
 
 import torch
 import torch.distributed as dist
 import torch.distributed.checkpoint as dcp
 from torch.distributed.checkpoint.state_dict import StateDictOptions, get_model_state_dict, set_model_state_dict
+from torch.distributed.tensor import DTensor, distribute_tensor
 
 __all__ = ["CheckpointManager", "save", "load"]
 
@@ -58,6 +59,48 @@ def _has_optimizer_state(path: str) -> bool:
     return any(k.startswith("optimizer.") for k in _metadata_keys(path))
 
 
+def _reoriented_q_entries(opt_sd: Dict[str, Any], path: str) -> List[Tuple[str, Any]]:
+    """Dion-family ``Q`` entries saved on the other side of their matrix.
+
+    Dion keeps Q (rows x rank) on the side of the matrix its sharding
+    dictates, so a layout change (for example FSDP x TP -> one process) can
+    flip it: saved [n, r] where this layout wants [m, r], or the reverse.
+    Those entries are loaded whole (a plain tensor of the saved shape) and
+    converted by :func:`_convert_reoriented_q`; returns (key, this layout's
+    template) pairs."""
+    md = dcp.FileSystemReader(path).read_metadata().state_dict_metadata
+    todo = []
+    for k, t in list(opt_sd.items()):
+        if not (k.startswith("state.") and k.endswith(".Q") and torch.is_tensor(t) and t.dim() == 2):
+            continue
+        meta = md.get("optimizer." + k)
+        saved = tuple(getattr(meta, "size", ()) or ())
+        if len(saved) != 2 or saved == tuple(t.shape) or saved[1] != t.shape[1]:
+            continue
+        local = t.to_local() if isinstance(t, DTensor) else t
+        opt_sd[k] = torch.empty(saved, dtype=t.dtype, device=local.device)
+        todo.append((k, t))
+    return todo
+
+
+def _convert_reoriented_q(opt_sd: Dict[str, Any], todo: List[Tuple[str, Any]]) -> None:
+    """Q on the other side of M: the column-normalised M Q (or M^T Q), the
+    estimate of that side's subspace the power iteration would form next
+    (Dion: P = M Q, then R = M^T orth(P) -> Q). Every rank computes it from
+    the whole M and keeps its own shard."""
+    for k, template in todo:
+        M = opt_sd[k[: -len("Q")] + "momentum"]
+        M = (M.full_tensor() if isinstance(M, DTensor) else M).float()
+        Qs = opt_sd[k].float().to(M.device)
+        P = M @ Qs if Qs.shape[0] == M.shape[1] else M.t() @ Qs
+        Q = (P / P.norm(dim=0, keepdim=True).clamp_min(1e-12)).to(template.dtype)
+        if tuple(Q.shape) != tuple(template.shape):
+            raise ValueError(f"{k}: saved Q {tuple(Qs.shape)} fits neither side of its momentum {tuple(M.shape)}")
+        if isinstance(template, DTensor):
+            Q = distribute_tensor(Q, template.device_mesh, template.placements, src_data_rank=None)
+        opt_sd[k] = Q
+
+
 def load(path: str, model, optimizers=None, data=None) -> int:
     """Load model (and, when the checkpoint has them, optimizer, step and
     data position) state; returns the saved step, 0 for a model-only
@@ -68,14 +111,17 @@ def load(path: str, model, optimizers=None, data=None) -> int:
     keys = set(_metadata_keys(path))
     has_opt = optimizers is not None and any(k.startswith("optimizer.") for k in keys)
     has_data = has_opt and data is not None and "train_state.data_samples" in keys
+    reoriented: List[Tuple[str, Any]] = []
     if has_opt:
         sd["optimizer"] = optimizers.state_dict()
+        reoriented = _reoriented_q_entries(sd["optimizer"], path)
         sd["train_state"] = {"step": torch.tensor(0)}
         if has_data:
             sd["train_state"]["data_samples"] = torch.tensor(0)
     dcp.load(sd, checkpoint_id=path)
     set_model_state_dict(model, sd["model"])
     if has_opt:
+        _convert_reoriented_q(sd["optimizer"], reoriented)
         optimizers.load_state_dict(sd["optimizer"])
         if has_data:
             data.load_state_dict({"samples": int(sd["train_state"]["data_samples"])})

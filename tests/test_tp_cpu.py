@@ -87,10 +87,10 @@ def _ckpt_body(folder, phase, optimizer, dp_shard, tp, rank, world):
 
 
 # Dion keeps Q on the side its sharding dictates (the FSDP x TP layout
-# orients column-parallel matrices differently from one process), so a Dion
-# checkpoint resumes in the layout that wrote it; Muon's state (momentum
-# only) moves to any layout.
-@pytest.mark.parametrize("optimizer,load_layout", [("Muon", (1, 1)), ("Dion", (2, 2))])
+# orients column-parallel matrices differently from one process); loading a
+# checkpoint into a layout that flips a matrix converts its Q to the other
+# side (column-normalised M Q), so the resumed run follows the 2-D run.
+@pytest.mark.parametrize("optimizer,load_layout", [("Muon", (1, 1)), ("Dion", (2, 2)), ("Dion", (1, 1))])
 def test_fsdp_tp_checkpoint_resume(tmp_path, optimizer, load_layout):
     """A checkpoint of the FSDP 2 x TP 2 layout resumes (parameters and
     optimizer state resharded by DCP) and continues with the losses of the
