@@ -57,20 +57,30 @@ class OptimizerMetricsCollector:
 
     @staticmethod
     def _norms(opt) -> Optional[Dict[str, float]]:
+        """Norms of this rank's parameter shards (and of their gradients while
+        they exist: a trainer that clears gradients before collecting gets the
+        parameter norm only)."""
         grads, params = [], []
         for g in opt.param_groups:
             for p in g["params"]:
+                params.append(_local(p).detach())
                 if p.grad is not None:
                     grads.append(_local(p.grad).detach())
-                    params.append(_local(p).detach())
-        if not grads:
+        if not params:
             return None
-        gs = ops.multi_sumsq([t.contiguous() for t in grads]) if grads[0].is_cuda else torch.stack(
-            [t.float().square().sum() for t in grads])
-        ps = ops.multi_sumsq([t.contiguous() for t in params]) if params[0].is_cuda else torch.stack(
-            [t.float().square().sum() for t in params])
-        both = torch.stack([gs.sum(), ps.sum()]).cpu().tolist()
-        return {"grad_norm": both[0] ** 0.5, "param_norm": both[1] ** 0.5}
+
+        def sumsq(ts):
+            if not ts:
+                return torch.zeros((), device=params[0].device)
+            if ts[0].is_cuda:
+                return ops.multi_sumsq([t.contiguous() for t in ts]).sum()
+            return torch.stack([t.float().square().sum() for t in ts]).sum()
+
+        both = torch.stack([sumsq(grads), sumsq(params)]).cpu().tolist()
+        out = {"param_norm": both[1] ** 0.5}
+        if grads:
+            out["grad_norm"] = both[0] ** 0.5
+        return out
 
     def collect(self, step: int, **extra: Any) -> Dict[str, Any]:
         metrics: Dict[str, Any] = {"step": step, "timestamp": time.time()}
@@ -89,9 +99,8 @@ class OptimizerMetricsCollector:
                 for name, val in (vals or {}).items():
                     metrics[f"{prefix}/{label}/{name}"] = val
             n = self._norms(opt)
-            if n is not None:
-                metrics[f"{prefix}/grad_norm"] = n["grad_norm"]
-                metrics[f"{prefix}/param_norm"] = n["param_norm"]
+            for k, v in (n or {}).items():
+                metrics[f"{prefix}/{k}"] = v
         for k, v in metrics.items():
             if k not in ("step", "timestamp"):
                 self._history[k].append(v)

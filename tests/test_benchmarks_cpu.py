@@ -222,3 +222,35 @@ def test_layout_check_reports_each_combination():
     assert got == {("1x2x1x1", "Muon"): "ok", ("1x2x1x1", "SDion"): "ok",
                    ("1x1x2x1", "Muon"): "ok", ("1x1x2x1", "SDion"): "unsupported"}, got
     assert all(len(r["losses"]) == 2 for r in rows if r["status"] == "ok")
+
+
+def test_metrics_collector_records(tmp_path):
+    """One JSONL record per collect(): step, optimizer type, its diagnostics
+    (rank, effective rank, ...), and norms (the gradient norm only while
+    gradients exist)."""
+    import json
+
+    import torch
+
+    from dion_b200.benchmarks.metrics_collector import OptimizerMetricsCollector
+    from dion_b200.optim import AdaDion
+
+    torch.manual_seed(0)
+    p = torch.nn.Parameter(torch.randn(32, 16))
+    opt = AdaDion([p], lr=0.02, init_rank=4, rank_min=2, rank_max=8)
+    col = OptimizerMetricsCollector(opt, output_dir=str(tmp_path))
+    for step in (1, 2):
+        p.grad = torch.randn_like(p)
+        opt.step()
+        rec = col.collect(step, loss=1.0)
+    assert rec["opt_0/type"] == "AdaDion" and rec["loss"] == 1.0
+    assert abs(rec["opt_0/grad_norm"] - float(p.grad.norm())) < 1e-4
+    assert abs(rec["opt_0/param_norm"] - float(p.detach().norm())) < 1e-4
+    assert any(k.startswith("opt_0/rank/") for k in rec)
+    opt.zero_grad(set_to_none=True)
+    rec = col.collect(3)
+    assert "opt_0/grad_norm" not in rec and "opt_0/param_norm" in rec
+    col.close()
+    lines = [json.loads(l) for l in open(tmp_path / "optimizer_metrics.jsonl")]
+    assert [r["step"] for r in lines] == [1, 2, 3]
+    assert col.get_history()["loss"] == [1.0, 1.0]
