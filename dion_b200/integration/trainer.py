@@ -281,13 +281,15 @@ class Trainer:
         the data-parallel ranks; the same value is returned on every rank."""
         if self.val_data is None:
             raise ValueError("no validation dataset configured (TrainerConfig.val_dataset)")
-        if self.pp_runner is not None:
-            raise NotImplementedError("validation with pipeline parallelism is not supported")
         self.val_data.load_state_dict({"samples": 0})
         total = torch.zeros((), device=self.device, dtype=torch.float32)
         for _ in range(steps):
             t, l = self.val_data.next()
-            loss = self.model.loss(t.to(self.device, non_blocking=True), l.to(self.device, non_blocking=True))
+            t, l = t.to(self.device, non_blocking=True), l.to(self.device, non_blocking=True)
+            if self.pp_runner is not None:  # the schedule's forward-only pass; every stage gets the loss
+                total += self.pp_runner.eval(t, l).float()
+                continue
+            loss = self.model.loss(t, l)
             sp = getattr(self.model, "sp", None)
             if sp is not None:  # each TP rank holds its tokens' share of the batch loss
                 loss = loss.detach().clone()

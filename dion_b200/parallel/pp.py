@@ -93,7 +93,23 @@ class PipelineRunner:
             self.schedule.step(target=labels, losses=losses)
         else:
             self.schedule.step()
+        return self._broadcast_loss(losses)
+
+    def _broadcast_loss(self, losses: List[torch.Tensor]) -> torch.Tensor:
         loss = torch.stack(losses).mean().detach() if losses else torch.zeros((), device=self.device)
         # the loss lives on the last stage; every stage reports it
         dist.broadcast(loss, group_src=self.pp_size - 1, group=self.pp_group)
         return loss
+
+    @torch.no_grad()
+    def eval(self, tokens: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
+        """Forward only (the schedule's evaluation pass, no gradients); returns
+        the mean loss on every stage."""
+        losses: List[torch.Tensor] = []
+        if self.pp_rank == 0:
+            self.schedule.eval(tokens)
+        elif self.pp_rank == self.pp_size - 1:
+            self.schedule.eval(target=labels, losses=losses)
+        else:
+            self.schedule.eval()
+        return self._broadcast_loss(losses)

@@ -2,6 +2,7 @@
 alone and with FSDP over 2 data-parallel ranks) reproduces the losses of the
 unpipelined run on the same data."""
 import functools
+import os
 
 import pytest
 import torch
@@ -103,3 +104,36 @@ def test_data_parallel_without_fsdp_is_rejected():
     for r in out.values():
         assert r[0] == "ok", r[1]
         assert "dp_replicate" in r[1][0], r[1]
+
+
+def _val_body(folder, pp, rank, world):
+    from dion_b200.data import write_token_file
+    from dion_b200.integration.hybrid_optimizer import HybridOptimizersContainer
+    from dion_b200.integration.trainer import Trainer, TrainerConfig
+
+    val = os.path.join(folder, "val.bin")
+    if rank == 0 and not os.path.exists(val):
+        write_token_file(val, torch.randint(0, 512, (4000,), generator=torch.Generator().manual_seed(3)))
+    import torch.distributed as dist
+
+    dist.barrier()
+    cfg = TrainerConfig(model="tiny", model_overrides=dict(n_layers=4, vocab_size=512, max_seq_len=64), seq_len=32,
+                        local_batch_size=4, steps=1, warmup_steps=0, dp_shard=1, pp=pp, pp_microbatches=2,
+                        optimizer=HybridOptimizersContainer.Config(name="Muon"), seed=7, use_fsdp=False,
+                        val_dataset=val)
+    torch.manual_seed(0)
+    tr = Trainer(cfg, device=torch.device("cpu"))
+    return [tr.validate(2)]
+
+
+def test_pipeline_validation_matches_unpipelined(tmp_path):
+    """Validation through the pipeline's forward-only schedule gives the
+    unpipelined model's loss, on every stage."""
+
+    one = spawn(functools.partial(_val_body, str(tmp_path), 1), world=1)
+    two = spawn(functools.partial(_val_body, str(tmp_path), 2), world=2)
+    for out in (one, two):
+        for r in out.values():
+            assert r[0] == "ok", r[1]
+    assert two[0][1] == two[1][1]
+    assert abs(one[0][1][0] - two[0][1][0]) < 1e-4, (one[0][1], two[0][1])
