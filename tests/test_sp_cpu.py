@@ -116,3 +116,27 @@ def test_tp_matches_single_process(sequence_parallel):
     b = torch.tensor(got[0][1])
     assert torch.isfinite(b).all()
     assert torch.allclose(a, b, rtol=2e-3, atol=2e-3), (a, b)
+
+
+def _accum_body(local, global_batch, rank, world):
+    from dion_b200.integration.hybrid_optimizer import HybridOptimizersContainer
+    from dion_b200.integration.trainer import Trainer, TrainerConfig
+
+    cfg = TrainerConfig(model="tiny", model_overrides=dict(n_layers=2, vocab_size=512, max_seq_len=64), seq_len=32,
+                        local_batch_size=local, global_batch_size=global_batch, steps=3, warmup_steps=0, dp_shard=1,
+                        tp=2, optimizer=HybridOptimizersContainer.Config(name="Muon", lr=0.02), seed=5)
+    torch.manual_seed(0)
+    tr = Trainer(cfg, device=torch.device("cpu"))
+    return [float(tr.train_step(*tr.data.next())) for _ in range(3)]
+
+
+def test_gradient_accumulation_with_sequence_parallel_tp():
+    """TP 2 (sequence parallel): two accumulated micro-batches of 2 train like
+    one batch of 4 (the TP sum of replicated gradients runs once per step)."""
+    full = spawn(functools.partial(_accum_body, 4, 4), world=2)
+    acc = spawn(functools.partial(_accum_body, 2, 4), world=2)
+    for out in (full, acc):
+        for r, (status, res) in out.items():
+            assert status == "ok", res
+    a, b = torch.tensor(full[0][1]), torch.tensor(acc[0][1])
+    assert torch.allclose(a, b, rtol=1e-4, atol=1e-4), (a, b)
