@@ -1,5 +1,6 @@
-"""Benchmark tiers A (correctness), B (optimizer step timing, see
-optimizer_bench.py) and C (scale experiments), plus the profiler-trace parser.
+"""Benchmark tiers A (correctness), B (optimizer step timing: ``run_tier_b``
+per matrix shape, and optimizer_bench.py for the distributed 96-matrix step)
+and C (scale experiments), plus the profiler-trace parser.
 
 Tier A: single-step invariants of every optimizer (finite, params move,
 state keys), same-seed reproducibility and a distributed sanity run.
@@ -10,6 +11,7 @@ like ada_dion/benchmarks/tier_b_microbench.py:157-217, and also reports this
 package's kernels (``bdion::``) and the cuBLAS/cuDNN ones.
 
     python -m dion_b200.benchmarks.tiers a [--device cuda]
+    python -m dion_b200.benchmarks.tiers b [--device cuda] [--warmup 10 --steps 100]
     python -m dion_b200.benchmarks.tiers c
     python -m dion_b200.benchmarks.tiers trace <trace.json>
 """
@@ -23,7 +25,7 @@ from typing import Any, Dict, List
 
 import torch
 
-__all__ = ["run_tier_a", "generate_c1_fsdp_experiments", "generate_c2_hsdp_experiments",
+__all__ = ["run_tier_a", "run_tier_b", "TIER_B_SHAPES", "generate_c1_fsdp_experiments", "generate_c2_hsdp_experiments",
            "generate_performance_characterization", "experiment_to_cli", "parse_profiler_trace"]
 
 
@@ -68,6 +70,60 @@ def run_tier_a(device: str = "cpu") -> Dict[str, Dict[str, Any]]:
         out[name] = {"finite": finite, "params_changed": moved, "state_initialised": has_state,
                      "bit_exact_same_seed": repro, "pass": finite and moved and has_state and repro}
     return out
+
+
+# ---------------------------------------------------------------- tier B
+TIER_B_SHAPES = [(4096, 4096), (4096, 11008), (11008, 4096)]
+
+
+def run_tier_b(device: str = "cuda", shapes=None, warmup: int = 10, steps: int = 100,
+               dion_rank_fraction: float = 0.25, dion2_fraction: float = 0.25) -> Dict[str, Dict[str, Any]]:
+    """``optimizer.step()`` alone on one bf16 matrix per shape, for AdamW,
+    Muon, Dion and Dion2 (the reference's tier B, with its shapes, learning
+    rates and step counts: ada_dion/benchmarks/tier_b_microbench.py:24-108).
+    AdamW is this package's fused multi-tensor kernel (an ``algorithm:
+    adamw`` group). On CUDA every step is timed with CUDA events; on CPU with
+    the wall clock. Returns {"<m>x<n>": {optimizer: {mean_ms, std_ms, min_ms}}}."""
+    from ..optim import Dion, Dion2, Muon
+
+    configs = [
+        ("AdamW", lambda ps: Muon([{"params": ps, "algorithm": "adamw"}], lr=3e-4, weight_decay=0.1)),
+        ("Muon", lambda ps: Muon(ps, lr=0.02, mu=0.95)),
+        ("Dion", lambda ps: Dion(ps, lr=0.02, rank_fraction=dion_rank_fraction)),
+        ("Dion2", lambda ps: Dion2(ps, lr=0.02, fraction=dion2_fraction)),
+    ]
+    cuda = str(device).startswith("cuda")
+    results: Dict[str, Dict[str, Any]] = {}
+    for m, n in shapes or TIER_B_SHAPES:
+        row = results.setdefault(f"{m}x{n}", {})
+        for name, make in configs:
+            torch.manual_seed(0)
+            p = torch.nn.Parameter(torch.randn(m, n, device=device, dtype=torch.bfloat16))
+            opt = make([p])
+            times = []
+            for i in range(warmup + steps):
+                p.grad = torch.randn_like(p) * 0.01
+                if cuda:
+                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    a.record()
+                    opt.step()
+                    b.record()
+                    b.synchronize()
+                    t = a.elapsed_time(b)
+                else:
+                    import time
+
+                    t0 = time.perf_counter()
+                    opt.step()
+                    t = (time.perf_counter() - t0) * 1e3
+                opt.zero_grad(set_to_none=True)
+                if i >= warmup:
+                    times.append(t)
+            mean = sum(times) / len(times)
+            std = math.sqrt(sum((x - mean) ** 2 for x in times) / max(1, len(times) - 1))
+            row[name] = {"mean_ms": mean, "std_ms": std, "min_ms": min(times)}
+            del opt, p
+    return results
 
 
 # ---------------------------------------------------------------- tier C
@@ -170,14 +226,19 @@ def parse_profiler_trace(trace_path: str) -> Dict[str, Any]:
 
 def main(argv=None):
     p = argparse.ArgumentParser()
-    p.add_argument("tier", choices=["a", "c", "trace"])
+    p.add_argument("tier", choices=["a", "b", "c", "trace"])
     p.add_argument("path", nargs="?")
     p.add_argument("--device", default="cuda" if torch.cuda.is_available() else "cpu")
+    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--steps", type=int, default=100)
     a = p.parse_args(argv)
     if a.tier == "a":
         res = run_tier_a(a.device)
         for k, v in res.items():
             print(f"{k:12s} {'PASS' if v['pass'] else 'FAIL'} {v}")
+    elif a.tier == "b":
+        print(json.dumps({"tier": "b", "device": a.device, "results": run_tier_b(a.device, warmup=a.warmup,
+                                                                                steps=a.steps)}))
     elif a.tier == "c":
         for exp in generate_c1_fsdp_experiments() + generate_c2_hsdp_experiments() + \
                 generate_performance_characterization():

@@ -254,3 +254,13 @@ def test_metrics_collector_records(tmp_path):
     lines = [json.loads(l) for l in open(tmp_path / "optimizer_metrics.jsonl")]
     assert [r["step"] for r in lines] == [1, 2, 3]
     assert col.get_history()["loss"] == [1.0, 1.0]
+
+
+def test_tier_b_times_each_optimizer_per_shape():
+    from dion_b200.benchmarks import tiers
+
+    res = tiers.run_tier_b("cpu", shapes=[(64, 32), (32, 96)], warmup=1, steps=2)
+    assert set(res) == {"64x32", "32x96"}
+    for row in res.values():
+        assert set(row) == {"AdamW", "Muon", "Dion", "Dion2"}
+        assert all(v["mean_ms"] > 0 and v["min_ms"] <= v["mean_ms"] for v in row.values())
