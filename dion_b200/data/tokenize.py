@@ -127,24 +127,59 @@ class _ShardWriter:
         self.buf, self.n = [], 0
 
 
+_WORKER_TOK = None
+
+
+def _worker_init(spec: str) -> None:
+    global _WORKER_TOK
+    _WORKER_TOK = load_tokenizer(spec)
+
+
+def _encode_doc(tok, text: str) -> List[int]:
+    ids = tok.encode(text)
+    if tok.bos_id is not None:
+        ids = [tok.bos_id] + ids
+    if tok.eos_id is not None:
+        ids = ids + [tok.eos_id]
+    return ids
+
+
+def _worker_encode(text: str) -> List[int]:
+    return _encode_doc(_WORKER_TOK, text)
+
+
 def tokenize_to_files(inputs: Sequence[str], output: str, tokenizer="byte", text_field: str = "text",
-                      val_docs: int = 0, shard_tokens: int = 0, max_docs: Optional[int] = None) -> dict:
+                      val_docs: int = 0, shard_tokens: int = 0, max_docs: Optional[int] = None,
+                      workers: int = 1) -> dict:
     """Tokenize ``inputs`` into token files under the prefix ``output``;
-    returns the file lists, token counts and the tokenizer's vocabulary size."""
+    returns the file lists, token counts and the tokenizer's vocabulary size.
+    ``workers`` > 1 (with a tokenizer given by name or path) encodes the
+    documents in that many processes, keeping their order."""
     tok = load_tokenizer(tokenizer) if isinstance(tokenizer, str) else tokenizer
     train = _ShardWriter(output, shard_tokens)
     val = _ShardWriter(output + "-val", shard_tokens)
     docs = 0
-    for text in iter_documents(inputs, text_field):
-        if max_docs is not None and docs >= max_docs:
-            break
-        ids = tok.encode(text)
-        if tok.bos_id is not None:
-            ids = [tok.bos_id] + ids
-        if tok.eos_id is not None:
-            ids = ids + [tok.eos_id]
-        (val if docs < val_docs else train).add(ids)
-        docs += 1
+    texts = iter_documents(inputs, text_field)
+    if max_docs is not None:
+        import itertools
+
+        texts = itertools.islice(texts, max_docs)
+    pool = None
+    if workers > 1 and isinstance(tokenizer, str):
+        import multiprocessing as mp
+
+        pool = mp.get_context("spawn").Pool(workers, initializer=_worker_init, initargs=(tokenizer,))
+        encoded = pool.imap(_worker_encode, texts, chunksize=64)
+    else:
+        encoded = (_encode_doc(tok, t) for t in texts)
+    try:
+        for ids in encoded:
+            (val if docs < val_docs else train).add(ids)
+            docs += 1
+    finally:
+        if pool is not None:
+            pool.close()
+            pool.join()
     train.flush()
     val.flush()
     return {"train": train.files, "val": val.files, "train_tokens": train.total, "val_tokens": val.total,
@@ -160,6 +195,7 @@ def main(argv: Optional[Sequence[str]] = None) -> dict:
     p.add_argument("--val-docs", type=int, default=0, help="first N documents go to the validation files")
     p.add_argument("--shard-tokens", type=int, default=0, help="start a new file after this many tokens")
     p.add_argument("--max-docs", type=int, default=None)
+    p.add_argument("--workers", type=int, default=1, help="tokenizer processes (document order is kept)")
     a = p.parse_args(argv)
     inputs: List[str] = []
     for pat in a.input:
@@ -167,7 +203,8 @@ def main(argv: Optional[Sequence[str]] = None) -> dict:
         if not found:
             raise SystemExit(f"no input matches {pat!r}")
         inputs.extend(found)
-    res = tokenize_to_files(inputs, a.output, a.tokenizer, a.text_field, a.val_docs, a.shard_tokens, a.max_docs)
+    res = tokenize_to_files(inputs, a.output, a.tokenizer, a.text_field, a.val_docs, a.shard_tokens, a.max_docs,
+                            a.workers)
     print(json.dumps(res))
     return res
 

@@ -255,3 +255,16 @@ def test_validation_is_split_over_data_parallel_ranks(tmp_path):
             assert status == "ok", res
     assert two[0][1] == two[1][1]
     assert abs(two[0][1][0] - one[0][1][0]) < 1e-4, (two[0][1], one[0][1])
+
+
+def test_tokenize_with_worker_processes_keeps_order(tmp_path):
+    from dion_b200.data.tokenize import tokenize_to_files
+
+    with open(tmp_path / "d.jsonl", "w") as f:
+        for i in range(300):
+            f.write(json.dumps({"text": f"doc {i} " * (i % 7 + 1)}) + "\n")
+    one = tokenize_to_files([str(tmp_path / "d.jsonl")], str(tmp_path / "one"), "byte")
+    many = tokenize_to_files([str(tmp_path / "d.jsonl")], str(tmp_path / "many"), "byte", workers=3)
+    a = np.fromfile(one["train"][0], dtype="<u2", offset=32)
+    b = np.fromfile(many["train"][0], dtype="<u2", offset=32)
+    assert one["documents"] == many["documents"] == 300 and np.array_equal(a, b)
