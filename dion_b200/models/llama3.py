@@ -76,7 +76,7 @@ class Llama3Config:
 
 
 LLAMA3_CONFIGS: Dict[str, Llama3Config] = {
-    # BASELINE config 1 (CPU): 4 layers, d=256, 4 heads, SwiGLU 1024, vocab 4096
+    # CPU parity / golden-curve model: 4 layers, d=256, 4 heads, SwiGLU 1024, vocab 4096
     "tiny": Llama3Config(dim=256, n_layers=4, n_heads=4, n_kv_heads=4, vocab_size=4096, ffn_dim=1024,
                          rope_theta=10000.0, max_seq_len=256),
     "debug": Llama3Config(dim=256, n_layers=6, n_heads=16, n_kv_heads=16, vocab_size=2048, ffn_dim=768,
