@@ -141,7 +141,37 @@ def _matrix_names(model) -> List[str]:
     return [n for n, p in model.named_parameters() if id(p) in ids]
 
 
+# the research variants: reference module and class for each
+_LOWRANK = {"adadion": ("adadion", "AdaDion"), "sdion": ("sdion", "SDion"), "gsdion": ("gsdion", "GSDion"),
+            "agdion": ("agdion", "AGDion"), "qcdion": ("qcdion", "QCDion")}
+
+
+def _build_lowrank(impl: str, optimizer: str, model, matrix_names, a):
+    """The AdaDion family: matrices on the variant, the rest on its built-in
+    AdamW (``algorithm: adamw`` groups), the same hyper-parameters in both arms."""
+    named = list(model.named_parameters())
+    mats = [p for n, p in named if n in set(matrix_names)]
+    rest = [p for n, p in named if n not in set(matrix_names)]
+    groups = [{"params": mats}, {"params": rest, "algorithm": "adamw", "lr": a.scalar_lr,
+                                 "weight_decay": a.scalar_wd}]
+    mod, cls_name = _LOWRANK[optimizer]
+    if impl == "ours":
+        from .. import optim
+
+        cls = getattr(optim, cls_name)
+    else:
+        if REF_PATH not in sys.path:
+            sys.path.insert(0, REF_PATH)
+        import importlib
+
+        cls = getattr(importlib.import_module(f"ada_dion.optim.{mod}"), cls_name)
+    return cls(groups, lr=a.lr, mu=a.mu, init_rank=a.init_rank, rank_min=a.rank_min, rank_max=a.rank_max,
+               weight_decay=a.wd, adamw_betas=(0.9, 0.95), adamw_eps=1e-8)
+
+
 def _build_optimizer(impl: str, optimizer: str, model, matrix_names, a, mesh=None):
+    if optimizer in _LOWRANK:
+        return _build_lowrank(impl, optimizer, model, matrix_names, a)
     named = list(model.named_parameters())
     groups = _groups(named, set(matrix_names), a.scalar_lr, a.scalar_wd)
     if impl == "ours":
@@ -286,8 +316,9 @@ def compare(ours: List[float], ref: List[float], spread: List[float] = None) -> 
 def parse(argv=None):
     p = argparse.ArgumentParser()
     p.add_argument("--preset", default="tiny")
-    p.add_argument("--optimizer", choices=["dion", "muon", "adadion_v2"], default="dion",
-                   help="adadion_v2: adaptive rank, Q at --rank-fraction, starting at --init-rank-fraction")
+    p.add_argument("--optimizer", choices=["dion", "muon", "adadion_v2"] + sorted(_LOWRANK), default="dion",
+                   help="adadion_v2: adaptive rank, Q at --rank-fraction, starting at --init-rank-fraction; "
+                        "the AdaDion family: --init-rank, --rank-min, --rank-max")
     p.add_argument("--impl", choices=["ours", "reference", "both"], default="both")
     p.add_argument("--device", default="cpu")
     p.add_argument("--dtype", choices=["fp32", "bf16", "mixed"], default="fp32")
@@ -305,6 +336,8 @@ def parse(argv=None):
     p.add_argument("--rank-fraction", type=float, default=0.25)
     p.add_argument("--init-rank-fraction", type=float, default=0.125)
     p.add_argument("--rank-min", type=int, default=8)
+    p.add_argument("--init-rank", type=int, default=32)
+    p.add_argument("--rank-max", type=int, default=64)
     p.add_argument("--scalar-lr", type=float, default=3e-4)
     p.add_argument("--scalar-wd", type=float, default=0.1)
     p.add_argument("--ref-seeds", type=int, default=1, help="reference runs with optimizer seeds 0..n-1")

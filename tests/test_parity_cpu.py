@@ -2,7 +2,9 @@
 (4-layer Llama, d=256, 4 heads, SwiGLU 1024, vocab 4096, seq 256, batch 8,
 fp32, N(0, 0.02) init from seed 0; Dion rank d/4, mu 0.95, lr 0.01 on the
 matrices, AdamW lr 3e-4 / betas 0.9, 0.95 / wd 0.1 on the rest; 50 steps;
-AdaDionV2 with adaptive rank between 1/8 and 1/4 of the matrix side).
+AdaDionV2 with adaptive rank between 1/8 and 1/4 of the matrix side; the
+AdaDion family (AdaDion, SDion, GSDion, AGDion, QCDion) with rank 32 in
+[8, 64] and their built-in AdamW on the rest).
 
 The golden files under tests/golden/ were written by
 ``python -m dion_b200.benchmarks.parity ... --golden`` from runs of the
@@ -30,7 +32,9 @@ def _load(name):
 
 
 @pytest.mark.parametrize("name", ["parity_tiny_dion.json", "parity_tiny_muon.json",
-                                  "parity_tiny_adadion_v2.json"])
+                                  "parity_tiny_adadion_v2.json", "parity_tiny_adadion.json",
+                                  "parity_tiny_sdion.json", "parity_tiny_gsdion.json", "parity_tiny_agdion.json",
+                                  "parity_tiny_qcdion.json"])
 def test_loss_curve_matches_reference(name):
     from dion_b200.benchmarks import parity
 
