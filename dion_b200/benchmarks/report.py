@@ -49,11 +49,17 @@ def load_json_lines(path: str) -> List[dict]:
 
 
 def _parity_entry(path: str) -> dict:
+    """A parity run's output, or a committed golden file (``ours_losses`` /
+    ``reference_losses``, written with ``parity --golden``)."""
     with open(path) as f:
         d = json.load(f)
     cfg = d.get("config", {})
-    arms = {k: {"losses": d[k]["losses"], "seconds": d[k].get("seconds")} for k in ("ours", "reference") if k in d}
-    name = f"{cfg.get('preset', '?')} {cfg.get('optimizer', '?')}"
+    if "ours_losses" in d:
+        arms = {"ours": {"losses": d["ours_losses"], "seconds": None},
+                "reference": {"losses": d["reference_losses"][0], "seconds": None}}
+    else:
+        arms = {k: {"losses": d[k]["losses"], "seconds": d[k].get("seconds")} for k in ("ours", "reference") if k in d}
+    name = f"{cfg.get('preset', '?')} {cfg.get('optimizer', '?')} ({cfg.get('device', '?')})"
     return {"name": name, "config": cfg, "arms": arms, "comparison": d.get("comparison", {})}
 
 
@@ -177,14 +183,16 @@ def main(argv=None) -> None:
     p.add_argument("--parity", nargs="*", default=[])
     p.add_argument("--bench", nargs="*", default=[])
     p.add_argument("--optimizer", nargs="*", default=[])
-    p.add_argument("--data", default=None, help="regenerate from a data.json written by an earlier run")
+    p.add_argument("--data", default=None,
+                   help="start from a data.json written by an earlier run (inputs given here are added)")
     p.add_argument("--out", required=True)
     a = p.parse_args(argv)
-    if a.data:
+    data = collect(a.parity, a.bench, a.optimizer)
+    if a.data:  # an earlier run's data, with this call's inputs added
         with open(a.data) as f:
-            data = json.load(f)
-    else:
-        data = collect(a.parity, a.bench, a.optimizer)
+            old = json.load(f)
+        for k in ("parity", "bench", "optimizer"):
+            data[k] = old.get(k, []) + data[k]
     print(render(data, a.out))
 
 
