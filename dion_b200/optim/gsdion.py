@@ -151,6 +151,11 @@ class GSDion(LowRankOptimizer):
         m_t = alpha_t * c_t * s_t
         lr, wd = g["lr"], g["weight_decay"]
         step_scale = lr * ss * m_t
+        if not math.isfinite(step_scale):
+            # a non-finite momentum (e.g. a NaN gradient) makes the RMS-matched
+            # scale NaN even though the guard zeroed D: skip the update instead
+            # of writing NaN into the weights
+            step_scale = 0.0
         dw_fro = D.float().norm().item() * abs(step_scale)
         dw_rms = _rms(D).item() * abs(step_scale)
 

@@ -147,3 +147,22 @@ def test_state_does_not_grow_over_steps(cls, kw):
     assert _state_bytes(opt) <= size
     later = {k: len(v) for k, v in vars(opt).items() if isinstance(v, (dict, list)) and k != "param_groups"}
     assert later == caches, (caches, later)
+
+
+GUARDED = [(c, kw) for c, kw in ALL if c not in (Muon, Dion2)]
+
+
+@pytest.mark.parametrize("cls,kw", GUARDED, ids=[c.__name__ for c, _ in GUARDED])
+def test_nan_gradient_does_not_reach_the_weights(cls, kw):
+    """The Dion family guards its low-rank update against NaN / Inf (the
+    reference's fix_all_zero_or_nan and NaN zeroing; GSDion also skips a
+    non-finite step scale). Muon and Dion2 have no such guard, like the
+    reference's Muon: a NaN gradient reaches their weights."""
+    torch.manual_seed(7)
+    p = nn.Parameter(torch.randn(16, 8))
+    opt = cls([p], **kw)
+    g = torch.randn(16, 8)
+    g[3, 2] = float("nan")
+    p.grad = g
+    opt.step()
+    assert torch.isfinite(p).all()
