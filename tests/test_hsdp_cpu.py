@@ -76,7 +76,7 @@ def _ckpt_body(folder, phase, optimizer, rank, world):
     return out
 
 
-@pytest.mark.parametrize("optimizer", ["Dion", "Muon"])
+@pytest.mark.parametrize("optimizer", ["Dion", "Muon", "AdaDionV2", "AdaDion"])
 def test_hsdp_checkpoint_resume(tmp_path, optimizer):
     """HSDP 2 x 2: replicas synchronise their state before the save
     (Dion's ``synchronize_for_checkpoint``), and the resumed run continues
