@@ -51,6 +51,10 @@ class TrainingConfig:
     seq_len: int = 2048
     steps: int = 10000
     dtype: str = "bfloat16"
+    # FSDP mixed precision (torchtitan's names): compute dtype of the gathered
+    # parameters, and dtype of the gradient reduction
+    mixed_precision_param: str = "bfloat16"
+    mixed_precision_reduce: str = "float32"
     max_norm: float = 1.0
     seed: int = 0
 

@@ -70,6 +70,10 @@ class TrainerConfig:
     # local_batch_size x the data-parallel degree, the quotient being the number
     # of accumulated micro-batches (-1: no accumulation)
     global_batch_size: int = -1
+    # FSDP mixed precision: dtype of the gathered parameters (compute) and of
+    # the gradient reduction
+    param_dtype: str = "bfloat16"
+    reduce_dtype: str = "float32"
 
 
 def lr_lambda(step: int, warmup: int, total: int, min_factor: float) -> float:
@@ -163,7 +167,8 @@ class Trainer:
         if cfg.use_fsdp and self.dp_mesh is not None:
             # pipeline stages keep their parameters gathered across micro-batches
             # (and the last stage's LM head stays gathered for the loss)
-            apply_fsdp(model, self.dp_mesh, reshard_after_forward=cfg.pp == 1)
+            apply_fsdp(model, self.dp_mesh, param_dtype=getattr(torch, cfg.param_dtype),
+                       reduce_dtype=getattr(torch, cfg.reduce_dtype), reshard_after_forward=cfg.pp == 1)
         if cfg.pp > 1:
             self.pp_runner = PipelineRunner(model, self.mesh["pp"], device, cfg.pp_microbatches or 2 * cfg.pp,
                                             cfg.pp_schedule)

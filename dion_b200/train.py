@@ -63,6 +63,8 @@ def trainer_config_from_job(job: JobConfig) -> TrainerConfig:
         data_bytes_per_token=job.dataloader.bytes_per_token,
         val_dataset=job.validator.dataset if job.validator.enable else "",
         global_batch_size=job.training.global_batch_size,
+        param_dtype=job.training.mixed_precision_param,
+        reduce_dtype=job.training.mixed_precision_reduce,
     )
 
 

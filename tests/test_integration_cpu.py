@@ -452,3 +452,15 @@ def test_container_trains_research_variants(name):
     for r, (status, res) in out.items():
         assert status == "ok", res
         assert all(math.isfinite(v) for v in res)
+
+
+def test_fp32_mixed_precision_flag():
+    """--training.mixed_precision_param float32 trains with fp32 compute (the
+    gathered parameters stay fp32) and gives a loss close to the bf16 run's."""
+    from dion_b200 import train
+
+    base = ["--config", "llama3_debug_muon", "--training.steps", "2", "--training.seq_len", "32",
+            "--training.local_batch_size", "2", "--metrics.log_freq", "1"]
+    bf16 = train.main(base)
+    fp32 = train.main(base + ["--training.mixed_precision_param", "float32"])
+    assert all(math.isfinite(v) for v in fp32) and abs(bf16[0] - fp32[0]) < 0.05, (bf16, fp32)
