@@ -31,6 +31,7 @@ __all__ = [
     "ValidatorConfig",
     "ProfilingConfig",
     "DebugConfig",
+    "CompileConfig",
     "JobConfig",
     "apply_overrides",
 ]
@@ -97,6 +98,8 @@ class MetricsConfig:
     save_tb_folder: str = "tb"
     # W&B: project / run name / mode from WANDB_PROJECT, WANDB_RUN_NAME, WANDB_MODE
     enable_wandb: bool = False
+    wandb_project: Optional[str] = None
+    wandb_run_name: Optional[str] = None
     save_jsonl: Optional[str] = None
 
 
@@ -127,6 +130,15 @@ class ProfilingConfig:
 
 
 @dataclass
+class CompileConfig:
+    # torchtitan's [compile] section, accepted so its command lines carry over:
+    # the model's hot ops are hand-written kernels here, so torch.compile is
+    # not applied and ``enable`` only prints a note
+    enable: bool = False
+    components: str = "model,loss"
+
+
+@dataclass
 class DebugConfig:
     # torchtitan's [debug] section: ``--debug.seed`` (taking precedence over
     # training.seed) and ``--debug.deterministic``
@@ -148,6 +160,7 @@ class JobConfig:
     validator: ValidatorConfig = field(default_factory=ValidatorConfig)
     profiling: ProfilingConfig = field(default_factory=ProfilingConfig)
     debug: DebugConfig = field(default_factory=DebugConfig)
+    compile: CompileConfig = field(default_factory=CompileConfig)
 
     def to_dict(self) -> Dict[str, Any]:
         return dataclasses.asdict(self)
@@ -190,7 +203,7 @@ def apply_overrides(cfg: JobConfig, argv: Sequence[str]) -> List[str]:
         if "=" in key:
             key, val = key.split("=", 1)
         section, name = key.split(".", 1)
-        name = name.replace("-", "_")
+        section, name = section.replace("-", "_"), name.replace("-", "_")
         sec = getattr(cfg, section, None)
         if sec is None:
             rest.append(a)

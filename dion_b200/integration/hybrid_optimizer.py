@@ -95,6 +95,14 @@ class HybridOptimizersContainer(Optimizer):
         anchor_period: int = 50
         sdion_mode: str = "baseline"
         qbuf_max_cols: int = 256
+        # --- Dion2 row selection: "top_l1" or "random" ---
+        selection_method: str = "top_l1"
+        # --- GSDion switches ---
+        rank_normalize: bool = True
+        use_adaptive_scalar: bool = True
+        use_rms_matching: bool = True
+        use_trust_region: bool = True
+        use_residual_rank: bool = True
         # AdaDionV2 (adaptive-rank Dion)
         rank_fraction_max: float = 0.7
         init_rank_fraction: float = 0.25
@@ -148,7 +156,8 @@ class HybridOptimizersContainer(Optimizer):
                         lr=cfg.lr, mu=cfg.mu, rank_fraction=cfg.rank_fraction, weight_decay=cfg.weight_decay)
         if name == "Dion2":
             return optim.Dion2(groups, distributed_mesh=shard_mesh, lr=cfg.lr, fraction=cfg.fraction,
-                         ef_decay=cfg.ef_decay, weight_decay=cfg.weight_decay, tp_mesh=tp_mesh)
+                         ef_decay=cfg.ef_decay, weight_decay=cfg.weight_decay, tp_mesh=tp_mesh,
+                         selection_method=cfg.selection_method)
         if name == "AdaDionV2":
             return optim.AdaDionV2(groups, replicate_mesh=replicate_mesh, outer_shard_mesh=shard_mesh,
                              inner_shard_mesh=tp_mesh, lr=cfg.lr, mu=cfg.mu, weight_decay=cfg.weight_decay,
@@ -187,7 +196,10 @@ class HybridOptimizersContainer(Optimizer):
             return optim.SDion(groups, **lowrank)
         if name == "GSDion":
             return optim.GSDion(groups, use_anchor=cfg.use_anchor, anchor_alpha=cfg.anchor_alpha,
-                                anchor_period=cfg.anchor_period, **lowrank)
+                                anchor_period=cfg.anchor_period, rank_normalize=cfg.rank_normalize,
+                                use_adaptive_scalar=cfg.use_adaptive_scalar, use_rms_matching=cfg.use_rms_matching,
+                                use_trust_region=cfg.use_trust_region, use_residual_rank=cfg.use_residual_rank,
+                                **lowrank)
         if name == "AGDion":
             return optim.AGDion(groups, use_anchor=cfg.use_anchor, anchor_alpha=cfg.anchor_alpha, **lowrank)
         if name == "QCDion":

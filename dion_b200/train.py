@@ -28,7 +28,7 @@ from .integration.config import JobConfig, apply_overrides
 from .integration.config_registry import get_config
 from .integration.trainer import Trainer, TrainerConfig
 
-__all__ = ["trainer_config_from_job", "main"]
+__all__ = ["trainer_config_from_job", "parse_job", "main"]
 
 # bf16 dense peak used for MFU (measured B200 figure is in the bench outputs)
 PEAK_FLOPS = {"bfloat16": 2.25e15}
@@ -107,19 +107,41 @@ def _load_config(module: Optional[str], name: str) -> JobConfig:
     return fn()
 
 
-def main(argv: Optional[List[str]] = None) -> List[float]:
-    argv = list(sys.argv[1:] if argv is None else argv)
+def parse_job(argv: List[str]) -> JobConfig:
+    """The job configuration a command line selects: ``--config`` (and
+    ``--module``), then every ``--section.field value`` override. The
+    reference's torchtitan command lines parse as they are: section and field
+    names may use hyphens, ``--compile.*`` is accepted (torch.compile is not
+    used: the hot ops are hand-written kernels) and ``--hf-assets-path``
+    names the tokenizer assets (the data comes from token files here)."""
     p = argparse.ArgumentParser(add_help=True)
     p.add_argument("--config", required=True)
     p.add_argument("--module", default=None,
                    help="module whose config functions to use (torchtitan-style --module); "
                         "default: dion_b200.integration.config_registry")
     p.add_argument("--job.config_file", dest="unused", default=None)
+    p.add_argument("--hf-assets-path", "--hf_assets_path", dest="hf_assets_path", default=None,
+                   help="tokenizer assets; pass them to `python -m dion_b200.data.tokenize --tokenizer`")
     known, rest = p.parse_known_args(argv)
     job = _load_config(known.module, known.config)
     leftover = apply_overrides(job, rest)
     if leftover:
         raise SystemExit(f"unrecognised arguments: {leftover}")
+    job.hf_assets_path = known.hf_assets_path
+    return job
+
+
+def main(argv: Optional[List[str]] = None) -> List[float]:
+    argv = list(sys.argv[1:] if argv is None else argv)
+    job = parse_job(argv)
+    rank0 = int(os.environ.get("RANK", "0")) == 0
+    if job.compile.enable and rank0:
+        print("note: --compile.enable has no effect (the model's hot ops are hand-written sm_100a kernels)",
+              flush=True)
+    if getattr(job, "hf_assets_path", None) and job.dataloader.dataset == "synthetic" and rank0:
+        print(f"note: --hf-assets-path {job.hf_assets_path}: tokenize the corpus with `python -m "
+              "dion_b200.data.tokenize --tokenizer <that directory>` and pass --dataloader.dataset; "
+              "training on synthetic tokens", flush=True)
     if job.validator.enable and not job.validator.dataset:
         raise SystemExit("--validator.enable needs held-out token files: --validator.dataset PATH")
     if job.debug.deterministic:
@@ -140,8 +162,8 @@ def main(argv: Optional[List[str]] = None) -> List[float]:
         if mc.enable_wandb:
             import wandb
 
-            wb = wandb.init(project=os.environ.get("WANDB_PROJECT", "dion_b200"), name=os.environ.get("WANDB_RUN_NAME"),
-                            config=job.to_dict())
+            wb = wandb.init(project=mc.wandb_project or os.environ.get("WANDB_PROJECT", "dion_b200"),
+                            name=mc.wandb_run_name or os.environ.get("WANDB_RUN_NAME"), config=job.to_dict())
         if mc.save_jsonl or tb is not None or wb is not None:
             collector = OptimizerMetricsCollector(tr.optimizers, output_dir=mc.save_jsonl or mc.save_tb_folder,
                                                   tb_writer=tb, wandb_run=wb)

@@ -464,3 +464,33 @@ def test_fp32_mixed_precision_flag():
     bf16 = train.main(base)
     fp32 = train.main(base + ["--training.mixed_precision_param", "float32"])
     assert all(math.isfinite(v) for v in fp32) and abs(bf16[0] - fp32[0]) < 0.05, (bf16, fp32)
+
+
+def test_reference_command_lines_parse():
+    """The flags the reference's experiment scripts pass to torchtitan parse
+    here as they are (hyphenated sections and fields, --compile.*,
+    --hf-assets-path, the GSDion / Dion2 / SDion switches)."""
+    from dion_b200.train import parse_job, trainer_config_from_job
+
+    argv = ("--module ada_dion.integration.config_registry --config llama3_320m_adadion --training.steps 2000 "
+            "--training.local-batch-size 32 --training.global-batch-size 256 --training.seq-len 2048 "
+            "--hf-assets-path ./assets/hf/Meta-Llama-3.1-8B --optimizer.lr 0.02 --optimizer.init-rank 64 "
+            "--optimizer.no-use-anchor --parallelism.data-parallel-shard-degree 8 "
+            "--parallelism.data-parallel-replicate-degree 1 --parallelism.tensor_parallel_degree 1 --compile.enable "
+            "--activation-checkpoint.mode selective --activation-checkpoint.selective-ac-option op "
+            "--metrics.enable-wandb --metrics.enable-tensorboard --metrics.log-freq 10 --metrics.wandb_project p "
+            "--metrics.wandb_run_name r --debug.seed 42 --validator.freq 200 --validator.steps 50 "
+            "--profiling.enable_profiling --profiling.save_traces_folder t --optimizer.selection_method random "
+            "--optimizer.no-use-adaptive-scalar --optimizer.no-rank-normalize --optimizer.use-rms-matching "
+            "--optimizer.no-use-trust-region --optimizer.no-use-residual-rank --optimizer.sdion-mode skip "
+            "--optimizer.no-adaptive-rank --optimizer.anchor-alpha 0.1 --optimizer.fraction 0.25 "
+            "--optimizer.rank_fraction 0.25 --optimizer.mu 0.95").split()
+    job = parse_job(argv)
+    assert job.compile.enable and job.hf_assets_path.endswith("Meta-Llama-3.1-8B")
+    assert job.activation_checkpoint.mode == "selective" and job.metrics.wandb_project == "p"
+    o = job.optimizer
+    assert (o.use_anchor, o.adaptive_rank, o.use_adaptive_scalar, o.rank_normalize, o.use_trust_region) == (
+        False, False, False, False, False)
+    assert o.use_rms_matching and o.selection_method == "random" and o.sdion_mode == "skip"
+    tc = trainer_config_from_job(job)
+    assert tc.seed == 42 and tc.global_batch_size == 256 and tc.local_batch_size == 32
