@@ -145,10 +145,29 @@ class CheckpointManager:
         steps = [int(m.group(1)) for d in os.listdir(self.folder) if (m := re.fullmatch(r"step-(\d+)", d))]
         return os.path.join(self.folder, f"step-{max(steps)}") if steps else None
 
-    def maybe_load(self, trainer) -> None:
-        p = self.latest()
+    def maybe_load(self, trainer, load_step: int = -1, initial_load_path: Optional[str] = None,
+                   initial_load_model_only: bool = True) -> Optional[str]:
+        """Resume from ``step-<load_step>`` (or, with -1, the newest full
+        checkpoint in the folder); with no checkpoint in the folder, start
+        from ``initial_load_path`` (its weights only, unless
+        ``initial_load_model_only`` is False). Returns the path loaded."""
+        if load_step >= 0:
+            p = os.path.join(self.folder, f"step-{load_step}")
+            if not os.path.isdir(p):
+                raise FileNotFoundError(f"no checkpoint {p}")
+        else:
+            p = self.latest()
+        data = getattr(trainer, "data", None)
         if p is not None:
-            trainer.step_idx = load(p, self.model, self.optimizers, data=getattr(trainer, "data", None))
+            trainer.step_idx = load(p, self.model, self.optimizers, data=data)
+            return p
+        if initial_load_path:
+            if initial_load_model_only:
+                load(initial_load_path, self.model, None)
+            else:
+                trainer.step_idx = load(initial_load_path, self.model, self.optimizers, data=data)
+            return initial_load_path
+        return None
 
     def maybe_save(self, trainer, step: int, final: bool = False) -> Optional[str]:
         """Full checkpoint every ``interval`` steps (the final step included);

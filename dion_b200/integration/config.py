@@ -89,6 +89,12 @@ class CheckpointConfig:
     folder: str = "checkpoint"
     interval: int = 1000
     last_save_model_only: bool = True
+    # resume from step-<load_step> instead of the newest full checkpoint (-1: newest)
+    load_step: int = -1
+    # when `folder` holds no checkpoint yet: start from this checkpoint (e.g. a
+    # model-only export); with initial_load_model_only only its weights are taken
+    initial_load_path: Optional[str] = None
+    initial_load_model_only: bool = True
 
 
 @dataclass

@@ -173,7 +173,9 @@ def main(argv: Optional[List[str]] = None) -> List[float]:
 
         ckpt = CheckpointManager(job.checkpoint.folder, tr.model, tr.optimizers, interval=job.checkpoint.interval,
                                  model_only_last=job.checkpoint.last_save_model_only)
-        ckpt.maybe_load(tr)
+        cc = job.checkpoint
+        ckpt.maybe_load(tr, load_step=cc.load_step, initial_load_path=cc.initial_load_path,
+                        initial_load_model_only=cc.initial_load_model_only)
     prof = _profiler(job, tr)
     flops_tok = tr.model_cfg.flops_per_token(tc.seq_len)
     tokens_step = tc.local_batch_size * tr.grad_accum * tc.seq_len

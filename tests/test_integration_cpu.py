@@ -494,3 +494,28 @@ def test_reference_command_lines_parse():
     assert o.use_rms_matching and o.selection_method == "random" and o.sdion_mode == "skip"
     tc = trainer_config_from_job(job)
     assert tc.seed == 42 and tc.global_batch_size == 256 and tc.local_batch_size == 32
+
+
+def test_checkpoint_initial_load_and_load_step(tmp_path):
+    """--checkpoint.initial_load_path starts a new run from another run's
+    model-only export (weights only, step 0); --checkpoint.load_step resumes
+    from a chosen full checkpoint rather than the newest."""
+    from dion_b200 import train
+
+    base = ["--config", "llama3_debug_muon", "--training.seq_len", "32", "--training.local_batch_size", "2",
+            "--metrics.log_freq", "1", "--checkpoint.enable"]
+    a = tmp_path / "a"
+    train.main(base + ["--checkpoint.folder", str(a), "--checkpoint.interval", "2", "--training.steps", "4",
+                       "--checkpoint.last_save_model_only"])
+    assert (a / "step-2").exists() and (a / "step-4").exists() and (a / "step-4-model").exists()
+    # a new run from the model-only export: starts at step 0 with run A's final weights
+    b = tmp_path / "b"
+    losses = train.main(base + ["--checkpoint.folder", str(b), "--checkpoint.interval", "100",
+                                "--checkpoint.initial_load_path", str(a / "step-4-model"), "--training.steps", "2"])
+    assert len(losses) == 2
+    # resume run A from step 2 (not the newest, step 4): 2 more steps are logged
+    losses = train.main(base + ["--checkpoint.folder", str(a), "--checkpoint.interval", "100",
+                                "--checkpoint.load_step", "2", "--training.steps", "4"])
+    assert len(losses) == 2
+    with pytest.raises(FileNotFoundError):
+        train.main(base + ["--checkpoint.folder", str(a), "--checkpoint.load_step", "3", "--training.steps", "4"])
