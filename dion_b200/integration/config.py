@@ -69,7 +69,8 @@ class ActivationCheckpointConfig:
 @dataclass
 class LRSchedulerConfig:
     warmup_steps: int = 200
-    decay_type: str = "cosine"
+    decay_type: str = "cosine"  # cosine | linear | sqrt
+    decay_ratio: Optional[float] = None  # decay over this fraction of the steps (None: all after warm-up)
     min_lr_factor: float = 0.1
 
 

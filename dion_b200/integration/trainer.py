@@ -41,6 +41,7 @@ class TrainerConfig:
     steps: int = 100
     warmup_steps: int = 200
     decay_ratio: Optional[float] = None
+    decay_type: str = "cosine"
     min_lr_factor: float = 0.1
     max_norm: float = 1.0
     seed: int = 2
@@ -76,14 +77,31 @@ class TrainerConfig:
     reduce_dtype: str = "float32"
 
 
-def lr_lambda(step: int, warmup: int, total: int, min_factor: float) -> float:
-    """Linear warmup then cosine decay to ``min_factor`` (multiplier on the base lr)."""
+def lr_lambda(step: int, warmup: int, total: int, min_factor: float, decay_ratio: Optional[float] = None,
+              decay_type: str = "cosine") -> float:
+    """Multiplier on the base lr: linear warm-up over ``warmup`` steps, an
+    optional stable phase, then decay to ``min_factor`` over the last
+    ``decay_ratio * total`` steps (all the steps after warm-up when
+    ``decay_ratio`` is None), shaped ``cosine``, ``linear`` or ``sqrt``
+    (1 - sqrt(progress)): torchtitan's warmup-stable-decay schedule, which
+    the reference configures (ada_dion/integration/config_registry.py:171-176)."""
     if warmup > 0 and step < warmup:
         return (step + 1) / (warmup + 1)
-    if total <= warmup:
+    decay = total - warmup if decay_ratio is None else int(round(total * decay_ratio))
+    decay = max(0, min(decay, total - warmup))
+    start = total - decay
+    if step < start or decay <= 0:
         return 1.0
-    prog = min(1.0, (step - warmup) / max(1, total - warmup))
-    return min_factor + (1 - min_factor) * 0.5 * (1 + math.cos(math.pi * prog))
+    prog = min(1.0, (step - start) / max(1, decay))
+    if decay_type == "linear":
+        adj = 1.0 - prog
+    elif decay_type == "sqrt":
+        adj = 1.0 - math.sqrt(prog)
+    elif decay_type == "cosine":
+        adj = 0.5 * (1 + math.cos(math.pi * prog))
+    else:
+        raise ValueError(f"decay_type must be cosine, linear or sqrt, got {decay_type!r}")
+    return min_factor + (1 - min_factor) * adj
 
 
 def clip_grad_norm_multi_mesh_(params: List[torch.nn.Parameter], max_norm: float,
@@ -215,7 +233,7 @@ class Trainer:
     def _set_lr(self) -> None:
         c = self.cfg
         total = c.steps
-        f = lr_lambda(self.step_idx, c.warmup_steps, total, c.min_lr_factor)
+        f = lr_lambda(self.step_idx, c.warmup_steps, total, c.min_lr_factor, c.decay_ratio, c.decay_type)
         for opt, base in zip(self.optimizers, self._base_lrs):
             for g, b in zip(opt.param_groups, base):
                 g["lr"] = b * f

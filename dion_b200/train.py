@@ -44,6 +44,8 @@ def trainer_config_from_job(job: JobConfig) -> TrainerConfig:
         steps=job.training.steps,
         warmup_steps=job.lr_scheduler.warmup_steps,
         min_lr_factor=job.lr_scheduler.min_lr_factor,
+        decay_ratio=job.lr_scheduler.decay_ratio,
+        decay_type=job.lr_scheduler.decay_type,
         max_norm=job.training.max_norm,
         seed=job.debug.seed or job.training.seed or job.dataloader.seed,
         init_mode=job.model.init,

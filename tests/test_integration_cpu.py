@@ -519,3 +519,28 @@ def test_checkpoint_initial_load_and_load_step(tmp_path):
     assert len(losses) == 2
     with pytest.raises(FileNotFoundError):
         train.main(base + ["--checkpoint.folder", str(a), "--checkpoint.load_step", "3", "--training.steps", "4"])
+
+
+def test_lr_schedule_shapes():
+    """Warm-up, then cosine decay over the rest by default; with decay_ratio
+    a stable phase first (warmup-stable-decay), and linear / sqrt shapes."""
+    from dion_b200.integration.trainer import lr_lambda
+
+    total, warm = 100, 10
+    assert lr_lambda(0, warm, total, 0.1) == pytest.approx(1 / 11)
+    assert lr_lambda(warm, warm, total, 0.1) == pytest.approx(1.0)
+    assert lr_lambda(total, warm, total, 0.1) == pytest.approx(0.1)
+    assert lr_lambda(55, warm, total, 0.1) == pytest.approx(0.1 + 0.9 * 0.5)  # cosine midpoint
+    # WSD: flat until the last 20 steps, then linear / sqrt down to the floor
+    assert lr_lambda(79, warm, total, 0.0, 0.2, "linear") == 1.0
+    assert lr_lambda(90, warm, total, 0.0, 0.2, "linear") == pytest.approx(0.5)
+    assert lr_lambda(90, warm, total, 0.0, 0.2, "sqrt") == pytest.approx(1 - 0.5 ** 0.5)
+    with pytest.raises(ValueError):
+        lr_lambda(90, warm, total, 0.0, 0.2, "step")
+    from dion_b200.integration.config_registry import get_config
+    from dion_b200.train import trainer_config_from_job
+
+    job = get_config("llama3_debug_muon")
+    apply_overrides(job, ["--lr_scheduler.decay_ratio", "0.2", "--lr_scheduler.decay_type", "linear"])
+    tc = trainer_config_from_job(job)
+    assert tc.decay_ratio == 0.2 and tc.decay_type == "linear"
