@@ -158,14 +158,25 @@ def main(argv: Optional[List[str]] = None) -> List[float]:
     if tr.rank == 0:
         mc = job.metrics
         if mc.enable_tensorboard:
-            from torch.utils.tensorboard import SummaryWriter
+            try:
+                from torch.utils.tensorboard import SummaryWriter
 
-            tb = SummaryWriter(log_dir=mc.save_tb_folder)
+                tb = SummaryWriter(log_dir=mc.save_tb_folder)
+            except Exception as e:  # a missing package must not stop the run
+                print(f"warning: TensorBoard disabled ({type(e).__name__}: {e})", flush=True)
         if mc.enable_wandb:
-            import wandb
+            try:
+                import wandb
 
-            wb = wandb.init(project=mc.wandb_project or os.environ.get("WANDB_PROJECT", "dion_b200"),
-                            name=mc.wandb_run_name or os.environ.get("WANDB_RUN_NAME"), config=job.to_dict())
+                # without credentials (or with WANDB_MODE=offline) the run is recorded locally
+                # for a later `wandb sync`: a node without network access never waits on W&B
+                mode = os.environ.get("WANDB_MODE") or ("online" if os.environ.get("WANDB_API_KEY") else "offline")
+                wb = wandb.init(project=mc.wandb_project or os.environ.get("WANDB_PROJECT", "dion_b200"),
+                                name=mc.wandb_run_name or os.environ.get("WANDB_RUN_NAME"), config=job.to_dict(),
+                                mode=mode)
+            except Exception as e:
+                print(f"warning: W&B disabled ({type(e).__name__}: {e})", flush=True)
+                wb = None
         if mc.save_jsonl or tb is not None or wb is not None:
             collector = OptimizerMetricsCollector(tr.optimizers, output_dir=mc.save_jsonl or mc.save_tb_folder,
                                                   tb_writer=tb, wandb_run=wb)

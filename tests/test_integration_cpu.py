@@ -544,3 +544,22 @@ def test_lr_schedule_shapes():
     apply_overrides(job, ["--lr_scheduler.decay_ratio", "0.2", "--lr_scheduler.decay_type", "linear"])
     tc = trainer_config_from_job(job)
     assert tc.decay_ratio == 0.2 and tc.decay_type == "linear"
+
+
+def test_train_entry_wandb_offline_without_credentials(tmp_path, monkeypatch):
+    """The registry's full-size configs enable W&B, as the reference's do;
+    without credentials the run is recorded offline instead of waiting on the
+    network."""
+    pytest.importorskip("wandb")
+    from dion_b200 import train
+
+    monkeypatch.chdir(tmp_path)
+    monkeypatch.delenv("WANDB_API_KEY", raising=False)
+    monkeypatch.delenv("WANDB_MODE", raising=False)
+    monkeypatch.setenv("WANDB_DIR", str(tmp_path))
+    losses = train.main(["--config", "llama3_debug_muon", "--training.steps", "2", "--training.seq_len", "32",
+                         "--training.local_batch_size", "2", "--metrics.log_freq", "1", "--metrics.enable_wandb",
+                         "--metrics.wandb_project", "p", "--metrics.wandb_run_name", "r"])
+    assert len(losses) == 2
+    runs = list((tmp_path / "wandb").glob("offline-run-*"))
+    assert runs, list(tmp_path.rglob("*"))[:20]
