@@ -148,6 +148,8 @@ def llama3_320m_adadion_v2_fixed() -> JobConfig:
 # ---------------------------------------------------------------- debug (tiny, 10 steps, checkpoint every 10)
 def _debug(opt: Opt) -> JobConfig:
     cfg = _base("debug", opt, steps=10, warmup=2, ckpt_interval=10, model_only=False)
+    # the reference's debug schedule: 2 warm-up steps, linear decay to 0 over the last 80 %
+    cfg.lr_scheduler = LRSchedulerConfig(warmup_steps=2, decay_ratio=0.8, decay_type="linear", min_lr_factor=0.0)
     cfg.metrics.enable_tensorboard = False
     cfg.metrics.enable_wandb = False
     return cfg

@@ -101,6 +101,8 @@ def test_registry_names_and_fields():
     assert c.lr_scheduler.warmup_steps == 200 and c.lr_scheduler.min_lr_factor == 0.1
     assert get_config("llama3_320m_muon").lr_scheduler.warmup_steps == 610
     assert get_config("llama3_debug_dion").checkpoint.interval == 10
+    ls = get_config("llama3_debug_muon").lr_scheduler
+    assert (ls.warmup_steps, ls.decay_ratio, ls.decay_type, ls.min_lr_factor) == (2, 0.8, "linear", 0.0)
 
 
 def test_cli_overrides():
