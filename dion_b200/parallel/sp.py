@@ -73,6 +73,9 @@ class SPGroup:
     # ------------------------------------------------------------ token shards
     def shard_rows(self, x: Tensor) -> Tensor:
         """This rank's contiguous block of rows of a [N, ...] tensor."""
+        if x.shape[0] % self.T:
+            raise ValueError(f"sequence parallelism over {self.T} ranks needs the batch's token count "
+                             f"(batch x sequence length = {x.shape[0]}) to be a multiple of {self.T}")
         n = x.shape[0] // self.T
         return x[self.me * n:(self.me + 1) * n]
 

@@ -140,3 +140,23 @@ def test_gradient_accumulation_with_sequence_parallel_tp():
             assert status == "ok", res
     a, b = torch.tensor(full[0][1]), torch.tensor(acc[0][1])
     assert torch.allclose(a, b, rtol=1e-4, atol=1e-4), (a, b)
+
+
+def _odd_tokens_body(rank, world):
+    import torch.distributed as dist
+
+    from dion_b200.parallel.sp import SPGroup
+
+    sp = SPGroup(dist.group.WORLD, torch.device("cpu"))
+    try:
+        sp.shard_rows(torch.zeros(7, 4))
+    except ValueError as e:
+        return [str(e)]
+    return ["no error"]
+
+
+def test_token_count_must_divide_over_tp_ranks():
+    out = spawn(_odd_tokens_body, world=2)
+    for r, (status, res) in out.items():
+        assert status == "ok", res
+        assert "multiple of 2" in res[0], res
