@@ -129,7 +129,8 @@ static std::tuple<int64_t, int, size_t> probe(const std::string& path, size_t fi
 
 class TokenStream {
  public:
-  TokenStream(const std::vector<std::string>& paths, int bpt_hint) {
+  // random: windows are read in a shuffled order (no read-ahead); otherwise in file order
+  TokenStream(const std::vector<std::string>& paths, int bpt_hint, bool random) {
     if (paths.empty()) throw std::runtime_error("no token files given");
     int64_t start = 0;
     for (const auto& p : paths) {
@@ -150,7 +151,7 @@ class TokenStream {
       s.map = ::mmap(nullptr, s.map_len, PROT_READ, MAP_SHARED, fd, 0);
       ::close(fd);  // the mapping keeps the file referenced
       if (s.map == MAP_FAILED) throw std::runtime_error(p + ": mmap failed");
-      ::madvise(s.map, s.map_len, MADV_RANDOM);
+      ::madvise(s.map, s.map_len, random ? MADV_RANDOM : MADV_SEQUENTIAL);
       const uint8_t* base = static_cast<const uint8_t*>(s.map);
       auto [n, bpt, hdr] = probe(p, s.map_len, base, bpt_hint);
       s.n_tokens = n;
@@ -218,7 +219,7 @@ class TokenLoader {
   TokenLoader(std::vector<std::string> paths, int64_t seq_len, int64_t local_batch, int64_t rank, int64_t world,
               uint64_t seed, bool shuffle, int64_t depth, int64_t vocab, int64_t bytes_per_token,
               int64_t position, double timeout_s)
-      : stream_(paths, (int)bytes_per_token),
+      : stream_(paths, (int)bytes_per_token, shuffle),
         S_(seq_len),
         b_(local_batch),
         rank_(rank),
