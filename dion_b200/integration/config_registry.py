@@ -135,14 +135,41 @@ def _adadion_v2(adaptive: bool, rf: float = 0.25) -> Opt:
                rank_step_up=16, rank_step_down=8, erank_ema_beta=0.9, scalar_lr=3e-4, scalar_weight_decay=0.01)
 
 
+def _320m_adadion_v2(adaptive: bool, init_rank_fraction: float = 0.5) -> JobConfig:
+    """The reference's 320M AdaDionV2 trainer (ada_dion/optim/config_registry.py:102-191):
+    Dion-matched hyper-parameters (lr 0.012, rank fraction 1/2), adaptive rank up to
+    0.7, warm-up 610 then cosine to 0, selective AC every 2nd block, no LM-head lr
+    scaling."""
+    opt = Opt(name="AdaDionV2", lr=0.012, mu=0.95, rank_fraction=0.5, adaptive_rank=adaptive,
+              init_rank_fraction=init_rank_fraction, rank_fraction_max=0.7, erank_ema_beta=0.5, rank_scale=1.5,
+              rank_min=16, rank_quantize=8, weight_decay=0.1, scalar_lr=0.012, scalar_beta1=0.95,
+              scalar_beta2=0.95, scalar_eps=1e-8, scalar_weight_decay=0.1, output_head_lr_scaling=False)
+    cfg = _base("320M", opt, steps=6104, warmup=610)
+    cfg.lr_scheduler.min_lr_factor = 0.0
+    cfg.activation_checkpoint.mode = "selective"
+    cfg.activation_checkpoint.selective_ac_option = "2"
+    return cfg
+
+
 @register
 def llama3_320m_adadion_v2() -> JobConfig:
-    return _base("320M", _adadion_v2(True), steps=6104, warmup=610)
+    return _320m_adadion_v2(True)
+
+
+@register
+def llama3_320m_adadion_v2_dion_lr() -> JobConfig:
+    return _320m_adadion_v2(True)
+
+
+@register
+def llama3_320m_adadion_v2_dion_equivalent() -> JobConfig:
+    """adaptive_rank off: exactly Dion at rank fraction 1/2 (must match llama3_320m_dion's val loss)."""
+    return _320m_adadion_v2(False)
 
 
 @register
 def llama3_320m_adadion_v2_fixed() -> JobConfig:
-    return _base("320M", _adadion_v2(False), steps=6104, warmup=610)
+    return _320m_adadion_v2(False)
 
 
 # ---------------------------------------------------------------- debug (tiny, 10 steps, checkpoint every 10)
@@ -183,6 +210,19 @@ def llama3_debug_adadion() -> JobConfig:
 @register
 def llama3_debug_adadion_v2() -> JobConfig:
     return _debug(_adadion_v2(True))
+
+
+@register
+def llama3_debug_2gpu_adadion_v2() -> JobConfig:
+    """The tiny model for 2 GPUs, 50 steps, 4 sequences per GPU
+    (ada_dion/optim/config_registry.py:198-217)."""
+    opt = Opt(name="AdaDionV2", lr=0.012, rank_fraction=0.5, adaptive_rank=True, init_rank_fraction=0.25,
+              rank_fraction_max=0.7, erank_ema_beta=0.5, rank_scale=1.5, rank_min=8, rank_quantize=8,
+              weight_decay=0.1, scalar_lr=0.012, scalar_weight_decay=0.1)
+    cfg = _debug(opt)
+    cfg.training.steps = 50
+    cfg.training.local_batch_size = 4
+    return cfg
 
 
 # ---------------------------------------------------------------- B200 benchmark flavours

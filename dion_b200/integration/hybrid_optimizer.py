@@ -46,7 +46,7 @@ def build_param_groups(model: nn.Module, cfg: "HybridOptimizersContainer.Config"
         groups.append(
             {
                 "params": g.output_params,
-                "lr": cfg.scalar_lr / math.sqrt(d_model),
+                "lr": cfg.scalar_lr / math.sqrt(d_model) if cfg.output_head_lr_scaling else cfg.scalar_lr,
                 "weight_decay": cfg.scalar_weight_decay,
                 **scalar,
             }
@@ -106,6 +106,9 @@ class HybridOptimizersContainer(Optimizer):
         # AdaDionV2 (adaptive-rank Dion)
         rank_fraction_max: float = 0.7
         init_rank_fraction: float = 0.25
+        rank_scale: float = 1.5
+        # LM head lr = scalar_lr / sqrt(d_model) (the reference container's rule); False: scalar_lr
+        output_head_lr_scaling: bool = True
         # scalar groups
         scalar_algorithm: str = "adamw"
         scalar_lr: float = 3e-4
@@ -161,10 +164,13 @@ class HybridOptimizersContainer(Optimizer):
         if name == "AdaDionV2":
             return optim.AdaDionV2(groups, replicate_mesh=replicate_mesh, outer_shard_mesh=shard_mesh,
                              inner_shard_mesh=tp_mesh, lr=cfg.lr, mu=cfg.mu, weight_decay=cfg.weight_decay,
-                             rank_fraction_max=cfg.rank_fraction_max, adaptive_rank=cfg.adaptive_rank,
-                             init_rank_fraction=cfg.init_rank_fraction, rank_min=cfg.rank_min,
-                             rank_quantize=cfg.rank_quantize, rank_step_up=cfg.rank_step_up,
-                             rank_step_down=cfg.rank_step_down, erank_ema_beta=cfg.erank_ema_beta)
+                             # Q width: rank_fraction_max with adaptive rank, rank_fraction without
+                             # (ada_dion/optim/config_registry.py:72)
+                             rank_fraction_max=cfg.rank_fraction_max if cfg.adaptive_rank else cfg.rank_fraction,
+                             adaptive_rank=cfg.adaptive_rank, init_rank_fraction=cfg.init_rank_fraction,
+                             rank_min=cfg.rank_min, rank_quantize=cfg.rank_quantize, rank_step_up=cfg.rank_step_up,
+                             rank_step_down=cfg.rank_step_down, erank_ema_beta=cfg.erank_ema_beta,
+                             rank_scale=cfg.rank_scale)
         if name == "AdaDion":
             if tp_mesh is not None:
                 raise ValueError("AdaDion (SDion) supports data-parallel layouts (DDP / FSDP); it has no "

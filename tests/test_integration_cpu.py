@@ -565,3 +565,28 @@ def test_train_entry_wandb_offline_without_credentials(tmp_path, monkeypatch):
     assert len(losses) == 2
     runs = list((tmp_path / "wandb").glob("offline-run-*"))
     assert runs, list(tmp_path.rglob("*"))[:20]
+
+
+def test_reference_adadion_v2_configs():
+    """The reference's AdaDionV2 trainer configs by name, with its
+    hyper-parameters; the Dion-equivalent one sizes Q by rank_fraction, and
+    output_head_lr_scaling=False keeps the LM head at scalar_lr."""
+    for n in ["llama3_320m_adadion_v2", "llama3_320m_adadion_v2_dion_lr", "llama3_320m_adadion_v2_dion_equivalent",
+              "llama3_debug_2gpu_adadion_v2"]:
+        assert n in REGISTRY
+    c = get_config("llama3_320m_adadion_v2")
+    o = c.optimizer
+    assert (o.lr, o.rank_fraction_max, o.init_rank_fraction, o.erank_ema_beta, o.rank_scale) == (0.012, 0.7, 0.5, 0.5,
+                                                                                                  1.5)
+    assert c.lr_scheduler.warmup_steps == 610 and c.lr_scheduler.min_lr_factor == 0.0
+    assert c.activation_checkpoint.selective_ac_option == "2"
+    d = get_config("llama3_debug_2gpu_adadion_v2")
+    assert d.training.steps == 50 and d.training.local_batch_size == 4 and d.optimizer.rank_min == 8
+
+    model = Transformer(llama3_config("debug"))
+    eq = get_config("llama3_320m_adadion_v2_dion_equivalent").optimizer
+    cont = HybridOptimizersContainer(eq, model_parts=[model])
+    opt = cont.optimizers[0]
+    assert type(opt).__name__ == "AdaDionV2" and not opt._adaptive_rank
+    heads = [g for g in opt.param_groups if any(p is model.output.weight for p in g["params"])]
+    assert heads and heads[0]["lr"] == eq.scalar_lr
