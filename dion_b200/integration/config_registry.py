@@ -103,30 +103,38 @@ def llama3_160m_adadion() -> JobConfig:
     return _base("160M", _adadion())
 
 
-# ---------------------------------------------------------------- 320M (warmup 610, 6104 steps)
+# ---------------------------------------------------------------- 320M (warmup 610, 6104 steps, cosine to 0)
+def _320m(opt: Opt) -> JobConfig:
+    cfg = _base("320M", opt, steps=6104, warmup=610)
+    cfg.lr_scheduler.min_lr_factor = 0.0  # ada_dion/integration/config_registry.py:359-364
+    return cfg
+
+
 @register
 def llama3_320m_adamw() -> JobConfig:
-    return _base("320M", _adamw(0.008), steps=6104, warmup=610)
+    opt = _adamw(0.008)
+    opt.scalar_beta1 = 0.95  # betas (0.95, 0.95) for the 320M AdamW baseline
+    return _320m(opt)
 
 
 @register
 def llama3_320m_muon() -> JobConfig:
-    return _base("320M", _muon(), steps=6104, warmup=610)
+    return _320m(_muon())
 
 
 @register
 def llama3_320m_dion() -> JobConfig:
-    return _base("320M", _dion(), steps=6104, warmup=610)
+    return _320m(_dion())
 
 
 @register
 def llama3_320m_dion2() -> JobConfig:
-    return _base("320M", _dion2(), steps=6104, warmup=610)
+    return _320m(_dion2())
 
 
 @register
 def llama3_320m_adadion() -> JobConfig:
-    return _base("320M", _adadion(), steps=6104, warmup=610)
+    return _320m(_adadion())
 
 
 def _adadion_v2(adaptive: bool, rf: float = 0.25) -> Opt:
@@ -144,8 +152,7 @@ def _320m_adadion_v2(adaptive: bool, init_rank_fraction: float = 0.5) -> JobConf
               init_rank_fraction=init_rank_fraction, rank_fraction_max=0.7, erank_ema_beta=0.5, rank_scale=1.5,
               rank_min=16, rank_quantize=8, weight_decay=0.1, scalar_lr=0.012, scalar_beta1=0.95,
               scalar_beta2=0.95, scalar_eps=1e-8, scalar_weight_decay=0.1, output_head_lr_scaling=False)
-    cfg = _base("320M", opt, steps=6104, warmup=610)
-    cfg.lr_scheduler.min_lr_factor = 0.0
+    cfg = _320m(opt)
     cfg.activation_checkpoint.mode = "selective"
     cfg.activation_checkpoint.selective_ac_option = "2"
     return cfg

@@ -100,6 +100,9 @@ def test_registry_names_and_fields():
     assert c.training.seq_len == 2048 and c.training.local_batch_size == 8 and c.training.max_norm == 1.0
     assert c.lr_scheduler.warmup_steps == 200 and c.lr_scheduler.min_lr_factor == 0.1
     assert get_config("llama3_320m_muon").lr_scheduler.warmup_steps == 610
+    assert get_config("llama3_320m_dion").lr_scheduler.min_lr_factor == 0.0
+    a = get_config("llama3_320m_adamw").optimizer
+    assert (a.lr, a.scalar_beta1, a.scalar_beta2) == (0.008, 0.95, 0.95)
     assert get_config("llama3_debug_dion").checkpoint.interval == 10
     ls = get_config("llama3_debug_muon").lr_scheduler
     assert (ls.warmup_steps, ls.decay_ratio, ls.decay_type, ls.min_lr_factor) == (2, 0.8, "linear", 0.0)
