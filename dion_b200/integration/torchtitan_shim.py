@@ -33,22 +33,28 @@ _NAMES = {"muon": "Muon", "dion": "Dion", "dion2": "Dion2", "adadion": "AdaDion"
           "adadionv2": "AdaDionV2", "adamw": "AdamW"}
 
 
-@dataclass
-class Optimizer:
-    """Fields merged into torchtitan's ``[optimizer]`` section."""
+_SCALARS = {"float": float, "int": int, "bool": bool, "str": str, float: float, int: int, bool: bool, str: str}
+# torchtitan's own [optimizer] fields, read separately
+_TITAN_OWNED = {"name", "lr", "weight_decay", "scalar_beta1", "scalar_beta2", "scalar_eps"}
 
-    mu: float = 0.95
-    nesterov: bool = False
-    adjust_lr: str = "spectral_norm"
-    rank_fraction: float = 0.25
-    fraction: float = 0.25
-    ef_decay: float = 0.95
-    adaptive_rank: bool = True
-    rank_fraction_max: float = 0.7
-    init_rank_fraction: float = 0.25
-    rank_min: int = 16
-    scalar_lr: float = 3e-4
-    scalar_weight_decay: float = 0.01
+# Fields merged into torchtitan's ``[optimizer]`` section: every scalar field of
+# the container's Config (Dion / Dion2 / AdaDion / AdaDionV2 / GSDion switches),
+# so each one is settable from torchtitan's command line.
+def _field_class(f):
+    if f.type in _SCALARS:
+        return _SCALARS[f.type]
+    if f.type in ("Optional[str]", Optional[str]) and isinstance(f.default, str):
+        return str  # e.g. adjust_lr: a name, or None to switch it off
+    return None
+
+
+Optimizer = dataclasses.make_dataclass(
+    "Optimizer",
+    [(f.name, _field_class(f), field(default=f.default))
+     for f in dataclasses.fields(HybridOptimizersContainer.Config)
+     if f.name not in _TITAN_OWNED and _field_class(f) is not None and f.default is not dataclasses.MISSING],
+)
+Optimizer.__doc__ = "Fields merged into torchtitan's ``[optimizer]`` section."
 
 
 @dataclass
