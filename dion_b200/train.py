@@ -109,6 +109,23 @@ def _load_config(module: Optional[str], name: str) -> JobConfig:
     return fn()
 
 
+def _print_fields(argv: List[str]) -> None:
+    """Every ``--section.field`` of the job configuration, with its value in
+    ``--config NAME`` (or the defaults)."""
+    import dataclasses
+
+    job = JobConfig()
+    if "--config" in argv:
+        i = argv.index("--config")
+        job = _load_config(None, argv[i + 1])
+    for sec in dataclasses.fields(job):
+        val = getattr(job, sec.name)
+        if not dataclasses.is_dataclass(val):
+            continue
+        for f in dataclasses.fields(val):
+            print(f"--{sec.name}.{f.name} {getattr(val, f.name)!r}")
+
+
 def parse_job(argv: List[str]) -> JobConfig:
     """The job configuration a command line selects: ``--config`` (and
     ``--module``), then every ``--section.field value`` override. The
@@ -116,7 +133,11 @@ def parse_job(argv: List[str]) -> JobConfig:
     names may use hyphens, ``--compile.*`` is accepted (torch.compile is not
     used: the hot ops are hand-written kernels) and ``--hf-assets-path``
     names the tokenizer assets (the data comes from token files here)."""
-    p = argparse.ArgumentParser(add_help=True)
+    if "--list-fields" in argv:
+        _print_fields(argv)
+        raise SystemExit(0)
+    p = argparse.ArgumentParser(add_help=True, epilog="--list-fields [--config NAME]: every --section.field "
+                                                      "override with its value in that config")
     p.add_argument("--config", required=True)
     p.add_argument("--module", default=None,
                    help="module whose config functions to use (torchtitan-style --module); "

@@ -593,3 +593,12 @@ def test_reference_adadion_v2_configs():
     assert type(opt).__name__ == "AdaDionV2" and not opt._adaptive_rank
     heads = [g for g in opt.param_groups if any(p is model.output.weight for p in g["params"])]
     assert heads and heads[0]["lr"] == eq.scalar_lr
+
+
+def test_list_fields(capsys):
+    from dion_b200 import train
+
+    with pytest.raises(SystemExit):
+        train.main(["--list-fields", "--config", "llama3_160m_dion"])
+    out = capsys.readouterr().out
+    assert "--optimizer.rank_fraction 0.25" in out and "--training.steps 10000" in out
