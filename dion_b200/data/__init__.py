@@ -1,4 +1,5 @@
-"""Training data: token files read by the native loader, and synthetic tokens.
+"""Training data: token files read by the native loader, text tokenized on
+the fly, and synthetic tokens.
 
 The reference trains through torchtitan's HuggingFace loader (c4_test;
 ada_dion/integration/config_registry.py:161-168 names the dataset), which
@@ -8,8 +9,10 @@ tokenized once into token files (:mod:`dion_b200.data.tokenize`), and
 :class:`TokenFileLoader` reads windows from the memory-mapped files with a
 C++ prefetch thread (``dion_b200/csrc/io/token_loader.cpp``), so the
 training loop never waits on tokenization or file reads.
+:class:`TextStreamLoader` (``--dataloader.dataset text:<files>``) keeps
+torchtitan's on-the-fly form for small corpora.
 
-Both loaders hand out pinned int64 ``(tokens, labels)`` pairs of shape
+The loaders hand out pinned int64 ``(tokens, labels)`` pairs of shape
 ``[local_batch, seq_len]``, fresh buffers per step (the caching host
 allocator reuses a buffer only after its asynchronous copy has finished),
 and expose ``state_dict`` / ``load_state_dict`` with the number of global
@@ -24,7 +27,7 @@ from typing import Dict, Iterator, List, Optional, Sequence, Tuple, Union
 import numpy as np
 import torch
 
-__all__ = ["TokenFileLoader", "SyntheticTokens", "write_token_file", "token_file_info", "expand_paths",
+__all__ = ["TokenFileLoader", "TextStreamLoader", "SyntheticTokens", "write_token_file", "token_file_info", "expand_paths",
            "build_loader", "HEADER_BYTES", "MAGIC"]
 
 MAGIC = b"DB2TOKN1"
@@ -194,11 +197,117 @@ class SyntheticTokens:
             self._draw()
 
 
+class TextStreamLoader:
+    """Text documents tokenized on the fly, as torchtitan's HuggingFace text
+    loader does (the reference trains through it): rank ``r`` of ``world``
+    takes documents ``r, r + world, ...`` of the input files (in order,
+    re-read after the last), encodes each as ``[BOS] + ids + [EOS]``,
+    concatenates them and cuts non-overlapping windows of ``seq_len + 1``
+    tokens. A background thread prepares ``prefetch`` batches ahead.
+
+    The state is the number of windows this rank has consumed; loading it
+    re-reads the documents up to that point (use token files and
+    :class:`TokenFileLoader` for large corpora: they resume in O(1) and
+    need no tokenizer at training time)."""
+
+    def __init__(self, paths: Union[str, Sequence[str]], tokenizer, seq_len: int, local_batch: int, rank: int = 0,
+                 world: int = 1, text_field: str = "text", vocab: int = 0, prefetch: int = 4, position: int = 0):
+        from .tokenize import load_tokenizer
+
+        self.paths = expand_paths(paths) if isinstance(paths, str) else list(paths)
+        self.tok = load_tokenizer(tokenizer) if isinstance(tokenizer, str) else tokenizer
+        self.seq_len, self.local_batch = int(seq_len), int(local_batch)
+        self.rank, self.world = int(rank), int(world)
+        self.text_field, self.vocab, self.prefetch = text_field, int(vocab), max(1, int(prefetch))
+        if self.vocab and self.tok.vocab_size > self.vocab:
+            raise ValueError(f"the tokenizer's vocabulary ({self.tok.vocab_size}) exceeds the model's ({self.vocab})")
+        self._start(int(position))
+
+    def _windows(self):
+        from .tokenize import _encode_doc, iter_documents
+
+        L = self.seq_len + 1
+        buf: List[int] = []
+        while True:
+            any_doc = False
+            for i, text in enumerate(iter_documents(self.paths, self.text_field)):
+                if i % self.world != self.rank:
+                    continue
+                any_doc = True
+                buf.extend(_encode_doc(self.tok, text))
+                while len(buf) >= L:
+                    yield buf[:L]
+                    del buf[:L]
+            if not any_doc:
+                raise ValueError(f"rank {self.rank} of {self.world} gets no document from {self.paths}")
+
+    def _start(self, position: int) -> None:
+        import queue
+        import threading
+
+        self._windows_used = position
+        q: "queue.Queue" = queue.Queue(maxsize=self.prefetch)
+        stop = threading.Event()
+        self._q, self._stop = q, stop  # the thread keeps its own queue and flag across a restart
+
+        def work():
+            try:
+                it = self._windows()
+                for _ in range(position):  # resume: skip the windows already used
+                    next(it)
+                while not stop.is_set():
+                    rows = [next(it) for _ in range(self.local_batch)]
+                    t = torch.tensor(rows, dtype=torch.int64)
+                    while not stop.is_set():
+                        try:
+                            q.put(t, timeout=0.1)
+                            break
+                        except queue.Full:
+                            continue
+            except BaseException as e:  # surfaces in next()
+                q.put(e)
+
+        self._thread = threading.Thread(target=work, daemon=True)
+        self._thread.start()
+
+    def next(self) -> Tuple[torch.Tensor, torch.Tensor]:
+        item = self._q.get(timeout=600)
+        if isinstance(item, BaseException):
+            raise item
+        self._windows_used += self.local_batch
+        t, l = _pinned((self.local_batch, self.seq_len)), _pinned((self.local_batch, self.seq_len))
+        t.copy_(item[:, :-1])
+        l.copy_(item[:, 1:])
+        return t, l
+
+    def __iter__(self) -> Iterator[Tuple[torch.Tensor, torch.Tensor]]:
+        while True:
+            yield self.next()
+
+    def close(self) -> None:
+        self._stop.set()
+        self._thread.join(timeout=5)
+
+    def state_dict(self) -> Dict[str, int]:
+        # windows used per rank (the same on every rank: each step takes local_batch)
+        return {"samples": int(self._windows_used)}
+
+    def load_state_dict(self, sd: Dict[str, int]) -> None:
+        self.close()
+        self._start(int(sd["samples"]))
+
+
 def build_loader(dataset: str, *, vocab: int, seq_len: int, local_batch: int, seed: int, rank: int, world: int,
-                 shuffle: bool = True, prefetch: int = 4, bytes_per_token: int = 0):
-    """``"synthetic"`` -> :class:`SyntheticTokens`; anything else names token
-    files (see :func:`expand_paths`) -> :class:`TokenFileLoader`."""
+                 shuffle: bool = True, prefetch: int = 4, bytes_per_token: int = 0, tokenizer: str = "byte",
+                 text_field: str = "text"):
+    """``"synthetic"`` -> :class:`SyntheticTokens`; ``"text:<files>"``
+    (jsonl / json / parquet / txt) -> :class:`TextStreamLoader` with
+    ``tokenizer``; anything else names token files (see
+    :func:`expand_paths`) -> :class:`TokenFileLoader`."""
     if dataset in ("", "synthetic"):
         return SyntheticTokens(vocab, seq_len, local_batch, seed, rank, world)
+    if dataset.startswith("text:"):
+        return TextStreamLoader(dataset[len("text:"):], tokenizer, seq_len, local_batch, rank=rank, world=world,
+                                text_field=text_field, vocab=vocab, prefetch=prefetch)
     return TokenFileLoader(dataset, seq_len, local_batch, rank=rank, world=world, seed=seed, shuffle=shuffle,
                            prefetch=prefetch, vocab=vocab, bytes_per_token=bytes_per_token)

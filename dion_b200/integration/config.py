@@ -114,8 +114,11 @@ class MetricsConfig:
 class DataConfig:
     # "synthetic" or token files: comma-separated files, directories of *.bin or
     # glob patterns (written by `python -m dion_b200.data.tokenize`)
+    # "text:<files>" (jsonl / json / parquet / txt) tokenizes on the fly with `tokenizer`
     dataset: str = "synthetic"
     seed: int = 0
+    tokenizer: str = "byte"  # for "text:" datasets: "byte" or a local HuggingFace tokenizer directory
+    text_field: str = "text"
     shuffle: bool = True
     prefetch: int = 4
     bytes_per_token: int = 0  # raw token files without a header: 2 or 4

@@ -65,6 +65,8 @@ class TrainerConfig:
     data_shuffle: bool = True
     data_prefetch: int = 4
     data_bytes_per_token: int = 0  # raw token files only (files with a header carry it)
+    data_tokenizer: str = "byte"  # "text:<files>" datasets: "byte" or a local HuggingFace tokenizer directory
+    data_text_field: str = "text"
     # held-out token files for ``validate`` ("" = none)
     val_dataset: str = ""
     # sequences per optimizer step over all data-parallel ranks; a multiple of
@@ -215,7 +217,8 @@ class Trainer:
         self.data = build_loader(cfg.dataset, vocab=mcfg.vocab_size, seq_len=cfg.seq_len,
                                  local_batch=cfg.local_batch_size * self.grad_accum, seed=cfg.seed, rank=self.data_rank,
                                  world=self.data_world, shuffle=cfg.data_shuffle, prefetch=cfg.data_prefetch,
-                                 bytes_per_token=cfg.data_bytes_per_token)
+                                 bytes_per_token=cfg.data_bytes_per_token, tokenizer=cfg.data_tokenizer,
+                                 text_field=cfg.data_text_field)
         self.val_data = None
         if cfg.val_dataset:
             self.val_data = TokenFileLoader(cfg.val_dataset, cfg.seq_len, cfg.local_batch_size, rank=self.data_rank,

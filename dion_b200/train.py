@@ -63,6 +63,8 @@ def trainer_config_from_job(job: JobConfig) -> TrainerConfig:
         data_shuffle=job.dataloader.shuffle,
         data_prefetch=job.dataloader.prefetch,
         data_bytes_per_token=job.dataloader.bytes_per_token,
+        data_tokenizer=job.dataloader.tokenizer,
+        data_text_field=job.dataloader.text_field,
         val_dataset=job.validator.dataset if job.validator.enable else "",
         global_batch_size=job.training.global_batch_size,
         param_dtype=job.training.mixed_precision_param,

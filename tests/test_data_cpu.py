@@ -268,3 +268,50 @@ def test_tokenize_with_worker_processes_keeps_order(tmp_path):
     a = np.fromfile(one["train"][0], dtype="<u2", offset=32)
     b = np.fromfile(many["train"][0], dtype="<u2", offset=32)
     assert one["documents"] == many["documents"] == 300 and np.array_equal(a, b)
+
+
+def _docs(tmp_path, n=60):
+    p = tmp_path / "docs.jsonl"
+    with open(p, "w") as f:
+        for i in range(n):
+            f.write(json.dumps({"text": f"document {i}: " + "abc " * (i % 9 + 3)}) + "\n")
+    return str(p)
+
+
+def test_text_stream_loader_windows_ranks_and_resume(tmp_path):
+    from dion_b200.data import TextStreamLoader
+    from dion_b200.data.tokenize import ByteTokenizer, _encode_doc
+
+    path = _docs(tmp_path)
+    tok = ByteTokenizer()
+    texts = [json.loads(l)["text"] for l in open(path)]
+    S, b, W = 16, 2, 2
+    for r in range(W):
+        ld = TextStreamLoader(path, "byte", S, b, rank=r, world=W, vocab=258)
+        stream = [t for i, txt in enumerate(texts) if i % W == r for t in _encode_doc(tok, txt)]
+        got = [ld.next() for _ in range(3)]
+        for k, (t, l) in enumerate(got):
+            for i in range(b):
+                w = stream[(k * b + i) * (S + 1):(k * b + i + 1) * (S + 1)]
+                assert t[i].tolist() == w[:-1] and l[i].tolist() == w[1:]
+        sd = ld.state_dict()
+        assert sd == {"samples": 6}
+        want = ld.next()
+        again = TextStreamLoader(path, "byte", S, b, rank=r, world=W)
+        again.load_state_dict(sd)
+        nxt = again.next()
+        assert torch.equal(want[0], nxt[0]) and torch.equal(want[1], nxt[1])
+        ld.close()
+        again.close()
+    with pytest.raises(ValueError, match="vocabulary"):
+        TextStreamLoader(path, "byte", S, b, vocab=100)
+
+
+def test_trainer_on_text_stream(tmp_path):
+    from dion_b200 import train
+
+    path = _docs(tmp_path, 200)
+    losses = train.main(["--config", "llama3_debug_muon", "--training.steps", "3", "--training.seq_len", "32",
+                         "--training.local_batch_size", "2", "--metrics.log_freq", "1",
+                         "--dataloader.dataset", "text:" + path, "--dataloader.tokenizer", "byte"])
+    assert len(losses) == 3 and all(math.isfinite(v) for v in losses)
