@@ -31,7 +31,8 @@ def _sync_for_checkpoint(optimizers) -> None:
             fn()
 
 
-def save(folder: str, model, optimizers, step: int, model_only: bool = False, data=None) -> str:
+def save(folder: str, model, optimizers, step: int, model_only: bool = False, data=None,
+         async_save: bool = False):
     """Write a DCP checkpoint. Full checkpoints go to ``step-<N>``; a
     model-only save goes to ``step-<N>-model``, a name that resuming never
     picks (it holds no optimizer state to resume from). ``data``: a loader
@@ -45,8 +46,24 @@ def save(folder: str, model, optimizers, step: int, model_only: bool = False, da
         sd["train_state"] = {"step": torch.tensor(step)}
         if data is not None and hasattr(data, "state_dict"):
             sd["train_state"]["data_samples"] = torch.tensor(int(data.state_dict()["samples"]))
+    if async_save:
+        # the state is staged to host memory before this returns; the files are
+        # written in the background while training continues (a future). Each
+        # tensor is copied into its own storage first: optimizer state lives in
+        # views of shared arenas, which the stager cannot copy storage-wise.
+        return path, dcp.async_save(_own_storage(sd), checkpoint_id=path)
     dcp.save(sd, checkpoint_id=path)
     return path
+
+
+def _own_storage(obj):
+    if isinstance(obj, dict):
+        return {k: _own_storage(v) for k, v in obj.items()}
+    if isinstance(obj, list):
+        return [_own_storage(v) for v in obj]
+    if torch.is_tensor(obj):
+        return obj.detach().clone()
+    return obj
 
 
 def _metadata_keys(path: str):
@@ -130,12 +147,36 @@ def load(path: str, model, optimizers=None, data=None) -> int:
 
 
 class CheckpointManager:
-    def __init__(self, folder: str, model, optimizers, interval: int = 1000, model_only_last: bool = True):
+    """Interval checkpoints of a trainer. ``async_mode`` "async": each save
+    returns once the state is staged in host memory and the files are written
+    in the background (torchtitan's async checkpointing); the next save, and
+    :meth:`wait`, wait for the previous write."""
+
+    def __init__(self, folder: str, model, optimizers, interval: int = 1000, model_only_last: bool = True,
+                 async_mode: str = "disabled"):
+        if async_mode not in ("disabled", "async"):
+            raise ValueError(f"async_mode must be 'disabled' or 'async', got {async_mode!r}")
         self.folder = folder
         self.model = model
         self.optimizers = optimizers
         self.interval = interval
         self.model_only_last = model_only_last
+        self.async_mode = async_mode
+        self._pending = None
+
+    def wait(self) -> None:
+        """Block until the last background write has finished."""
+        if self._pending is not None:
+            self._pending.result()
+            self._pending = None
+
+    def _save(self, step: int, model_only: bool = False, data=None) -> str:
+        self.wait()
+        if self.async_mode == "async":
+            path, self._pending = save(self.folder, self.model, self.optimizers, step, model_only=model_only,
+                                       data=data, async_save=True)
+            return path
+        return save(self.folder, self.model, self.optimizers, step, model_only=model_only, data=data)
 
     def latest(self) -> Optional[str]:
         """Newest full checkpoint (``step-<N>``); model-only final saves
@@ -151,6 +192,7 @@ class CheckpointManager:
         checkpoint in the folder); with no checkpoint in the folder, start
         from ``initial_load_path`` (its weights only, unless
         ``initial_load_model_only`` is False). Returns the path loaded."""
+        self.wait()
         if load_step >= 0:
             p = os.path.join(self.folder, f"step-{load_step}")
             if not os.path.isdir(p):
@@ -177,10 +219,11 @@ class CheckpointManager:
         path = None
         data = getattr(trainer, "data", None)
         if self.interval > 0 and step % self.interval == 0:
-            path = save(self.folder, self.model, self.optimizers, step, data=data)
+            path = self._save(step, data=data)
         if final:
             if self.model_only_last:
-                path = save(self.folder, self.model, self.optimizers, step, model_only=True)
+                path = self._save(step, model_only=True)
             elif path is None:
-                path = save(self.folder, self.model, self.optimizers, step, data=data)
+                path = self._save(step, data=data)
+            self.wait()
         return path

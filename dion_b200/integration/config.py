@@ -96,6 +96,8 @@ class CheckpointConfig:
     # model-only export); with initial_load_model_only only its weights are taken
     initial_load_path: Optional[str] = None
     initial_load_model_only: bool = True
+    # "async": write checkpoints in the background once the state is staged in host memory
+    async_mode: str = "disabled"
 
 
 @dataclass

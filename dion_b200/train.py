@@ -208,7 +208,8 @@ def main(argv: Optional[List[str]] = None) -> List[float]:
         from .checkpoint import CheckpointManager
 
         ckpt = CheckpointManager(job.checkpoint.folder, tr.model, tr.optimizers, interval=job.checkpoint.interval,
-                                 model_only_last=job.checkpoint.last_save_model_only)
+                                 model_only_last=job.checkpoint.last_save_model_only,
+                                 async_mode=job.checkpoint.async_mode)
         cc = job.checkpoint
         ckpt.maybe_load(tr, load_step=cc.load_step, initial_load_path=cc.initial_load_path,
                         initial_load_model_only=cc.initial_load_model_only)
@@ -250,6 +251,8 @@ def main(argv: Optional[List[str]] = None) -> List[float]:
             prof.step()
     if prof is not None:
         prof.__exit__(None, None, None)
+    if ckpt is not None:
+        ckpt.wait()
     if collector is not None:
         collector.close()
     if tb is not None:

@@ -602,3 +602,21 @@ def test_list_fields(capsys):
         train.main(["--list-fields", "--config", "llama3_160m_dion"])
     out = capsys.readouterr().out
     assert "--optimizer.rank_fraction 0.25" in out and "--training.steps 10000" in out
+
+
+def test_async_checkpoint_resume(tmp_path):
+    """--checkpoint.async_mode async writes in the background; the resumed run
+    continues exactly like one resumed from a synchronous checkpoint."""
+    from dion_b200 import train
+
+    base = ["--config", "llama3_debug_dion", "--training.seq_len", "32", "--training.local_batch_size", "2",
+            "--metrics.log_freq", "1", "--checkpoint.enable", "--checkpoint.interval", "2",
+            "--checkpoint.no-last_save_model_only"]
+    out = {}
+    for mode in ("disabled", "async"):
+        ck = tmp_path / mode
+        train.main(base + ["--checkpoint.folder", str(ck), "--checkpoint.async_mode", mode, "--training.steps", "2"])
+        assert (ck / "step-2" / ".metadata").exists()
+        out[mode] = train.main(base + ["--checkpoint.folder", str(ck), "--checkpoint.async_mode", mode,
+                                       "--training.steps", "4"])
+    assert out["disabled"] == out["async"] and len(out["async"]) == 2
