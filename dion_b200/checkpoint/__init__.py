@@ -32,7 +32,7 @@ def _sync_for_checkpoint(optimizers) -> None:
 
 
 def save(folder: str, model, optimizers, step: int, model_only: bool = False, data=None,
-         async_save: bool = False):
+         async_save: bool = False, process_group=None):
     """Write a DCP checkpoint. Full checkpoints go to ``step-<N>``; a
     model-only save goes to ``step-<N>-model``, a name that resuming never
     picks (it holds no optimizer state to resume from). ``data``: a loader
@@ -51,7 +51,7 @@ def save(folder: str, model, optimizers, step: int, model_only: bool = False, da
         # written in the background while training continues (a future). Each
         # tensor is copied into its own storage first: optimizer state lives in
         # views of shared arenas, which the stager cannot copy storage-wise.
-        return path, dcp.async_save(_own_storage(sd), checkpoint_id=path)
+        return path, dcp.async_save(_own_storage(sd), checkpoint_id=path, process_group=process_group)
     dcp.save(sd, checkpoint_id=path)
     return path
 
@@ -163,6 +163,11 @@ class CheckpointManager:
         self.model_only_last = model_only_last
         self.async_mode = async_mode
         self._pending = None
+        self._pg = None
+        if async_mode == "async" and dist.is_initialized() and dist.get_world_size() > 1:
+            # the background write coordinates the ranks on a group of its own, so
+            # it never interleaves with the training step's collectives
+            self._pg = dist.new_group(backend="gloo")
 
     def wait(self) -> None:
         """Block until the last background write has finished."""
@@ -174,7 +179,7 @@ class CheckpointManager:
         self.wait()
         if self.async_mode == "async":
             path, self._pending = save(self.folder, self.model, self.optimizers, step, model_only=model_only,
-                                       data=data, async_save=True)
+                                       data=data, async_save=True, process_group=self._pg)
             return path
         return save(self.folder, self.model, self.optimizers, step, model_only=model_only, data=data)
 

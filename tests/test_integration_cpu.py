@@ -260,7 +260,7 @@ def test_checkpoint_load_model_only_and_full(tmp_path):
         ckpt.load(str(tmp_path / "step-5"), _MockLlama(), c3)
 
 
-def _reshard_body(folder, phase, optimizer, rank, world):
+def _reshard_body(folder, phase, optimizer, rank, world, async_mode="disabled"):
     """phase "save": FSDP over `world` ranks, 2 steps, checkpoint, then 2 more
     steps; phase "load": resume the checkpoint and take the same 2 steps."""
     import torch.distributed as dist
@@ -274,7 +274,7 @@ def _reshard_body(folder, phase, optimizer, rank, world):
                         optimizer=HybridOptimizersContainer.Config(name=optimizer, lr=0.02, scalar_lr=3e-3), seed=5)
     torch.manual_seed(0)
     tr = Trainer(cfg, device=torch.device("cpu"))
-    ck = CheckpointManager(folder, tr.model, tr.optimizers, interval=2, model_only_last=False)
+    ck = CheckpointManager(folder, tr.model, tr.optimizers, interval=2, model_only_last=False, async_mode=async_mode)
     if phase == "save":
         for s in (1, 2):
             tr.train_step(*tr.data.next())
@@ -289,6 +289,7 @@ def _reshard_body(folder, phase, optimizer, rank, world):
             dist.all_reduce(loss)
             loss /= world
         losses.append(float(loss))
+    ck.wait()
     return losses
 
 
@@ -620,3 +621,20 @@ def test_async_checkpoint_resume(tmp_path):
         out[mode] = train.main(base + ["--checkpoint.folder", str(ck), "--checkpoint.async_mode", mode,
                                        "--training.steps", "4"])
     assert out["disabled"] == out["async"] and len(out["async"]) == 2
+
+
+def test_async_checkpoint_two_ranks(tmp_path):
+    """Background checkpoint writes under FSDP over 2 ranks (on a group of
+    their own) overlap the next steps and resume like synchronous ones."""
+    import functools
+
+    from test_distributed_cpu import spawn
+
+    folder = str(tmp_path / "ck")
+    saved = spawn(functools.partial(_reshard_body, folder, "save", "Dion", async_mode="async"), world=2)
+    for r, (status, res) in saved.items():
+        assert status == "ok", res
+    loaded = spawn(functools.partial(_reshard_body, folder, "load", "Dion"), world=2)
+    for r, (status, res) in loaded.items():
+        assert status == "ok", res
+    assert torch.allclose(torch.tensor(saved[0][1]), torch.tensor(loaded[0][1]), rtol=1e-4, atol=1e-4)
