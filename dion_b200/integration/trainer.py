@@ -22,7 +22,7 @@ import torch
 import torch.distributed as dist
 import torch.nn as nn
 
-from ..data import SyntheticTokens, TokenFileLoader, build_loader
+from ..data import SyntheticTokens, TokenFileLoader, build_loader  # noqa: F401 (re-exported)
 from ..models.llama3 import Llama3Config, Transformer, llama3_config
 from ..parallel.fsdp import apply_fsdp
 from ..parallel.tp import apply_tp
@@ -220,10 +220,12 @@ class Trainer:
                                  bytes_per_token=cfg.data_bytes_per_token, tokenizer=cfg.data_tokenizer,
                                  text_field=cfg.data_text_field)
         self.val_data = None
-        if cfg.val_dataset:
-            self.val_data = TokenFileLoader(cfg.val_dataset, cfg.seq_len, cfg.local_batch_size, rank=self.data_rank,
-                                            world=self.data_world, shuffle=False, prefetch=cfg.data_prefetch,
-                                            vocab=mcfg.vocab_size, bytes_per_token=cfg.data_bytes_per_token)
+        if cfg.val_dataset:  # token files or "text:<files>", read in order from the start on every pass
+            self.val_data = build_loader(cfg.val_dataset, vocab=mcfg.vocab_size, seq_len=cfg.seq_len,
+                                         local_batch=cfg.local_batch_size, seed=cfg.seed, rank=self.data_rank,
+                                         world=self.data_world, shuffle=False, prefetch=cfg.data_prefetch,
+                                         bytes_per_token=cfg.data_bytes_per_token, tokenizer=cfg.data_tokenizer,
+                                         text_field=cfg.data_text_field)
 
     @property
     def last_grad_norm(self) -> float:

@@ -315,3 +315,17 @@ def test_trainer_on_text_stream(tmp_path):
                          "--training.local_batch_size", "2", "--metrics.log_freq", "1",
                          "--dataloader.dataset", "text:" + path, "--dataloader.tokenizer", "byte"])
     assert len(losses) == 3 and all(math.isfinite(v) for v in losses)
+
+
+def test_validation_on_text_stream(tmp_path):
+    from dion_b200.integration.hybrid_optimizer import HybridOptimizersContainer
+    from dion_b200.integration.trainer import Trainer, TrainerConfig
+
+    path = _docs(tmp_path, 120)
+    cfg = TrainerConfig(model="debug", model_overrides=dict(vocab_size=512), seq_len=32, local_batch_size=2,
+                        steps=2, warmup_steps=0, optimizer=HybridOptimizersContainer.Config(name="Muon"),
+                        dataset="text:" + path, val_dataset="text:" + path)
+    tr = Trainer(cfg, device=torch.device("cpu"))
+    v1 = tr.validate(2)
+    tr.train_step(*tr.data.next())
+    assert math.isfinite(v1) and tr.validate(2) != v1  # same batches, trained weights
