@@ -83,16 +83,20 @@ def token_file_info(path: str, bytes_per_token: int = 0) -> Dict[str, int]:
     return {"tokens": int(n), "bytes_per_token": int(bpt), "header_bytes": int(hdr)}
 
 
-def expand_paths(spec: Union[str, Sequence[str]]) -> List[str]:
+TEXT_SUFFIXES = (".jsonl", ".json", ".parquet", ".txt", ".jsonl.gz", ".json.gz", ".txt.gz")
+
+
+def expand_paths(spec: Union[str, Sequence[str]], suffixes: Sequence[str] = (".bin",)) -> List[str]:
     """Files named by ``spec``: a comma-separated list of files, directories
-    (every ``*.bin`` inside, sorted) or glob patterns, in the order given."""
+    (every file inside ending in one of ``suffixes``, sorted) or glob
+    patterns, in the order given."""
     items = spec.split(",") if isinstance(spec, str) else list(spec)
     out: List[str] = []
     for item in (i.strip() for i in items):
         if not item:
             continue
         if os.path.isdir(item):
-            found = sorted(glob.glob(os.path.join(item, "*.bin")))
+            found = sorted(f for f in glob.glob(os.path.join(item, "*")) if f.endswith(tuple(suffixes)))
         elif any(c in item for c in "*?["):
             found = sorted(glob.glob(item))
         else:
@@ -214,7 +218,7 @@ class TextStreamLoader:
                  world: int = 1, text_field: str = "text", vocab: int = 0, prefetch: int = 4, position: int = 0):
         from .tokenize import load_tokenizer
 
-        self.paths = expand_paths(paths) if isinstance(paths, str) else list(paths)
+        self.paths = expand_paths(paths, TEXT_SUFFIXES)
         self.tok = load_tokenizer(tokenizer) if isinstance(tokenizer, str) else tokenizer
         self.seq_len, self.local_batch = int(seq_len), int(local_batch)
         self.rank, self.world = int(rank), int(world)

@@ -329,3 +329,17 @@ def test_validation_on_text_stream(tmp_path):
     v1 = tr.validate(2)
     tr.train_step(*tr.data.next())
     assert math.isfinite(v1) and tr.validate(2) != v1  # same batches, trained weights
+
+
+def test_text_stream_reads_a_directory(tmp_path):
+    from dion_b200.data import TextStreamLoader, expand_paths
+
+    d = tmp_path / "corpus"
+    d.mkdir()
+    _docs(d)
+    (d / "notes.md").write_text("not an input")
+    assert [os.path.basename(p) for p in expand_paths(str(d), (".jsonl",))] == ["docs.jsonl"]
+    ld = TextStreamLoader(str(d), "byte", 16, 2)
+    t, l = ld.next()
+    assert t.shape == (2, 16)
+    ld.close()
