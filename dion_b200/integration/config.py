@@ -110,6 +110,9 @@ class MetricsConfig:
     wandb_project: Optional[str] = None
     wandb_run_name: Optional[str] = None
     save_jsonl: Optional[str] = None
+    # denominator of the logged MFU, TFLOP/s per GPU (0: the B200's 2250 dense bf16 figure;
+    # pass a measured rate to report against it)
+    peak_tflops: float = 0.0
 
 
 @dataclass

@@ -30,7 +30,7 @@ from .integration.trainer import Trainer, TrainerConfig
 
 __all__ = ["trainer_config_from_job", "parse_job", "main"]
 
-# bf16 dense peak used for MFU (measured B200 figure is in the bench outputs)
+# default MFU denominator: B200 dense bf16 (--metrics.peak_tflops sets another, e.g. a measured rate)
 PEAK_FLOPS = {"bfloat16": 2.25e15}
 
 
@@ -232,7 +232,8 @@ def main(argv: Optional[List[str]] = None) -> List[float]:
             tps = tokens_step / dt
             tflops = flops_tok * tps / 1e12
             mem = torch.cuda.max_memory_allocated() / 2**30 if torch.cuda.is_available() else 0.0
-            mfu = 100.0 * flops_tok * tps / PEAK_FLOPS["bfloat16"]
+            peak = job.metrics.peak_tflops * 1e12 if job.metrics.peak_tflops > 0 else PEAK_FLOPS["bfloat16"]
+            mfu = 100.0 * flops_tok * tps / peak
             gn = tr.last_grad_norm
             if tr.rank == 0:
                 print(f"step: {s:5d}  loss: {v:8.4f}  grad_norm: {gn:7.4f}  memory: {mem:5.2f}GiB  "
