@@ -343,3 +343,12 @@ def test_text_stream_reads_a_directory(tmp_path):
     t, l = ld.next()
     assert t.shape == (2, 16)
     ld.close()
+
+
+def test_token_file_info_cli(tmp_path, capsys):
+    from dion_b200.data.__main__ import main
+
+    write_token_file(str(tmp_path / "t.bin"), list(b"hello token files"))
+    assert main(["info", str(tmp_path / "t.bin"), "--seq-len", "4", "--decode-byte", "5"]) == 0
+    out = capsys.readouterr().out
+    assert "17 tokens" in out and "3 windows of 5 tokens" in out and "'hello'" in out
