@@ -32,7 +32,7 @@ def _sync_for_checkpoint(optimizers) -> None:
 
 
 def save(folder: str, model, optimizers, step: int, model_only: bool = False, data=None,
-         async_save: bool = False, process_group=None):
+         async_save: bool = False, process_group=None, export_dtype: Optional[torch.dtype] = None):
     """Write a DCP checkpoint. Full checkpoints go to ``step-<N>``; a
     model-only save goes to ``step-<N>-model``, a name that resuming never
     picks (it holds no optimizer state to resume from). ``data``: a loader
@@ -41,6 +41,9 @@ def save(folder: str, model, optimizers, step: int, model_only: bool = False, da
     path = os.path.join(folder, f"step-{step}-model" if model_only else f"step-{step}")
     _sync_for_checkpoint(optimizers)
     sd: Dict[str, Any] = {"model": get_model_state_dict(model)}
+    if model_only and export_dtype is not None:  # e.g. bf16 weights for an export
+        sd["model"] = {k: v.to(export_dtype) if torch.is_tensor(v) and v.is_floating_point() else v
+                       for k, v in sd["model"].items()}
     if not model_only:
         sd["optimizer"] = optimizers.state_dict()
         sd["train_state"] = {"step": torch.tensor(step)}
@@ -153,7 +156,7 @@ class CheckpointManager:
     :meth:`wait`, wait for the previous write."""
 
     def __init__(self, folder: str, model, optimizers, interval: int = 1000, model_only_last: bool = True,
-                 async_mode: str = "disabled"):
+                 async_mode: str = "disabled", export_dtype: Optional[torch.dtype] = None):
         if async_mode not in ("disabled", "async"):
             raise ValueError(f"async_mode must be 'disabled' or 'async', got {async_mode!r}")
         self.folder = folder
@@ -162,6 +165,7 @@ class CheckpointManager:
         self.interval = interval
         self.model_only_last = model_only_last
         self.async_mode = async_mode
+        self.export_dtype = export_dtype  # dtype of the model-only final export (None: as trained)
         self._pending = None
         self._pg = None
         if async_mode == "async" and dist.is_initialized() and dist.get_world_size() > 1:
@@ -177,11 +181,13 @@ class CheckpointManager:
 
     def _save(self, step: int, model_only: bool = False, data=None) -> str:
         self.wait()
+        dt = self.export_dtype if model_only else None
         if self.async_mode == "async":
             path, self._pending = save(self.folder, self.model, self.optimizers, step, model_only=model_only,
-                                       data=data, async_save=True, process_group=self._pg)
+                                       data=data, async_save=True, process_group=self._pg, export_dtype=dt)
             return path
-        return save(self.folder, self.model, self.optimizers, step, model_only=model_only, data=data)
+        return save(self.folder, self.model, self.optimizers, step, model_only=model_only, data=data,
+                    export_dtype=dt)
 
     def latest(self) -> Optional[str]:
         """Newest full checkpoint (``step-<N>``); model-only final saves

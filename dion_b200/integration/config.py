@@ -98,6 +98,8 @@ class CheckpointConfig:
     initial_load_model_only: bool = True
     # "async": write checkpoints in the background once the state is staged in host memory
     async_mode: str = "disabled"
+    # dtype of the model-only final export (torchtitan's export_dtype)
+    export_dtype: str = "float32"
 
 
 @dataclass

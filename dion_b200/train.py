@@ -209,7 +209,8 @@ def main(argv: Optional[List[str]] = None) -> List[float]:
 
         ckpt = CheckpointManager(job.checkpoint.folder, tr.model, tr.optimizers, interval=job.checkpoint.interval,
                                  model_only_last=job.checkpoint.last_save_model_only,
-                                 async_mode=job.checkpoint.async_mode)
+                                 async_mode=job.checkpoint.async_mode,
+                                 export_dtype=getattr(torch, job.checkpoint.export_dtype))
         cc = job.checkpoint
         ckpt.maybe_load(tr, load_step=cc.load_step, initial_load_path=cc.initial_load_path,
                         initial_load_model_only=cc.initial_load_model_only)

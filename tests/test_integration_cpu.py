@@ -642,3 +642,25 @@ def test_async_checkpoint_two_ranks(tmp_path):
     for r, (status, res) in loaded.items():
         assert status == "ok", res
     assert torch.allclose(torch.tensor(saved[0][1]), torch.tensor(loaded[0][1]), rtol=1e-4, atol=1e-4)
+
+
+def test_model_only_export_dtype(tmp_path):
+    """--checkpoint.export_dtype bfloat16 writes the final model-only export
+    in bf16 (full checkpoints keep fp32), and it loads into an fp32 model."""
+    import torch.distributed.checkpoint as dcp
+
+    from dion_b200 import train
+
+    ck = tmp_path / "ck"
+    train.main(["--config", "llama3_debug_muon", "--training.steps", "2", "--training.seq_len", "32",
+                "--training.local_batch_size", "2", "--metrics.log_freq", "1", "--checkpoint.enable",
+                "--checkpoint.folder", str(ck), "--checkpoint.interval", "2", "--checkpoint.last_save_model_only",
+                "--checkpoint.export_dtype", "bfloat16"])
+    md = dcp.FileSystemReader(str(ck / "step-2-model")).read_metadata().state_dict_metadata
+    full = dcp.FileSystemReader(str(ck / "step-2")).read_metadata().state_dict_metadata
+    key = "model.output.weight"
+    assert md[key].properties.dtype == torch.bfloat16 and full[key].properties.dtype == torch.float32
+    from dion_b200.checkpoint import load
+
+    m = Transformer(llama3_config("debug"))
+    assert load(str(ck / "step-2-model"), m) == 0 and m.output.weight.dtype == torch.float32
