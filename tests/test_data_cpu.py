@@ -352,3 +352,32 @@ def test_token_file_info_cli(tmp_path, capsys):
     assert main(["info", str(tmp_path / "t.bin"), "--seq-len", "4", "--decode-byte", "5"]) == 0
     out = capsys.readouterr().out
     assert "17 tokens" in out and "3 windows of 5 tokens" in out and "'hello'" in out
+
+
+def _fsdp_text_body(path, rank, world):
+    from dion_b200.integration.hybrid_optimizer import HybridOptimizersContainer
+    from dion_b200.integration.trainer import Trainer, TrainerConfig
+
+    cfg = TrainerConfig(model="debug", model_overrides=dict(vocab_size=512), seq_len=32, local_batch_size=2,
+                        steps=2, warmup_steps=0, optimizer=HybridOptimizersContainer.Config(name="Dion"),
+                        dataset="text:" + path, dp_shard=world, seed=3)
+    torch.manual_seed(0)
+    tr = Trainer(cfg, device=torch.device("cpu"))
+    t, _ = tr.data.next()
+    loss = float(tr.train_step(t, _))
+    return [loss] + t[0].tolist()
+
+
+def test_text_stream_under_fsdp_gives_each_rank_its_documents(tmp_path):
+    from test_distributed_cpu import spawn
+
+    path = _docs(tmp_path, 100)
+    out = spawn(functools.partial(_fsdp_text_body, path), world=2)
+    for r, (status, res) in out.items():
+        assert status == "ok", res
+        assert math.isfinite(res[0])
+    # rank 0 starts with document 0, rank 1 with document 1: "[BOS]document 0: ..." / "[BOS]document 1: ..."
+    from dion_b200.data.tokenize import ByteTokenizer
+
+    tok = ByteTokenizer()
+    assert tok.decode(out[0][1][2:13]) == "document 0:" and tok.decode(out[1][1][2:13]) == "document 1:"
